@@ -1,0 +1,868 @@
+#!/usr/bin/env python
+"""bench.py -- throughput of the b2blas GEMM/GEMV hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload W] [--impl b2blas|reference]
+
+One JSON line on rank 0.  The default workload is the HGEMM configuration:
+8192 x 8192 x 8192, f16 in / f32 accumulate / f16 out, alpha 1, beta 0,
+inputs i.i.d. normal(0, 0.1) rounded to f16 (seeded, synthetic).  On N GPUs
+(one process per GPU, torchrun) it is column-sharded with A replicated: rank
+r computes its own 8192 x 8192 panel of an 8192 x (8192*N) x 8192 product,
+so per-GPU work is fixed ("weak"); no collective runs in the data path
+unless --gather asks for the assembled C.
+
+A "step" is one GEMM call over one batch of resident device inputs, timed
+with CUDA events on the stream the kernels run on (K steps between a barrier
++ synchronize on both sides, max over ranks).  `e2e` is the same metric
+through the host-slice API (b2b_hgemm_simple): every step copies A and B from
+page-locked host memory and C back.
+
+Other workloads (--workload): sgemm (8192^3, alpha 1.5, beta 0.5), dgemm
+(4096^3), batched (4096 x 256^3 strided, batch-sharded), sgemv (16384^2, N),
+mlp (4 layers 1024-4096-4096-4096-1024, batch 4096, sgemm + saxpy bias).
+
+--impl reference times the CPU restatement of the reference's algorithm
+(the oracle's host triple loop) on this machine's cores, rank 0 only, with a
+bounded sample of the same workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cublas-rs_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "GEMM TFLOP/s & % of roofline at 1/2/4/8 B200 (8192³ HGEMM/SGEMM); SGEMV GB/s"
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        d["_source"] = "measured (MEASURED_PEAKS.json)"
+        return d
+    d = dict(FALLBACK_PEAKS)
+    d["_source"] = "fallback (no MEASURED_PEAKS.json)"
+    return d
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of each workload's dominant kernel, from the
+    committed ncu summary (profiles/dram_traffic.json), or {}."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# --------------------------------------------------------------- clocks
+
+_REASONS = [
+    (0x1, "gpu_idle"), (0x2, "applications_clocks_setting"), (0x4, "sw_power_cap"), (0x8, "hw_slowdown"),
+    (0x10, "sync_boost"), (0x20, "sw_thermal_slowdown"), (0x40, "hw_thermal_slowdown"),
+    (0x80, "hw_power_brake_slowdown"), (0x100, "display_clock_setting"),
+]
+
+
+class ClockSampler:
+    """Polls NVML (SM clock, event reasons) every few ms while running."""
+
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.samples = []
+        self.max_mhz = None
+        self.ok = False
+        self._stop = threading.Event()
+        self._period = period_s
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            h = None
+            try:
+                uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+                for i in range(pynvml.nvmlDeviceGetCount()):
+                    hi = pynvml.nvmlDeviceGetHandleByIndex(i)
+                    u = pynvml.nvmlDeviceGetUUID(hi)
+                    u = u.decode() if isinstance(u, bytes) else u
+                    if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                        h = hi
+                        break
+            except Exception:
+                h = None
+            if h is None:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[cuda_index]) if vis and vis.split(",")[0].isdigit() else cuda_index
+                h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self._h = h
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                clk = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                try:
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except AttributeError:
+                    rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.samples.append((clk, rs))
+            except Exception:
+                pass
+            self._stop.wait(self._period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": "nvml" if self.ok else "unavailable"}
+        clks = [c for c, _ in self.samples]
+        mask = 0
+        for _, r in self.samples:
+            mask |= int(r)
+        reasons = [name for bit, name in _REASONS if mask & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(clks), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
+
+
+# ------------------------------------------------------------ workloads
+
+def _pinned_numpy(t):
+    """Page-locked host copy of a device tensor, as a numpy array."""
+    import torch
+
+    h = torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=True)
+    h.copy_(t)
+    return h, h.numpy()
+
+
+class Workload:
+    name = ""
+    unit = "TFLOP/s"
+    dtype = "f32"
+    scaling = "weak"
+    launches_per_step = 1
+    kernel = ""
+    bound = "tensor"
+
+    def units_per_step(self):  # flops (or bytes) this rank processes per step
+        raise NotImplementedError
+
+    def scale(self, v):  # units/s -> unit
+        return v / 1e12
+
+
+class GemmWorkload(Workload):
+    """C = alpha*A*B + beta*C with A replicated and B/C column panels."""
+
+    def __init__(self, h, rank, world, args, kind, m, n_total, k, alpha, beta, weak):
+        import numpy as np
+        import torch
+
+        import b2blas
+        from b2blas import shard
+
+        self.h, self.kind = h, kind
+        self.m, self.k, self.alpha, self.beta = m, k, alpha, beta
+        self.world, self.rank = world, rank
+        if weak:
+            self.n = n_total
+            self.widths = [n_total] * world
+            self.global_n = n_total * world
+            self.scaling = "weak"
+        else:
+            self.widths = shard.column_panels(n_total, world, 8)
+            self.n = self.widths[rank]
+            self.global_n = n_total
+            self.scaling = "strong" if world > 1 else "weak"
+        dev = torch.device("cuda", torch.cuda.current_device())
+        tdt = {"hgemm": torch.float16, "sgemm": torch.float32, "dgemm": torch.float64}[kind]
+        self.dtype = {"hgemm": "f16", "sgemm": "f32", "dgemm": "f64"}[kind]
+        self.np_dt = {"hgemm": np.uint16, "sgemm": np.float32, "dgemm": np.float64}[kind]
+        gA = torch.Generator(device=dev).manual_seed(42)  # replicated A: same on every rank
+        gB = torch.Generator(device=dev).manual_seed(1000 + rank)
+        gC = torch.Generator(device=dev).manual_seed(2000 + rank)
+        if kind == "hgemm":
+            self.A = (torch.randn(m, k, device=dev, generator=gA) * 0.1).to(tdt)
+            self.B = (torch.randn(k, self.n, device=dev, generator=gB) * 0.1).to(tdt)
+            self.C = (torch.randn(m, self.n, device=dev, generator=gC) * 0.1).to(tdt) if beta else \
+                torch.zeros(m, self.n, device=dev, dtype=tdt)
+        else:
+            self.A = (torch.rand(m, k, device=dev, generator=gA, dtype=tdt) * 2 - 1)
+            self.B = (torch.rand(k, self.n, device=dev, generator=gB, dtype=tdt) * 2 - 1)
+            self.C = (torch.rand(m, self.n, device=dev, generator=gC, dtype=tdt) * 2 - 1)
+        self.C0 = self.C.clone() if beta else None
+        bdt = np.uint16 if kind == "hgemm" else self.np_dt
+        self.a = b2blas.DeviceBuffer.from_ptr(h, self.A.data_ptr(), m * k, bdt, owner=self.A)
+        self.b = b2blas.DeviceBuffer.from_ptr(h, self.B.data_ptr(), k * self.n, bdt, owner=self.B)
+        self.c = b2blas.DeviceBuffer.from_ptr(h, self.C.data_ptr(), m * self.n, bdt, owner=self.C)
+        self.cfg = b2blas.GemmConfig(m, self.n, k, alpha, beta)
+        self.fn = {"hgemm": h.hgemm, "sgemm": h.sgemm, "dgemm": h.dgemm}[kind]
+        self.simple = {"hgemm": h.hgemm_simple, "sgemm": h.sgemm_simple, "dgemm": h.dgemm_simple}[kind]
+        self.kernel = {"hgemm": "hgemm_tc_kernel", "sgemm": "gemm_simt_kernel<float>",
+                       "dgemm": "gemm_simt_kernel<double>"}[kind]
+        self.bound = "tensor" if kind == "hgemm" else "fma"
+        self.gather = bool(args.gather) and world > 1
+        if self.gather:
+            self.panels = torch.empty(sum(self.widths) * m, device=dev, dtype=tdt)
+            self.full = torch.empty(m, sum(self.widths), device=dev, dtype=tdt)
+            self.launches_per_step = 2
+
+    def step(self):
+        self.fn(self.cfg, self.a, self.b, self.c)
+        if self.gather:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.panels, self.C.view(-1))
+            esz = self.C.element_size()
+            self.h.panels_to_rowmajor(esz, self.m, self.widths, self.panels.data_ptr(), self.full.data_ptr())
+
+    def units_per_step(self):
+        return 2.0 * self.m * self.n * self.k
+
+    def e2e_setup(self):
+        self._hA, self.hA = _pinned_numpy(self.A)
+        self._hB, self.hB = _pinned_numpy(self.B)
+        self._hC, self.hC = _pinned_numpy(self.C)
+        if self.kind == "hgemm":
+            self.hA, self.hB, self.hC = (x.view(self.np_dt) for x in (self.hA, self.hB, self.hC))
+        self.hA, self.hB, self.hC = (x.reshape(-1) for x in (self.hA, self.hB, self.hC))
+        esz = self.A.element_size()
+        h2d = (self.m * self.k + self.k * self.n + (self.m * self.n if self.beta else 0)) * esz
+        return h2d, self.m * self.n * esz
+
+    def e2e_step(self):
+        self.simple(self.cfg, self.hA, self.hB, self.hC)
+
+    def config(self):
+        d = {"workload": f"{self.kind} {self.m}x{self.global_n}x{self.k}"
+                         + (f", column-sharded over {self.world} GPUs ({self.n} columns per GPU), A replicated"
+                            if self.world > 1 else ""),
+             "m": self.m, "n": self.global_n, "k": self.k, "n_per_gpu": self.n, "alpha": self.alpha,
+             "beta": self.beta, "gather": self.gather, "parallelism": f"column-shard x{self.world}",
+             "l2": "inputs larger than L2 (126 MB): no flush needed"}
+        return d
+
+    def cpu_sample(self, oracle, target_s):
+        """Times the host triple loop on a row sample of this rank's problem."""
+        import numpy as np
+
+        n, k = self.n, self.k
+        B = self.B.cpu().numpy()
+        if self.kind == "hgemm":
+            B = B.view(np.uint16)
+        B = np.ascontiguousarray(B).reshape(-1)
+        nt = oracle.num_threads()
+        rows = nt
+        out = {}
+        for attempt in range(2):
+            A = np.ascontiguousarray(self.A[:rows].cpu().numpy())
+            C = np.ascontiguousarray(self.C[:rows].cpu().numpy())
+            if self.kind == "hgemm":
+                A, C = A.view(np.uint16).reshape(-1), C.view(np.uint16).reshape(-1)
+                bf = np.empty(k * n, np.float32)
+                acc = np.empty(rows * n, np.float32)
+                t0 = time.perf_counter()
+                oracle.cpu_hgemm_rows(rows, n, k, self.alpha, A, B, self.beta, C, bf, acc)
+            elif self.kind == "sgemm":
+                A, C = A.reshape(-1), C.reshape(-1)
+                acc = np.empty(rows * n, np.float32)
+                t0 = time.perf_counter()
+                oracle.cpu_sgemm_rows(rows, n, k, self.alpha, A, B, self.beta, C, acc)
+            else:
+                A, C = A.reshape(-1), C.reshape(-1)
+                acc = np.empty(rows * n, np.float64)
+                t0 = time.perf_counter()
+                oracle.cpu_dgemm_rows(rows, n, k, self.alpha, A, B, self.beta, C, acc)
+            dt = time.perf_counter() - t0
+            out = {"value": 2.0 * rows * n * k / dt / 1e12, "seconds": dt, "rows": rows}
+            if attempt == 0:
+                per_row = dt / rows
+                rows = int(max(nt, min(self.m, target_s / max(per_row, 1e-9))))
+                rows = max(nt, rows // nt * nt)
+        out["sample"] = (f"first {out['rows']} rows of C ({out['rows']}x{n}x{k}, "
+                         f"{2.0 * out['rows'] * n * k / 1e9:.1f} GFLOP), i-k-j host loop")
+        return out
+
+
+class BatchedWorkload(Workload):
+    """Strided-batched SGEMM, batch-sharded (no collective)."""
+
+    def __init__(self, h, rank, world, args):
+        import torch
+
+        import b2blas
+        from b2blas import shard
+
+        self.h = h
+        self.total_batch, self.m = 4096, 256
+        b0, b1 = shard.batch_shard(self.total_batch, world, rank)
+        self.batch = b1 - b0
+        self.world = world
+        self.scaling = "strong" if world > 1 else "weak"
+        m = self.m
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(42 + rank)
+        self.A = torch.rand(self.batch, m, m, device=dev, generator=g) * 2 - 1
+        self.B = torch.rand(self.batch, m, m, device=dev, generator=g) * 2 - 1
+        self.C = torch.zeros(self.batch, m, m, device=dev)
+        mk = m * m
+        self.a = b2blas.DeviceBuffer.from_ptr(h, self.A.data_ptr(), self.batch * mk, "float32", owner=self.A)
+        self.b = b2blas.DeviceBuffer.from_ptr(h, self.B.data_ptr(), self.batch * mk, "float32", owner=self.B)
+        self.c = b2blas.DeviceBuffer.from_ptr(h, self.C.data_ptr(), self.batch * mk, "float32", owner=self.C)
+        self.cfg = b2blas.GemmConfig(m, m, m, 1.0, 0.0)
+        self.kernel = "gemm_simt_kernel<float> (batched)"
+        self.bound = "fma"
+
+    def step(self):
+        mk = self.m * self.m
+        self.h.strided_batched_sgemm(self.cfg, self.batch, self.a, mk, self.b, mk, self.c, mk)
+
+    def units_per_step(self):
+        return 2.0 * self.batch * self.m ** 3
+
+    def e2e_setup(self):
+        self._hA, self.hA = _pinned_numpy(self.A)
+        self._hB, self.hB = _pinned_numpy(self.B)
+        self._hC, self.hC = _pinned_numpy(self.C)
+        self.hA, self.hB, self.hC = (x.reshape(-1) for x in (self.hA, self.hB, self.hC))
+        n = self.batch * self.m * self.m * 4
+        return 2 * n, n
+
+    def e2e_step(self):
+        mk = self.m * self.m
+        self.h.strided_batched_sgemm_simple(self.cfg, self.batch, self.hA, mk, self.hB, mk, self.hC, mk)
+
+    def config(self):
+        return {"workload": f"strided-batched sgemm {self.total_batch} x {self.m}^3"
+                            + (f", {self.batch} batches per GPU" if self.world > 1 else ""),
+                "batch": self.total_batch, "batch_per_gpu": self.batch, "m": self.m, "n": self.m, "k": self.m,
+                "alpha": 1.0, "beta": 0.0, "parallelism": f"batch-shard x{self.world}",
+                "l2": "inputs larger than L2 (3 GiB): no flush needed"}
+
+    def cpu_sample(self, oracle, target_s):
+        import numpy as np
+
+        m = self.m
+        nb = 1
+        out = {}
+        for attempt in range(2):
+            A = self.A[:nb].cpu().numpy().reshape(-1)
+            B = self.B[:nb].cpu().numpy()
+            C = np.zeros(nb * m * m, np.float32)
+            acc = np.empty(m * m, np.float32)
+            t0 = time.perf_counter()
+            for i in range(nb):
+                oracle.cpu_sgemm_rows(m, m, m, 1.0, np.ascontiguousarray(A[i * m * m:(i + 1) * m * m]),
+                                      np.ascontiguousarray(B[i].reshape(-1)), 0.0, C[i * m * m:(i + 1) * m * m], acc)
+            dt = time.perf_counter() - t0
+            out = {"value": 2.0 * nb * m ** 3 / dt / 1e12, "seconds": dt, "batches": nb}
+            if attempt == 0:
+                nb = int(max(1, min(self.batch, target_s / max(dt, 1e-9))))
+        out["sample"] = f"first {out['batches']} of the {self.total_batch} 256^3 batches, i-k-j host loop"
+        return out
+
+
+class SgemvWorkload(Workload):
+    """SGEMV 16384 x 16384, N, alpha 1, beta 0 (replicas on N GPUs)."""
+
+    unit = "GB/s"
+    bound = "hbm"
+
+    def __init__(self, h, rank, world, args):
+        import torch
+
+        import b2blas
+
+        self.h, self.world = h, world
+        self.m = self.n = 16384
+        self.trans = 1 if args.trans else 0
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(42 + rank)
+        self.A = torch.rand(self.m, self.n, device=dev, generator=g) * 2 - 1
+        xl, yl = (self.n, self.m) if self.trans == 0 else (self.m, self.n)
+        self.x = torch.rand(xl, device=dev, generator=g) * 2 - 1
+        self.y = torch.zeros(yl, device=dev)
+        self.a = b2blas.DeviceBuffer.from_ptr(h, self.A.data_ptr(), self.m * self.n, "float32", owner=self.A)
+        self.xd = b2blas.DeviceBuffer.from_ptr(h, self.x.data_ptr(), xl, "float32", owner=self.x)
+        self.yd = b2blas.DeviceBuffer.from_ptr(h, self.y.data_ptr(), yl, "float32", owner=self.y)
+        self.kernel = "sgemv_n_kernel" if self.trans == 0 else "sgemv_t_partial_kernel"
+        self.launches_per_step = 1 if self.trans == 0 else 2
+        self.dtype = "f32"
+
+    def step(self):
+        self.h.sgemv(self.trans, self.m, self.n, 1.0, self.a, self.xd, 0.0, self.yd)
+
+    def units_per_step(self):
+        return 4.0 * (self.m * self.n + self.m + self.n)
+
+    def scale(self, v):
+        return v / 1e9
+
+    def e2e_setup(self):
+        self._hA, self.hA = _pinned_numpy(self.A)
+        self._hx, self.hx = _pinned_numpy(self.x)
+        self._hy, self.hy = _pinned_numpy(self.y)
+        self.hA = self.hA.reshape(-1)
+        return 4 * (self.m * self.n + len(self.hx)), 4 * len(self.hy)
+
+    def e2e_step(self):
+        self.h.sgemv_simple(self.trans, self.m, self.n, 1.0, self.hA, self.hx, 0.0, self.hy)
+
+    def config(self):
+        return {"workload": f"sgemv {self.m}x{self.n} {'NT'[self.trans]}"
+                            + (f", one replica per GPU" if self.world > 1 else ""),
+                "m": self.m, "n": self.n, "trans": "NT"[self.trans], "alpha": 1.0, "beta": 0.0,
+                "parallelism": f"replicas x{self.world}", "l2": "A is 1 GiB, larger than L2: no flush needed"}
+
+    def cpu_sample(self, oracle, target_s):
+        import numpy as np
+
+        n = self.n
+        x = self.x.cpu().numpy()
+        rows = 256
+        out = {}
+        for attempt in range(2):
+            A = np.ascontiguousarray(self.A[:rows].cpu().numpy()).reshape(-1)
+            y = np.zeros(rows, np.float32)
+            t0 = time.perf_counter()
+            reps = 0
+            while True:
+                oracle.cpu_sgemv_rows(rows, n, 1.0, A, x, 0.0, y)
+                reps += 1
+                if time.perf_counter() - t0 > (0.2 if attempt == 0 else target_s):
+                    break
+            dt = time.perf_counter() - t0
+            out = {"value": reps * 4.0 * (rows * n + n + rows) / dt / 1e9, "seconds": dt, "rows": rows}
+            if attempt == 0:
+                rows = min(self.m, 4096)
+        out["sample"] = f"{out['rows']} rows x {n} (repeated for ~{target_s:.0f} s), row loop"
+        return out
+
+
+class MlpWorkload(Workload):
+    """Resident-weight fp32 MLP forward: 4 x (sgemm + saxpy bias), batch 4096."""
+
+    def __init__(self, h, rank, world, args):
+        import torch
+
+        import b2blas
+
+        self.h, self.world = h, world
+        self.dims = [1024, 4096, 4096, 4096, 1024]
+        self.batch = 4096
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(42 + rank)
+        self.X = torch.rand(self.batch, self.dims[0], device=dev, generator=g) * 2 - 1
+        self.W, self.bias, self.Z = [], [], []
+        for i in range(4):
+            fi, fo = self.dims[i], self.dims[i + 1]
+            self.W.append(torch.randn(fi, fo, device=dev, generator=g) / fi ** 0.5)
+            b = torch.randn(fo, device=dev, generator=g) * 0.01
+            self.bias.append(b.repeat(self.batch, 1).contiguous())  # pre-broadcast, as the example does
+            self.Z.append(torch.empty(self.batch, fo, device=dev))
+        wrap = lambda t: b2blas.DeviceBuffer.from_ptr(h, t.data_ptr(), t.numel(), "float32", owner=t)  # noqa
+        self.xb = wrap(self.X)
+        self.wb = [wrap(t) for t in self.W]
+        self.bb = [wrap(t) for t in self.bias]
+        self.zb = [wrap(t) for t in self.Z]
+        self.launches_per_step = 8
+        self.kernel = "gemm_simt_kernel<float>"
+        self.bound = "fma"
+
+    def forward(self, xb):
+        inp = xb
+        for i in range(4):
+            fi, fo = self.dims[i], self.dims[i + 1]
+            self.h.sgemm_tiled(__import__("b2blas").GemmConfig(self.batch, fo, fi, 1.0, 0.0), inp, self.wb[i],
+                               self.zb[i])
+            self.h.saxpy(self.batch * fo, 1.0, self.bb[i], self.zb[i])
+            inp = self.zb[i]
+
+    def step(self):
+        self.forward(self.xb)
+
+    def units_per_step(self):
+        return sum(2.0 * self.batch * self.dims[i] * self.dims[i + 1] for i in range(4))
+
+    def e2e_setup(self):
+        import torch
+
+        self._hX, self.hX = _pinned_numpy(self.X)
+        self._hY = torch.empty(self.Z[-1].shape, dtype=torch.float32, pin_memory=True)
+        return self.X.numel() * 4, self.Z[-1].numel() * 4
+
+    def e2e_step(self):
+        import torch
+
+        self.X.copy_(torch.from_numpy(self.hX), non_blocking=True)
+        self.forward(self.xb)
+        self._hY.copy_(self.Z[-1], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    def config(self):
+        return {"workload": "mlp forward 1024-4096-4096-4096-1024, batch 4096, sgemm + saxpy bias"
+                            + (", one replica per GPU" if self.world > 1 else ""),
+                "layers": self.dims, "batch": self.batch, "parallelism": f"replicas x{self.world}",
+                "l2": "weights + activations larger than L2: no flush needed"}
+
+    def cpu_sample(self, oracle, target_s):
+        import numpy as np
+
+        rows = oracle.num_threads()
+        t0 = time.perf_counter()
+        flops = 0.0
+        inp = np.ascontiguousarray(self.X[:rows].cpu().numpy()).reshape(-1)
+        for i in range(4):
+            fi, fo = self.dims[i], self.dims[i + 1]
+            W = self.W[i].cpu().numpy().reshape(-1)
+            z = np.zeros(rows * fo, np.float32)
+            acc = np.empty(rows * fo, np.float32)
+            oracle.cpu_sgemm_rows(rows, fo, fi, 1.0, inp, W, 0.0, z, acc)
+            z += np.tile(self.bias[i][0].cpu().numpy(), rows)
+            flops += 2.0 * rows * fi * fo
+            inp = z
+        dt = time.perf_counter() - t0
+        return {"value": flops / dt / 1e12, "seconds": dt,
+                "sample": f"{rows} rows of the batch through all 4 layers, i-k-j host loop"}
+
+
+def make_workload(name, h, rank, world, args):
+    if name == "hgemm":
+        return GemmWorkload(h, rank, world, args, "hgemm", 8192, 8192, 8192, 1.0, 0.0, weak=True)
+    if name == "sgemm":
+        return GemmWorkload(h, rank, world, args, "sgemm", 8192, 8192, 8192, 1.5, 0.5, weak=False)
+    if name == "dgemm":
+        return GemmWorkload(h, rank, world, args, "dgemm", 4096, 4096, 4096, 1.5, 0.5, weak=False)
+    if name == "batched":
+        return BatchedWorkload(h, rank, world, args)
+    if name == "sgemv":
+        return SgemvWorkload(h, rank, world, args)
+    if name == "mlp":
+        return MlpWorkload(h, rank, world, args)
+    raise SystemExit(f"unknown workload {name}")
+
+
+# ----------------------------------------------------------------- peaks
+
+def roofline_peak(w, peaks, handle_info):
+    """(peak value, unit, source) for the workload's dominant kernel."""
+    if w.bound == "tensor":
+        return peaks["bf16_tflops"], "TFLOP/s", \
+            f"dense f16/bf16 tensor, cuBLAS bf16 burst, {peaks['_source']}"
+    if w.bound == "hbm":
+        return peaks["hbm_gbs"], "GB/s", f"HBM copy bandwidth, {peaks['_source']}"
+    sms = handle_info["sm_count"]
+    mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    lanes = 64 if w.dtype == "f64" else 128
+    return sms * lanes * 2 * mhz * 1e6 / 1e12, "TFLOP/s", \
+        f"computed FP{'64' if lanes == 64 else '32'} vector peak: {sms} SMs x {lanes} lanes x 2 x {mhz:.0f} MHz"
+
+
+# ------------------------------------------------------------ reference
+
+def run_reference(args, rank, world):
+    """The reference arm: the CPU restatement of the reference's algorithm
+    (the oracle's host loops), rank 0 only, a bounded sample per step."""
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    from oracle import oracle
+
+    oracle.set_num_threads(os.cpu_count() or 1)
+    nt = oracle.num_threads()
+    rng = np.random.default_rng(42)
+    wl = args.workload
+    per_step = 1.5  # seconds of CPU work per step
+    if wl in ("hgemm", "sgemm", "dgemm"):
+        m, n, k = (8192, 8192, 8192) if wl != "dgemm" else (4096, 4096, 4096)
+        alpha, beta = (1.0, 0.0) if wl == "hgemm" else (1.5, 0.5)
+        if wl == "hgemm":
+            B = (rng.standard_normal(k * n, dtype=np.float32) * 0.1).astype(np.float16).view(np.uint16)
+        else:
+            B = (rng.random(k * n) * 2 - 1).astype(np.float32 if wl == "sgemm" else np.float64)
+
+        def run(rows):
+            if wl == "hgemm":
+                A = (rng.standard_normal(rows * k, dtype=np.float32) * 0.1).astype(np.float16).view(np.uint16)
+                C = np.zeros(rows * n, np.uint16)
+                bf, acc = np.empty(k * n, np.float32), np.empty(rows * n, np.float32)
+                t0 = time.perf_counter()
+                oracle.cpu_hgemm_rows(rows, n, k, alpha, A, B, beta, C, bf, acc)
+            elif wl == "sgemm":
+                A = (rng.random(rows * k) * 2 - 1).astype(np.float32)
+                C = (rng.random(rows * n) * 2 - 1).astype(np.float32)
+                acc = np.empty(rows * n, np.float32)
+                t0 = time.perf_counter()
+                oracle.cpu_sgemm_rows(rows, n, k, alpha, A, B, beta, C, acc)
+            else:
+                A = rng.random(rows * k) * 2 - 1
+                C = rng.random(rows * n) * 2 - 1
+                acc = np.empty(rows * n)
+                t0 = time.perf_counter()
+                oracle.cpu_dgemm_rows(rows, n, k, alpha, A, B, beta, C, acc)
+            return time.perf_counter() - t0, 2.0 * rows * n * k
+
+        dt, _ = run(nt)
+        rows = max(nt, int(per_step / max(dt / nt, 1e-9)) // nt * nt)
+        rows = min(rows, m)
+        unit = "TFLOP/s"
+        sample = f"{rows} of {m} rows of C per step ({rows}x{n}x{k}), i-k-j host loop, {nt} threads"
+        cfg = {"workload": f"{wl} {m}x{n}x{k}", "m": m, "n": n, "k": k, "alpha": alpha, "beta": beta}
+        step = lambda: run(rows)  # noqa: E731
+        scale = 1e12
+        dtype = {"hgemm": "f16", "sgemm": "f32", "dgemm": "f64"}[wl]
+    elif wl == "batched":
+        m = 256
+        A = (rng.random(m * m) * 2 - 1).astype(np.float32)
+        B = (rng.random(m * m) * 2 - 1).astype(np.float32)
+        C = np.zeros(m * m, np.float32)
+        acc = np.empty(m * m, np.float32)
+
+        def run1():
+            t0 = time.perf_counter()
+            oracle.cpu_sgemm_rows(m, m, m, 1.0, A, B, 0.0, C, acc)
+            return time.perf_counter() - t0
+
+        nb = max(1, int(per_step / max(run1(), 1e-9)))
+
+        def step():
+            t = sum(run1() for _ in range(nb))
+            return t, 2.0 * nb * m ** 3
+
+        unit, scale, dtype = "TFLOP/s", 1e12, "f32"
+        sample = f"{nb} of the 4096 256^3 batches per step, i-k-j host loop, {nt} threads"
+        cfg = {"workload": "strided-batched sgemm 4096 x 256^3", "batch": 4096, "m": m, "n": m, "k": m}
+    elif wl == "sgemv":
+        n = 16384
+        rows = 4096
+        A = (rng.random(rows * n) * 2 - 1).astype(np.float32)
+        x = (rng.random(n) * 2 - 1).astype(np.float32)
+        y = np.zeros(rows, np.float32)
+
+        def step():
+            t0 = time.perf_counter()
+            oracle.cpu_sgemv_rows(rows, n, 1.0, A, x, 0.0, y)
+            return time.perf_counter() - t0, 4.0 * (rows * n + n + rows)
+
+        unit, scale, dtype = "GB/s", 1e9, "f32"
+        sample = f"{rows} of 16384 rows per step, row loop, {nt} threads"
+        cfg = {"workload": "sgemv 16384x16384 N", "m": 16384, "n": n}
+    else:
+        dims = [1024, 4096, 4096, 4096, 1024]
+        Ws = [(rng.standard_normal(dims[i] * dims[i + 1], dtype=np.float32) / dims[i] ** 0.5) for i in range(4)]
+        rows = nt * 4
+
+        def step():
+            inp = (rng.random(rows * dims[0]) * 2 - 1).astype(np.float32)
+            t0 = time.perf_counter()
+            fl = 0.0
+            for i in range(4):
+                z = np.zeros(rows * dims[i + 1], np.float32)
+                acc = np.empty_like(z)
+                oracle.cpu_sgemm_rows(rows, dims[i + 1], dims[i], 1.0, inp, Ws[i], 0.0, z, acc)
+                fl += 2.0 * rows * dims[i] * dims[i + 1]
+                inp = z
+            return time.perf_counter() - t0, fl
+
+        unit, scale, dtype = "TFLOP/s", 1e12, "f32"
+        sample = f"{rows} rows of the batch-4096 forward per step, i-k-j host loop, {nt} threads"
+        cfg = {"workload": "mlp forward 1024-4096-4096-4096-1024, batch 4096", "layers": dims, "batch": 4096}
+
+    for _ in range(args.warmup):
+        step()
+    tt, uu = 0.0, 0.0
+    for _ in range(args.steps):
+        t, u = step()
+        tt += t
+        uu += u
+    value = uu / tt / scale
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": tt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic (seeded)", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": nt, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference = CPU restatement of cublas-rs's kernels (Rust/cuda-oxide cannot be built here)"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ main
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b2blas", "reference"], default="b2blas")
+    ap.add_argument("--workload", choices=["hgemm", "sgemm", "dgemm", "batched", "sgemv", "mlp"], default="hgemm")
+    ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
+    ap.add_argument("--gather", action="store_true", help="column-sharded GEMMs: all-gather C every step")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import datetime
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    import b2blas
+
+    h = b2blas.Handle(local)
+    stream = torch.cuda.current_stream()
+    h.set_stream(stream.cuda_stream)
+    w = make_workload(args.workload, h, rank, world, args)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        w.step()
+    barrier()
+    h.synchronize()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier()
+    with sampler:
+        start.record(stream)
+        for _ in range(args.steps):
+            w.step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    h.synchronize()  # raises if a bounded device wait gave up
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    barrier()
+
+    units_local = w.units_per_step() * args.steps
+    total_units = units_local * world
+    value = w.scale(total_units / (ms_max / 1e3))
+
+    # dominant kernel roofline (per launch, this rank)
+    peaks = load_peaks()
+    info = h.device_info()
+    peak, punit, psrc = roofline_peak(w, peaks, info)
+    per_launch_ms = ms / args.steps
+    if isinstance(w, MlpWorkload):
+        # time the GEMMs alone for the kernel figure
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cfgs = [b2blas.GemmConfig(w.batch, w.dims[i + 1], w.dims[i], 1.0, 0.0) for i in range(4)]
+        e0.record(stream)
+        for _ in range(args.steps):
+            inp = w.xb
+            for i in range(4):
+                h.sgemm_tiled(cfgs[i], inp, w.wb[i], w.zb[i])
+                inp = w.zb[i]
+        e1.record(stream)
+        torch.cuda.synchronize()
+        per_launch_ms = e0.elapsed_time(e1) / args.steps
+        achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
+    elif isinstance(w, SgemvWorkload) or (isinstance(w, GemmWorkload) and w.gather):
+        achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
+    else:
+        achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
+    traffic = load_traffic().get(args.workload)
+    roof = {"bound": "hbm" if w.bound == "hbm" else "tensor" if w.bound == "tensor" else "fma",
+            "kernel": w.kernel, "achieved": achieved, "peak": peak, "unit": punit, "frac": achieved / peak,
+            "peak_source": psrc, "traffic": traffic,
+            "algorithmic_units_per_launch": w.units_per_step(),
+            "launch_ms": per_launch_ms}
+
+    # end to end through the host-slice API
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(3, min(args.steps, 10))
+    h2d, d2h = w.e2e_setup()
+    w.e2e_step()  # warm (staging allocation)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        w.e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = w.scale(w.units_per_step() * world * e2e_steps / (float(t.item()) / 1e3))
+    e2e = {"value": e2e_value, "unit": w.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "steps": e2e_steps, "api": "host-slice (_simple) calls on page-locked host buffers"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+
+        oracle.set_num_threads(os.cpu_count() or 1)
+        s = w.cpu_sample(oracle, args.cpu_seconds)
+        cpu = {"value": s["value"], "unit": w.unit, "cores": oracle.num_threads(), "kind": "port",
+               "sample": s["sample"], "seconds": round(s["seconds"], 2)}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": w.unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype,
+                "data": "synthetic (seeded torch generators; normal(0,0.1)->f16 for HGEMM, uniform[-1,1) else)",
+                "config": w.config(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": w.launches_per_step * args.steps, "clocks": sampler.summary()}
+        print(json.dumps(line), flush=True)
+    h.set_stream(None)
+    h.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

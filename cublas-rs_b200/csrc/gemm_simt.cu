@@ -1,0 +1,401 @@
+// gemm_simt.cu -- register-blocked FFMA / DFMA GEMM for sm_100a: SGEMM,
+// DGEMM and strided-batched SGEMM.
+//
+// Computes, per batch b, C_b <- alpha * A_b * B_b + beta * C_b with row-major
+// A_b[M x K], B_b[K x N], C_b[M x N] and X_b = X + b * stride_X, the operation
+// of cublas-rs's sgemm_* / dgemm_* / strided_batched_sgemm kernels
+// (crates/cublas-l3/src/sgemm.rs:31-360, dgemm.rs:25-334, batched.rs:25-102).
+// Unlike those (one 16x16 or 32x32 shared tile per CTA, one or four outputs
+// per thread), every CTA here owns a BM x BN tile and every thread a TM x TN
+// register block, so each shared-memory value feeds TM (or TN) FMAs:
+//
+//   * 256 threads = 8 warps laid out WARPS_M x WARPS_N; a warp is 4 x 8
+//     threads; a thread's rows are ty*4+{0..3} (+16 when TM=8) and its
+//     columns tx*4+{0..3} (+32 when TN=8) inside the warp tile, so fragment
+//     loads are 16-byte shared loads with no bank conflicts (A values are
+//     broadcast to the 8 threads of a row group, B values are 8 distinct
+//     16-byte chunks).
+//   * A is stored transposed in shared memory (As[k][m], padded by 4) so
+//     that fragments along M are contiguous; B is stored as-is (Bs[k][n]).
+//   * Two shared stages; the next k-tile is fetched from global memory into
+//     registers while the current one is multiplied, then stored to the
+//     other stage -- one __syncthreads per k-tile.
+//   * The epilogue skips reading C when beta == 0.
+//   * The batch and tile indices come from one flattened grid index, so there
+//     is no 65535 limit on the batch count (the reference puts the batch in
+//     gridDim.z, batched.rs:128-137).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename T>
+struct Vec4;
+template <>
+struct Vec4<float> {
+    __device__ __forceinline__ static void load(const float *p, float (&v)[4]) {
+        float4 t = *reinterpret_cast<const float4 *>(p);
+        v[0] = t.x;
+        v[1] = t.y;
+        v[2] = t.z;
+        v[3] = t.w;
+    }
+    __device__ __forceinline__ static void store(float *p, const float (&v)[4]) {
+        *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+};
+template <>
+struct Vec4<double> {
+    __device__ __forceinline__ static void load(const double *p, double (&v)[4]) {
+        double2 a = reinterpret_cast<const double2 *>(p)[0];
+        double2 b = reinterpret_cast<const double2 *>(p)[1];
+        v[0] = a.x;
+        v[1] = a.y;
+        v[2] = b.x;
+        v[3] = b.y;
+    }
+    __device__ __forceinline__ static void store(double *p, const double (&v)[4]) {
+        reinterpret_cast<double2 *>(p)[0] = make_double2(v[0], v[1]);
+        reinterpret_cast<double2 *>(p)[1] = make_double2(v[2], v[3]);
+    }
+};
+
+// 16-byte global vector of T (4 floats or 2 doubles).
+template <typename T>
+struct GVec;
+template <>
+struct GVec<float> {
+    static constexpr int W = 4;
+    using V = float4;
+    __device__ __forceinline__ static void get(const V &v, float (&o)[4]) {
+        o[0] = v.x;
+        o[1] = v.y;
+        o[2] = v.z;
+        o[3] = v.w;
+    }
+};
+template <>
+struct GVec<double> {
+    static constexpr int W = 2;
+    using V = double2;
+    __device__ __forceinline__ static void get(const V &v, double (&o)[2]) {
+        o[0] = v.x;
+        o[1] = v.y;
+    }
+};
+
+template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK>
+struct Cfg {
+    static constexpr int BM = WARPS_M * (TM / 4) * 16;
+    static constexpr int BN = WARPS_N * (TN / 4) * 32;
+    static constexpr int W = GVec<T>::W;
+    static constexpr int PADA = 4;
+    static constexpr int LDA_S = BM + PADA;  // As[k][m]
+    static constexpr int LDB_S = BN;         // Bs[k][n]
+    static constexpr int A_VECS = BM * BK / W / kThreads;
+    static constexpr int B_VECS = BK * BN / W / kThreads;
+    static constexpr int A_ELEMS = BM * BK / kThreads;  // scalar path
+    static constexpr int B_ELEMS = BK * BN / kThreads;
+    static constexpr int SMEM = 2 * BK * (LDA_S + LDB_S) * (int)sizeof(T);
+    static_assert(WARPS_M * WARPS_N * 32 == kThreads, "256 threads");
+    static_assert(A_VECS * W * kThreads == BM * BK, "A tile divides");
+    static_assert(B_VECS * W * kThreads == BK * BN, "B tile divides");
+};
+
+struct TileMap {
+    int64_t tiles_m, tiles_n, tiles_per_batch;
+};
+
+// Grouped raster: GROUP consecutive M tiles sweep the N tiles together, so
+// the A and B panels of the CTAs resident at one time stay in L2.
+__device__ __forceinline__ void map_tile(int64_t t, const TileMap &tm, int64_t &batch, int64_t &bm, int64_t &bn) {
+    constexpr int64_t GROUP = 8;
+    batch = t / tm.tiles_per_batch;
+    int64_t r = t - batch * tm.tiles_per_batch;
+    int64_t group_span = GROUP * tm.tiles_n;
+    int64_t g = r / group_span;
+    int64_t first_m = g * GROUP;
+    int64_t gm = tm.tiles_m - first_m < GROUP ? tm.tiles_m - first_m : GROUP;
+    int64_t rr = r - g * group_span;
+    bm = first_m + rr % gm;
+    bn = rr / gm;
+}
+
+template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, bool VEC, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB)
+    gemm_simt_kernel(const T *__restrict__ A, const T *__restrict__ B, T *__restrict__ C, int64_t M, int64_t N,
+                     int64_t K, T alpha, T beta, int64_t sA, int64_t sB, int64_t sC, TileMap tmap) {
+    using Cf = Cfg<T, TM, TN, WARPS_M, WARPS_N, BK>;
+    constexpr int BM = Cf::BM, BN = Cf::BN, W = Cf::W;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T *As = reinterpret_cast<T *>(smem_raw);         // [2][BK][LDA_S]
+    T *Bs = As + 2 * BK * Cf::LDA_S;                  // [2][BK][LDB_S]
+
+    int64_t batch, bm, bn;
+    map_tile(blockIdx.x, tmap, batch, bm, bn);
+    A += batch * sA;
+    B += batch * sB;
+    C += batch * sC;
+    const int64_t m0 = bm * BM, n0 = bn * BN;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int wm = warp / WARPS_N, wn = warp % WARPS_N;
+    const int ty = lane >> 3, tx = lane & 7;
+    const int row_base = wm * (TM / 4) * 16 + ty * 4;  // + g*16
+    const int col_base = wn * (TN / 4) * 32 + tx * 4;  // + g*32
+
+    T acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = T(0);
+
+    // Registers holding the next k-tile on its way to shared memory.
+    T ra[VEC ? Cf::A_VECS * W : Cf::A_ELEMS];
+    T rb[VEC ? Cf::B_VECS * W : Cf::B_ELEMS];
+
+    // Per-thread source pointers, advanced by one k-tile per fetch; the row
+    // (A) and column (B) bounds are fixed per thread, only k varies.
+    constexpr int AV = VEC ? Cf::A_VECS : Cf::A_ELEMS;
+    constexpr int BV = VEC ? Cf::B_VECS : Cf::B_ELEMS;
+    constexpr int AW = VEC ? W : 1;
+    const T *pa[AV];
+    const T *pb[BV];
+    int ka[AV], kb[BV];  // k offset of each load inside the tile
+    bool oka[AV], okb[BV];
+#pragma unroll
+    for (int v = 0; v < AV; ++v) {
+        const int idx = tid + v * kThreads;
+        const int r = idx / (BK / AW), kc = (idx % (BK / AW)) * AW;
+        oka[v] = m0 + r < M;
+        pa[v] = A + (oka[v] ? (m0 + r) * K : 0) + kc;
+        ka[v] = kc;
+    }
+#pragma unroll
+    for (int v = 0; v < BV; ++v) {
+        const int idx = tid + v * kThreads;
+        const int kr = idx / (BN / AW), c = (idx % (BN / AW)) * AW;
+        okb[v] = n0 + c < N;
+        pb[v] = B + static_cast<int64_t>(kr) * N + (okb[v] ? n0 + c : 0);
+        kb[v] = kr;
+    }
+    const int64_t b_step = static_cast<int64_t>(BK) * N;
+
+    auto fetch = [&](int64_t k0) {
+#pragma unroll
+        for (int v = 0; v < AV; ++v) {
+            if constexpr (VEC) {
+                T tmp[W];
+                if (oka[v] && k0 + ka[v] < K) {
+                    GVec<T>::get(*reinterpret_cast<const typename GVec<T>::V *>(pa[v]), tmp);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < W; ++e) tmp[e] = T(0);
+                }
+#pragma unroll
+                for (int e = 0; e < W; ++e) ra[v * W + e] = tmp[e];
+            } else {
+                ra[v] = (oka[v] && k0 + ka[v] < K) ? *pa[v] : T(0);
+            }
+            pa[v] += BK;
+        }
+#pragma unroll
+        for (int v = 0; v < BV; ++v) {
+            if constexpr (VEC) {
+                T tmp[W];
+                if (okb[v] && k0 + kb[v] < K) {
+                    GVec<T>::get(*reinterpret_cast<const typename GVec<T>::V *>(pb[v]), tmp);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < W; ++e) tmp[e] = T(0);
+                }
+#pragma unroll
+                for (int e = 0; e < W; ++e) rb[v * W + e] = tmp[e];
+            } else {
+                rb[v] = (okb[v] && k0 + kb[v] < K) ? *pb[v] : T(0);
+            }
+            pb[v] += b_step;
+        }
+    };
+
+    auto stash = [&](int stage) {
+        T *as = As + stage * BK * Cf::LDA_S;
+        T *bs = Bs + stage * BK * Cf::LDB_S;
+        if constexpr (VEC) {
+#pragma unroll
+            for (int v = 0; v < Cf::A_VECS; ++v) {
+                int idx = tid + v * kThreads;
+                int r = idx / (BK / W), kc = (idx % (BK / W)) * W;
+#pragma unroll
+                for (int e = 0; e < W; ++e) as[(kc + e) * Cf::LDA_S + r] = ra[v * W + e];
+            }
+#pragma unroll
+            for (int v = 0; v < Cf::B_VECS; ++v) {
+                int idx = tid + v * kThreads;
+                int kr = idx / (BN / W), c = (idx % (BN / W)) * W;
+                if constexpr (W == 4) {
+                    *reinterpret_cast<float4 *>(&bs[kr * Cf::LDB_S + c]) =
+                        make_float4(rb[v * 4 + 0], rb[v * 4 + 1], rb[v * 4 + 2], rb[v * 4 + 3]);
+                } else {
+                    *reinterpret_cast<double2 *>(&bs[kr * Cf::LDB_S + c]) = make_double2(rb[v * 2 + 0], rb[v * 2 + 1]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int v = 0; v < Cf::A_ELEMS; ++v) {
+                int idx = tid + v * kThreads;
+                int r = idx / BK, kc = idx % BK;
+                as[kc * Cf::LDA_S + r] = ra[v];
+            }
+#pragma unroll
+            for (int v = 0; v < Cf::B_ELEMS; ++v) {
+                int idx = tid + v * kThreads;
+                int kr = idx / BN, c = idx % BN;
+                bs[kr * Cf::LDB_S + c] = rb[v];
+            }
+        }
+    };
+
+    const int64_t ktiles = (K + BK - 1) / BK;
+    fetch(0);
+    stash(0);
+    __syncthreads();
+
+    for (int64_t kt = 0; kt < ktiles; ++kt) {
+        const int cur = static_cast<int>(kt & 1);
+        const bool more = kt + 1 < ktiles;
+        if (more) fetch((kt + 1) * BK);
+        const T *as = As + cur * BK * Cf::LDA_S;
+        const T *bs = Bs + cur * BK * Cf::LDB_S;
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            T af[TM], bf[TN];
+#pragma unroll
+            for (int g = 0; g < TM / 4; ++g) {
+                T t[4];
+                Vec4<T>::load(as + kk * Cf::LDA_S + row_base + g * 16, t);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) af[g * 4 + e] = t[e];
+            }
+#pragma unroll
+            for (int g = 0; g < TN / 4; ++g) {
+                T t[4];
+                Vec4<T>::load(bs + kk * Cf::LDB_S + col_base + g * 32, t);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) bf[g * 4 + e] = t[e];
+            }
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fma(af[i], bf[j], acc[i][j]);
+        }
+        if (more) stash(cur ^ 1);
+        __syncthreads();
+    }
+
+    // Epilogue: C = alpha*acc (+ beta*C).
+    const bool read_c = beta != T(0);
+#pragma unroll
+    for (int gi = 0; gi < TM / 4; ++gi) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t r = m0 + row_base + gi * 16 + i;
+            if (r >= M) continue;
+            T *crow = C + r * N;
+#pragma unroll
+            for (int gj = 0; gj < TN / 4; ++gj) {
+                const int64_t c = n0 + col_base + gj * 32;
+                T out[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) out[e] = alpha * acc[gi * 4 + i][gj * 4 + e];
+                if (VEC && c + 4 <= N) {
+                    if (read_c) {
+                        T old[4];
+                        Vec4<T>::load(crow + c, old);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) out[e] = fma(beta, old[e], out[e]);
+                    }
+                    Vec4<T>::store(crow + c, out);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (c + e < N) {
+                            T v = out[e];
+                            if (read_c) v = fma(beta, crow[c + e], v);
+                            crow[c + e] = v;
+                        }
+                    }
+                }
+            }
+        }
+    }
+}
+
+template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, int MINB>
+int run_simt(b2b_handle *h, int64_t M, int64_t N, int64_t K, T alpha, T beta, const T *A, int64_t sA, const T *B,
+             int64_t sB, T *C, int64_t sC, int64_t batch) {
+    using Cf = Cfg<T, TM, TN, WARPS_M, WARPS_N, BK>;
+    TileMap tm;
+    tm.tiles_m = (M + Cf::BM - 1) / Cf::BM;
+    tm.tiles_n = (N + Cf::BN - 1) / Cf::BN;
+    tm.tiles_per_batch = tm.tiles_m * tm.tiles_n;
+    const int64_t blocks = tm.tiles_per_batch * batch;
+    if (blocks > 0x7fffffffLL) return b2b::fail(B2B_ERR_INVALID_ARG, "GEMM grid exceeds 2^31-1 tiles");
+    // 16-byte vector path: every row start and the base pointers aligned.
+    constexpr int W = Cf::W;
+    const bool vec = (K % W == 0) && (N % W == 0) && (sA % W == 0) && (sB % W == 0) && (sC % W == 0) &&
+                     b2b::aligned16(A) && b2b::aligned16(B) && b2b::aligned16(C);
+    cudaError_t e;
+    if (vec) {
+        auto kern = gemm_simt_kernel<T, TM, TN, WARPS_M, WARPS_N, BK, true, MINB>;
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+        if (e == cudaSuccess) {
+            kern<<<static_cast<unsigned>(blocks), kThreads, Cf::SMEM, h->stream>>>(A, B, C, M, N, K, alpha, beta,
+                                                                                   sA, sB, sC, tm);
+            e = cudaGetLastError();
+        }
+    } else {
+        auto kern = gemm_simt_kernel<T, TM, TN, WARPS_M, WARPS_N, BK, false, MINB>;
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+        if (e == cudaSuccess) {
+            kern<<<static_cast<unsigned>(blocks), kThreads, Cf::SMEM, h->stream>>>(A, B, C, M, N, K, alpha, beta,
+                                                                                   sA, sB, sC, tm);
+            e = cudaGetLastError();
+        }
+    }
+    if (e != cudaSuccess) return b2b::fail_cuda(e, "GEMM launch");
+    return B2B_OK;
+}
+
+}  // namespace
+
+namespace b2b {
+
+// SGEMM: 128x128 CTA tile, 8x8 per thread, BK=8, two CTAs per SM.
+int launch_sgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
+                 float beta, float *C) {
+    return run_simt<float, 8, 8, 4, 2, 8, 2>(h, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, 0, B, 0, C, 0,
+                                             1);
+}
+
+int launch_sgemm_strided_batched(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
+                                 size_t sa, const float *B, size_t sb, float beta, float *C, size_t sc,
+                                 size_t batch) {
+    return run_simt<float, 8, 8, 4, 2, 8, 2>(h, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, (int64_t)sa, B,
+                                             (int64_t)sb, C, (int64_t)sc, (int64_t)batch);
+}
+
+// DGEMM: 64x64 CTA tile, 4x4 per thread, BK=16; the FP64 pipe issues at half
+// the FP32 rate, so a smaller register block keeps three CTAs resident.
+int launch_dgemm(b2b_handle *h, size_t m, size_t n, size_t k, double alpha, const double *A, const double *B,
+                 double beta, double *C) {
+    return run_simt<double, 4, 4, 4, 2, 16, 2>(h, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, 0, B, 0, C,
+                                               0, 1);
+}
+
+}  // namespace b2b

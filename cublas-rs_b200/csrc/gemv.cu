@@ -1,0 +1,244 @@
+// gemv.cu -- SGEMV for sm_100a: y <- alpha * op(A) * x + beta * y, A m x n
+// row-major, op(A) = A (N) or A^T (T), the operation of cublas-rs's
+// sgemv_n / sgemv_t / sgemv_n_tiled / sgemv_t_tiled
+// (crates/cublas-l2/src/gemv.rs:29-223).
+//
+// SGEMV reads every element of A once, so it is bound by HBM bandwidth; the
+// kernels are built to keep enough 16-byte loads in flight:
+//   * N: one warp per row; each lane streams 16-byte vectors of the row with
+//     ld.global.nc.L1::no_allocate (A is touched once, keep it out of L1),
+//     UNROLL vectors in flight per lane, while x is read through L1 (it is
+//     shared by every row); warp-shuffle reduction, lane 0 writes y.
+//   * T: the rows are split into S slices; CTA (column block, slice) walks
+//     its slice with each lane owning 4 consecutive columns (16-byte loads
+//     across the row, coalesced), reduces its 8 warps through shared memory
+//     and writes one partial row.  A second kernel sums the S partials in a
+//     fixed order (deterministic) and applies alpha/beta.  S is chosen so
+//     that about 4 CTAs per SM are in flight.  The partials live in the
+//     handle's workspace (S * n floats).
+// beta == 0 does not read y.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+
+__device__ __forceinline__ float4 ld_stream(const float4 *p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float ld_stream1(const float *p) {
+    float v;
+    asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <int UNROLL, bool VEC>
+__global__ void __launch_bounds__(kThreads) sgemv_n_kernel(const float *__restrict__ A, const float *__restrict__ x,
+                                                           float *__restrict__ y, int64_t m, int64_t n, float alpha,
+                                                           float beta) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+    if (row >= m) return;
+    float acc = 0.0f;
+    if constexpr (VEC) {
+        const float4 *a = reinterpret_cast<const float4 *>(A + row * n);
+        const float4 *xv = reinterpret_cast<const float4 *>(x);
+        const int64_t nv = n >> 2;
+        int64_t j = lane;
+        // Full groups: UNROLL independent 16-byte loads per lane in flight.
+        for (; j + 32 * (UNROLL - 1) < nv; j += 32 * UNROLL) {
+            float4 av[UNROLL], xx[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) av[u] = ld_stream(a + j + 32 * u);
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) xx[u] = __ldg(xv + j + 32 * u);
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                acc = fmaf(av[u].x, xx[u].x, acc);
+                acc = fmaf(av[u].y, xx[u].y, acc);
+                acc = fmaf(av[u].z, xx[u].z, acc);
+                acc = fmaf(av[u].w, xx[u].w, acc);
+            }
+        }
+        for (; j < nv; j += 32) {
+            float4 av = ld_stream(a + j), xx = __ldg(xv + j);
+            acc = fmaf(av.x, xx.x, acc);
+            acc = fmaf(av.y, xx.y, acc);
+            acc = fmaf(av.z, xx.z, acc);
+            acc = fmaf(av.w, xx.w, acc);
+        }
+    } else {
+        const float *a = A + row * n;
+        for (int64_t j = lane; j < n; j += 32) acc = fmaf(ld_stream1(a + j), __ldg(x + j), acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        float v = alpha * acc;
+        if (beta != 0.0f) v = fmaf(beta, y[row], v);
+        y[row] = v;
+    }
+}
+
+// T, pass 1: CTA (blockIdx.x = column block of 128, blockIdx.y = row slice).
+// Lane l of every warp owns columns cb*128 + 4l .. +3 (VEC) or
+// cb*128 + l + 32e, e = 0..3 (scalar).  Warp w takes rows r0+w, r0+w+8, ...
+// Writes partial[slice][col] (direct=false) or y (direct=true, one slice).
+template <bool VEC, bool DIRECT>
+__global__ void __launch_bounds__(kThreads) sgemv_t_partial_kernel(const float *__restrict__ A,
+                                                                   const float *__restrict__ x,
+                                                                   float *__restrict__ out, int64_t m, int64_t n,
+                                                                   int64_t rows_per_slice, float alpha, float beta) {
+    __shared__ float red[kWarps][128];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t c0 = static_cast<int64_t>(blockIdx.x) * 128;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * rows_per_slice;
+    const int64_t r1 = r0 + rows_per_slice < m ? r0 + rows_per_slice : m;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (VEC) {
+        const int64_t c = c0 + lane * 4;
+        if (c < n) {  // n % 4 == 0, so the whole vector is in range
+            int64_t r = r0 + warp;
+            for (; r + 3 * kWarps < r1; r += 4 * kWarps) {
+                float4 v[4];
+                float xs[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = ld_stream(reinterpret_cast<const float4 *>(A + (r + u * kWarps) * n + c));
+#pragma unroll
+                for (int u = 0; u < 4; ++u) xs[u] = __ldg(x + r + u * kWarps);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    acc[0] = fmaf(v[u].x, xs[u], acc[0]);
+                    acc[1] = fmaf(v[u].y, xs[u], acc[1]);
+                    acc[2] = fmaf(v[u].z, xs[u], acc[2]);
+                    acc[3] = fmaf(v[u].w, xs[u], acc[3]);
+                }
+            }
+            for (; r < r1; r += kWarps) {
+                float4 v = ld_stream(reinterpret_cast<const float4 *>(A + r * n + c));
+                float xs = __ldg(x + r);
+                acc[0] = fmaf(v.x, xs, acc[0]);
+                acc[1] = fmaf(v.y, xs, acc[1]);
+                acc[2] = fmaf(v.z, xs, acc[2]);
+                acc[3] = fmaf(v.w, xs, acc[3]);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[warp][lane * 4 + e] = acc[e];
+    } else {
+        for (int64_t r = r0 + warp; r < r1; r += kWarps) {
+            const float xs = __ldg(x + r);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int64_t c = c0 + lane + 32 * e;
+                if (c < n) acc[e] = fmaf(ld_stream1(A + r * n + c), xs, acc[e]);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[warp][lane + 32 * e] = acc[e];
+    }
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        const int64_t c = c0 + threadIdx.x;
+        if (c < n) {
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) s += red[w][threadIdx.x];
+            if constexpr (DIRECT) {
+                float v = alpha * s;
+                if (beta != 0.0f) v = fmaf(beta, out[c], v);
+                out[c] = v;
+            } else {
+                out[static_cast<int64_t>(blockIdx.y) * n + c] = s;
+            }
+        }
+    }
+}
+
+// T, pass 2: y[j] = alpha * sum_s partial[s][j] + beta * y[j], s in order.
+__global__ void sgemv_t_reduce_kernel(const float *__restrict__ partial, float *__restrict__ y, int64_t n,
+                                      int slices, float alpha, float beta) {
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    float s = 0.0f;
+    for (int i = 0; i < slices; ++i) s += partial[static_cast<int64_t>(i) * n + j];
+    float v = alpha * s;
+    if (beta != 0.0f) v = fmaf(beta, y[j], v);
+    y[j] = v;
+}
+
+}  // namespace
+
+namespace b2b {
+
+int launch_sgemv(b2b_handle *h, int trans, size_t m_, size_t n_, float alpha, const float *A, const float *x,
+                 float beta, float *y) {
+    const int64_t m = static_cast<int64_t>(m_), n = static_cast<int64_t>(n_);
+    const bool vec = (n % 4 == 0) && aligned16(A) && aligned16(x);
+    cudaError_t e;
+    if (trans == B2B_OP_N) {
+        const int64_t blocks = (m + kWarps - 1) / kWarps;
+        if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemv: m too large");
+        if (vec)
+            sgemv_n_kernel<8, true><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
+        else
+            sgemv_n_kernel<8, false><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fail_cuda(e, "sgemv N launch");
+        return B2B_OK;
+    }
+    const bool vec_t = (n % 4 == 0) && aligned16(A);
+    const int64_t col_blocks = (n + 127) / 128;
+    if (col_blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemv: n too large");
+    // Enough slices for ~4 CTAs per SM, each slice at least 64 rows.
+    int64_t target = 4LL * h->sm_count;
+    int64_t slices = (target + col_blocks - 1) / col_blocks;
+    int64_t max_slices = (m + 63) / 64;
+    if (slices > max_slices) slices = max_slices;
+    if (slices > 65535) slices = 65535;
+    if (slices < 1) slices = 1;
+    int64_t rows_per = (m + slices - 1) / slices;
+    slices = (m + rows_per - 1) / rows_per;
+    if (slices == 1) {
+        dim3 grid((unsigned)col_blocks, 1);
+        if (vec_t)
+            sgemv_t_partial_kernel<true, true><<<grid, kThreads, 0, h->stream>>>(A, x, y, m, n, rows_per, alpha, beta);
+        else
+            sgemv_t_partial_kernel<false, true><<<grid, kThreads, 0, h->stream>>>(A, x, y, m, n, rows_per, alpha, beta);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fail_cuda(e, "sgemv T launch");
+        return B2B_OK;
+    }
+    void *ws = nullptr;
+    int rc = workspace(h, static_cast<size_t>(slices) * static_cast<size_t>(n) * sizeof(float), &ws);
+    if (rc) return rc;
+    float *partial = static_cast<float *>(ws);
+    dim3 grid((unsigned)col_blocks, (unsigned)slices);
+    if (vec_t)
+        sgemv_t_partial_kernel<true, false><<<grid, kThreads, 0, h->stream>>>(A, x, partial, m, n, rows_per, alpha, beta);
+    else
+        sgemv_t_partial_kernel<false, false><<<grid, kThreads, 0, h->stream>>>(A, x, partial, m, n, rows_per, alpha, beta);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "sgemv T partial launch");
+    const int64_t rblocks = (n + 255) / 256;
+    sgemv_t_reduce_kernel<<<(unsigned)rblocks, 256, 0, h->stream>>>(partial, y, n, (int)slices, alpha, beta);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "sgemv T reduce launch");
+    return B2B_OK;
+}
+
+}  // namespace b2b

@@ -1,0 +1,318 @@
+// host_slices.cu -- the host-slice ("_simple") flavours: copy the operands in,
+// run the kernel, copy the result out, block until it is on the host.
+//
+// Mirrors cublas_l3::sgemm_* / dgemm_* / hgemm_half / strided_batched_sgemm /
+// batched_sgemm and cublas_l2::sgemv* / cublas_l1::saxpy host launchers
+// (crates/cublas-l3/src/sgemm.rs:401-424, hgemm.rs:135-187,
+// batched.rs:162-261, crates/cublas-l2/src/gemv.rs:266-305,
+// crates/cublas-l1/src/saxpy.rs:45-66), including their length checks, which
+// the reference enforces with assert! and which return B2B_ERR_DIMENSION here.
+//
+// Differences, all in the data movement, none in the results:
+//   * Device staging is a grow-only buffer owned by the handle instead of
+//     three fresh allocations per call.
+//   * C is not uploaded when beta == 0 (it is not read).
+//   * The GEMMs split M into row panels and pipeline them over three
+//     streams: B goes up first, then panel p's rows of A (and C) go up on the
+//     copy stream while panel p-1 computes and panel p-2's C comes back on
+//     the return stream.  With page-locked host buffers the host<->device
+//     copies in both directions overlap the tensor-core work.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+using namespace b2b;
+
+namespace {
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int dim_err(const char *fn, const char *what, size_t expected, size_t got) {
+    return fail(B2B_ERR_DIMENSION, std::string(fn) + ": dimension mismatch in " + what + ": expected " +
+                                       std::to_string(expected) + ", got " + std::to_string(got));
+}
+
+// Per-call stream/event set for the pipelined copies.
+struct Pipe {
+    cudaStream_t up = nullptr, down = nullptr;
+    std::vector<cudaEvent_t> ev;
+    ~Pipe() {
+        for (auto e : ev) cudaEventDestroy(e);
+        if (up) cudaStreamDestroy(up);
+        if (down) cudaStreamDestroy(down);
+    }
+    int init(int nev) {
+        cudaError_t e = cudaStreamCreateWithFlags(&up, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&down, cudaStreamNonBlocking);
+        for (int i = 0; i < nev && e == cudaSuccess; ++i) {
+            cudaEvent_t ev1;
+            e = cudaEventCreateWithFlags(&ev1, cudaEventDisableTiming);
+            if (e == cudaSuccess) ev.push_back(ev1);
+        }
+        if (e != cudaSuccess) return fail_cuda(e, "pipeline setup");
+        return B2B_OK;
+    }
+};
+
+int finish(b2b_handle *h) {
+    cudaError_t e = cudaStreamSynchronize(h->stream);
+    if (e != cudaSuccess) return fail_cuda(e, "host-slice call");
+    int st = 0;
+    e = cudaMemcpy(&st, h->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail_cuda(e, "reading device status");
+    if (st) {
+        cudaMemset(h->d_status, 0, sizeof(int));
+        return fail(B2B_ERR_DEVICE_TIMEOUT, "a bounded device wait gave up (status " + std::to_string(st) + ")");
+    }
+    return B2B_OK;
+}
+
+// Pipelined host-slice GEMM for element type T, with `launch` the device
+// launcher for one row panel.
+template <typename T, typename S, typename Launch>
+int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S alpha, const T *A, size_t a_len,
+                const T *B, size_t b_len, S beta, T *C, size_t c_len, Launch launch) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");
+    // Same order as the reference: length asserts first, then the early
+    // return on empty dimensions (sgemm.rs:469-474).
+    if (a_len != m * k) return dim_err(fn, "A length (m*k)", m * k, a_len);
+    if (b_len != k * n) return dim_err(fn, "B length (k*n)", k * n, b_len);
+    if (c_len != m * n) return dim_err(fn, "C length (m*n)", m * n, c_len);
+    if (m == 0 || n == 0 || k == 0) return B2B_OK;
+    if (!A || !B || !C) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL slice");
+    DeviceGuard g(h);
+    const size_t ea = m * k * sizeof(T), eb = k * n * sizeof(T), ec = m * n * sizeof(T);
+    const size_t oa = 0, ob = round_up(ea, 256), oc = ob + round_up(eb, 256);
+    void *stage = nullptr;
+    int rc = staging(h, oc + round_up(ec, 256), &stage);
+    if (rc) return rc;
+    T *dA = reinterpret_cast<T *>(static_cast<char *>(stage) + oa);
+    T *dB = reinterpret_cast<T *>(static_cast<char *>(stage) + ob);
+    T *dC = reinterpret_cast<T *>(static_cast<char *>(stage) + oc);
+    const bool up_c = beta != S(0);
+
+    // Row panels: ~8 for large problems, multiples of 128 rows so the
+    // tensor-core tiles of a panel start on a tile boundary.
+    const size_t bytes = ea + eb + ec;
+    int panels = bytes >= (size_t(64) << 20) ? 8 : 1;
+    size_t prow = round_up((m + panels - 1) / panels, 128);
+    if (prow > m) prow = m;
+    panels = static_cast<int>((m + prow - 1) / prow);
+
+    Pipe p;
+    if ((rc = p.init(2 * panels + 1))) return rc;
+    cudaError_t e = cudaSuccess;
+    cudaStream_t cs = h->stream;
+    // The compute stream's earlier work (e.g. a previous call still using
+    // the staging buffer) must finish before the copies overwrite it.
+    cudaEvent_t start_ev = p.ev[2 * panels];
+    e = cudaEventRecord(start_ev, cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p.up, start_ev, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dB, B, eb, cudaMemcpyHostToDevice, p.up);
+    for (int i = 0; i < panels && e == cudaSuccess; ++i) {
+        const size_t r0 = static_cast<size_t>(i) * prow;
+        const size_t rows = (r0 + prow <= m) ? prow : m - r0;
+        e = cudaMemcpyAsync(dA + r0 * k, A + r0 * k, rows * k * sizeof(T), cudaMemcpyHostToDevice, p.up);
+        if (e == cudaSuccess && up_c)
+            e = cudaMemcpyAsync(dC + r0 * n, C + r0 * n, rows * n * sizeof(T), cudaMemcpyHostToDevice, p.up);
+        if (e == cudaSuccess) e = cudaEventRecord(p.ev[2 * i], p.up);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, p.ev[2 * i], 0);
+        if (e != cudaSuccess) break;
+        rc = launch(h, rows, n, k, alpha, dA + r0 * k, dB, beta, dC + r0 * n);
+        if (rc) {
+            cudaStreamSynchronize(p.up);
+            cudaStreamSynchronize(cs);
+            return rc;
+        }
+        e = cudaEventRecord(p.ev[2 * i + 1], cs);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p.down, p.ev[2 * i + 1], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(C + r0 * n, dC + r0 * n, rows * n * sizeof(T), cudaMemcpyDeviceToHost, p.down);
+    }
+    cudaError_t e2 = cudaStreamSynchronize(p.up);
+    cudaError_t e3 = cudaStreamSynchronize(p.down);
+    if (e == cudaSuccess) e = e2;
+    if (e == cudaSuccess) e = e3;
+    if (e != cudaSuccess) {
+        cudaStreamSynchronize(cs);
+        return fail_cuda(e, fn);
+    }
+    return finish(h);
+}
+
+int h2d(b2b_handle *h, void *d, const void *s, size_t bytes) {
+    if (!bytes) return B2B_OK;
+    cudaError_t e = cudaMemcpyAsync(d, s, bytes, cudaMemcpyHostToDevice, h->stream);
+    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "host-to-device copy");
+}
+
+int d2h(b2b_handle *h, void *d, const void *s, size_t bytes) {
+    if (!bytes) return B2B_OK;
+    cudaError_t e = cudaMemcpyAsync(d, s, bytes, cudaMemcpyDeviceToHost, h->stream);
+    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "device-to-host copy");
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2b_sgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t k, float alpha, const float *A,
+                     size_t a_len, const float *B, size_t b_len, float beta, float *C, size_t c_len) {
+    if (algo < B2B_ALGO_DEFAULT || algo > B2B_ALGO_3XTF32)
+        return fail(B2B_ERR_INVALID_ARG, "b2b_sgemm_simple: unknown algo " + std::to_string(algo));
+    return gemm_simple<float, float>(
+        h, "b2b_sgemm_simple", m, n, k, alpha, A, a_len, B, b_len, beta, C, c_len,
+        [algo](b2b_handle *hh, size_t mm, size_t nn, size_t kk, float al, const float *a, const float *b, float be,
+               float *c) {
+            return algo == B2B_ALGO_3XTF32 ? launch_sgemm_3xtf32(hh, mm, nn, kk, al, a, b, be, c)
+                                           : launch_sgemm(hh, mm, nn, kk, al, a, b, be, c);
+        });
+}
+
+int b2b_dgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t k, double alpha, const double *A,
+                     size_t a_len, const double *B, size_t b_len, double beta, double *C, size_t c_len) {
+    if (algo < B2B_ALGO_DEFAULT || algo > B2B_ALGO_DOUBLE_BUF)
+        return fail(B2B_ERR_INVALID_ARG, "b2b_dgemm_simple: unknown algo " + std::to_string(algo));
+    return gemm_simple<double, double>(h, "b2b_dgemm_simple", m, n, k, alpha, A, a_len, B, b_len, beta, C, c_len,
+                                       launch_dgemm);
+}
+
+int b2b_hgemm_simple(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A, size_t a_len,
+                     const uint16_t *B, size_t b_len, float beta, uint16_t *C, size_t c_len) {
+    return gemm_simple<uint16_t, float>(h, "b2b_hgemm_simple", m, n, k, alpha, A, a_len, B, b_len, beta, C, c_len,
+                                        launch_hgemm);
+}
+
+int b2b_sgemm_strided_batched_simple(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
+                                     size_t a_len, size_t stride_a, const float *B, size_t b_len, size_t stride_b,
+                                     float beta, float *C, size_t c_len, size_t stride_c, size_t batch) {
+    const char *fn = "b2b_sgemm_strided_batched_simple";
+    if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");
+    // batched.rs:171-173: each slice must hold batch*stride elements.
+    if (a_len < batch * stride_a) return dim_err(fn, "A length (>= batch*stride_a)", batch * stride_a, a_len);
+    if (b_len < batch * stride_b) return dim_err(fn, "B length (>= batch*stride_b)", batch * stride_b, b_len);
+    if (c_len < batch * stride_c) return dim_err(fn, "C length (>= batch*stride_c)", batch * stride_c, c_len);
+    if (m == 0 || n == 0 || k == 0 || batch == 0) return B2B_OK;
+    if (!A || !B || !C) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL slice");
+    // Every batch must also fit inside its slice.
+    const size_t need_a = (batch - 1) * stride_a + m * k, need_b = (batch - 1) * stride_b + k * n,
+                 need_c = (batch - 1) * stride_c + m * n;
+    if (a_len < need_a) return dim_err(fn, "A length (last batch end)", need_a, a_len);
+    if (b_len < need_b) return dim_err(fn, "B length (last batch end)", need_b, b_len);
+    if (c_len < need_c) return dim_err(fn, "C length (last batch end)", need_c, c_len);
+    DeviceGuard g(h);
+    const size_t ea = a_len * 4, eb = b_len * 4, ec = c_len * 4;
+    const size_t ob = round_up(ea, 256), oc = ob + round_up(eb, 256);
+    void *stage = nullptr;
+    int rc = staging(h, oc + round_up(ec, 256), &stage);
+    if (rc) return rc;
+    float *dA = static_cast<float *>(stage);
+    float *dB = reinterpret_cast<float *>(static_cast<char *>(stage) + ob);
+    float *dC = reinterpret_cast<float *>(static_cast<char *>(stage) + oc);
+    // Packed outputs with beta == 0: C is write-only.  Otherwise upload it
+    // whole so elements between batches come back unchanged.
+    const bool packed = stride_c == m * n;
+    const bool up_c = beta != 0.0f || !packed;
+    if ((rc = h2d(h, dA, A, ea)) || (rc = h2d(h, dB, B, eb))) return rc;
+    if (up_c && (rc = h2d(h, dC, C, ec))) return rc;
+    rc = launch_sgemm_strided_batched(h, m, n, k, alpha, dA, stride_a, dB, stride_b, beta, dC, stride_c, batch);
+    if (rc) return rc;
+    if ((rc = d2h(h, C, dC, packed ? batch * m * n * 4 : ec))) return rc;
+    return finish(h);
+}
+
+int b2b_sgemm_batched_simple(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *const *A,
+                             const size_t *a_lens, const float *const *B, const size_t *b_lens, float beta,
+                             float *const *C, const size_t *c_lens, size_t batch) {
+    const char *fn = "b2b_sgemm_batched_simple";
+    if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");
+    if (batch && (!A || !B || !C || !a_lens || !b_lens || !c_lens))
+        return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL slice table");
+    if (m == 0 || n == 0 || k == 0 || batch == 0) return B2B_OK;
+    // batched.rs:236-238: every slice has exactly its matrix's length.
+    for (size_t b = 0; b < batch; ++b) {
+        if (a_lens[b] != m * k) return dim_err(fn, "a[b] length (m*k)", m * k, a_lens[b]);
+        if (b_lens[b] != k * n) return dim_err(fn, "b[b] length (k*n)", k * n, b_lens[b]);
+        if (c_lens[b] != m * n) return dim_err(fn, "c[b] length (m*n)", m * n, c_lens[b]);
+        if (!A[b] || !B[b] || !C[b]) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL slice");
+    }
+    DeviceGuard g(h);
+    const size_t sa = m * k, sb = k * n, sc = m * n;
+    const size_t ea = batch * sa * 4, eb = batch * sb * 4, ec = batch * sc * 4;
+    const size_t ob = round_up(ea, 256), oc = ob + round_up(eb, 256);
+    void *stage = nullptr;
+    int rc = staging(h, oc + round_up(ec, 256), &stage);
+    if (rc) return rc;
+    float *dA = static_cast<float *>(stage);
+    float *dB = reinterpret_cast<float *>(static_cast<char *>(stage) + ob);
+    float *dC = reinterpret_cast<float *>(static_cast<char *>(stage) + oc);
+    // Gather the slices straight into the strided device layout (the
+    // reference concatenates on the host first, batched.rs:228-242).
+    for (size_t b = 0; b < batch; ++b) {
+        if ((rc = h2d(h, dA + b * sa, A[b], sa * 4)) || (rc = h2d(h, dB + b * sb, B[b], sb * 4))) return rc;
+        if (beta != 0.0f && (rc = h2d(h, dC + b * sc, C[b], sc * 4))) return rc;
+    }
+    rc = launch_sgemm_strided_batched(h, m, n, k, alpha, dA, sa, dB, sb, beta, dC, sc, batch);
+    if (rc) return rc;
+    for (size_t b = 0; b < batch; ++b)
+        if ((rc = d2h(h, C[b], dC + b * sc, sc * 4))) return rc;
+    return finish(h);
+}
+
+int b2b_sgemv_simple(b2b_handle *h, int algo, int trans, size_t m, size_t n, float alpha, const float *A,
+                     size_t a_len, const float *x, size_t x_len, float beta, float *y, size_t y_len) {
+    const char *fn = "b2b_sgemv_simple";
+    if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");
+    if (algo < B2B_ALGO_DEFAULT || algo > B2B_ALGO_DOUBLE_BUF)
+        return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": unknown algo " + std::to_string(algo));
+    if (trans != B2B_OP_N && trans != B2B_OP_T)
+        return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": trans must be B2B_OP_N or B2B_OP_T");
+    // gemv.rs:279-285: A exactly m*n, x and y at least their op lengths.
+    if (a_len != m * n) return dim_err(fn, "A length (m*n)", m * n, a_len);
+    const size_t xl = trans == B2B_OP_N ? n : m, yl = trans == B2B_OP_N ? m : n;
+    if (x_len < xl) return dim_err(fn, "x length", xl, x_len);
+    if (y_len < yl) return dim_err(fn, "y length", yl, y_len);
+    if (m == 0 || n == 0) return B2B_OK;
+    if (!A || !x || !y) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL slice");
+    DeviceGuard g(h);
+    const size_t ea = m * n * 4, ex = xl * 4, ey = yl * 4;
+    const size_t ox = round_up(ea, 256), oy = ox + round_up(ex, 256);
+    void *stage = nullptr;
+    int rc = staging(h, oy + round_up(ey, 256), &stage);
+    if (rc) return rc;
+    float *dA = static_cast<float *>(stage);
+    float *dx = reinterpret_cast<float *>(static_cast<char *>(stage) + ox);
+    float *dy = reinterpret_cast<float *>(static_cast<char *>(stage) + oy);
+    if ((rc = h2d(h, dA, A, ea)) || (rc = h2d(h, dx, x, ex))) return rc;
+    if (beta != 0.0f && (rc = h2d(h, dy, y, ey))) return rc;
+    if ((rc = launch_sgemv(h, trans, m, n, alpha, dA, dx, beta, dy))) return rc;
+    if ((rc = d2h(h, y, dy, ey))) return rc;
+    return finish(h);
+}
+
+int b2b_saxpy_simple(b2b_handle *h, size_t n, float alpha, const float *x, size_t x_len, float *y, size_t y_len) {
+    const char *fn = "b2b_saxpy_simple";
+    if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");
+    if (x_len < n) return dim_err(fn, "x length (>= n)", n, x_len);  // saxpy.rs:53-54
+    if (y_len < n) return dim_err(fn, "y length (>= n)", n, y_len);
+    if (n == 0) return B2B_OK;
+    if (!x || !y) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL slice");
+    DeviceGuard g(h);
+    const size_t oy = round_up(n * 4, 256);
+    void *stage = nullptr;
+    int rc = staging(h, oy + round_up(n * 4, 256), &stage);
+    if (rc) return rc;
+    float *dx = static_cast<float *>(stage);
+    float *dy = reinterpret_cast<float *>(static_cast<char *>(stage) + oy);
+    if ((rc = h2d(h, dx, x, n * 4)) || (rc = h2d(h, dy, y, n * 4))) return rc;
+    if ((rc = launch_saxpy(h, n, alpha, dx, dy))) return rc;
+    if ((rc = d2h(h, y, dy, n * 4))) return rc;
+    return finish(h);
+}
+
+}  // extern "C"

@@ -1,0 +1,75 @@
+// internal.h -- handle layout, error plumbing and kernel-launch declarations
+// shared by the translation units of libb2blas.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "b2blas.h"
+
+// Device status word values written by kernels whose waits are bounded.
+// The low byte names the wait that gave up.
+#define B2B_DEVSTAT_TIMEOUT 0x100
+
+struct b2b_handle {
+    int device = 0;
+    int sm_count = 0;
+    int sm_clock_khz = 0;
+    cudaStream_t own_stream = nullptr;  // created by b2b_create
+    cudaStream_t stream = nullptr;      // where work is issued (own or caller's)
+    int *d_status = nullptr;            // device status word (bounded-wait timeouts)
+    // Grow-only device scratch for kernels that need it (split reductions).
+    void *workspace = nullptr;
+    size_t workspace_bytes = 0;
+    // Grow-only device staging for the host-slice calls (operands copied in).
+    void *staging = nullptr;
+    size_t staging_bytes = 0;
+    // Second stream and events for overlapping host<->device copies with
+    // compute inside the host-slice calls.
+    cudaStream_t copy_stream = nullptr;
+    // Upper bound on any single bounded device wait, in nanoseconds.
+    uint64_t wait_limit_ns = 2000000000ull;
+};
+
+namespace b2b {
+
+// Records `msg` as the calling thread's last error and returns `code`.
+int fail(int code, const std::string &msg);
+int fail_cuda(cudaError_t e, const char *what);
+
+// Makes the handle's device current for the lifetime of the guard.
+struct DeviceGuard {
+    int prev = -1;
+    bool changed = false;
+    explicit DeviceGuard(const b2b_handle *h);
+    ~DeviceGuard();
+};
+
+// Returns a device pointer to at least `bytes` of handle scratch (grown in
+// stream order on the handle's stream).
+int workspace(b2b_handle *h, size_t bytes, void **ptr);
+int staging(b2b_handle *h, size_t bytes, void **ptr);
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- kernel launchers (each returns a b2b_status) --------------------------
+int launch_sgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
+                 float beta, float *C);
+int launch_dgemm(b2b_handle *h, size_t m, size_t n, size_t k, double alpha, const double *A, const double *B,
+                 double beta, double *C);
+int launch_sgemm_strided_batched(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
+                                 size_t sa, const float *B, size_t sb, float beta, float *C, size_t sc,
+                                 size_t batch);
+int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A, const uint16_t *B,
+                 float beta, uint16_t *C);
+int launch_sgemm_3xtf32(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
+                        const float *B, float beta, float *C);
+int launch_sgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A, const float *x,
+                 float beta, float *y);
+int launch_saxpy(b2b_handle *h, size_t n, float alpha, const float *x, float *y);
+int launch_panels_to_rowmajor(b2b_handle *h, size_t elem_bytes, size_t m, size_t g, const size_t *widths,
+                              const void *panels, void *C);
+
+}  // namespace b2b

@@ -1,0 +1,1 @@
+"""CPU oracle package (test infrastructure only; see oracle.c)."""

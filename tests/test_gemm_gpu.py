@@ -1,0 +1,233 @@
+"""SGEMM / DGEMM / strided-batched / batched parity on the GPU, through the C
+ABI, against the CPU oracle.  Tolerance: normwise relative error
+||C - C*||_F / ||C*||_F <= 4*K*eps(dtype) against the FP64 evaluation."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+VARIANTS = ["naive", "tiled", "vectorized", "double_buf"]
+
+
+def _cfg(m, n, k, alpha, beta):
+    import b2blas
+
+    return b2blas.GemmConfig(m, n, k, alpha, beta)
+
+
+def _gemm_dev(handle, op, variant, cfg, A, B, C):
+    a, b, c = handle.upload(A), handle.upload(B), handle.upload(C)
+    getattr(handle, f"{op}_{variant}" if variant else op)(cfg, a, b, c)
+    handle.synchronize()
+    return handle.download(c)
+
+
+# ------------------------------------------------------------ known answers
+
+@pytest.mark.parametrize("case", [c for c in load_golden("known_answers.json")["cases"]
+                                  if c["op"] in ("sgemm", "dgemm")], ids=lambda c: f"{c['op']}-{c['m']}")
+def test_known_answer_all_variants(handle, case):
+    dt = np.float32 if case["op"] == "sgemm" else np.float64
+    m, n, k = case["m"], case["n"], case["k"]
+    cfg = _cfg(m, n, k, case["alpha"], case["beta"])
+    for v in case["variants"]:
+        # host-slice flavour, as the reference example calls it
+        c = np.zeros(m * n, dt)
+        getattr(handle, f"{case['op']}_{v}_simple")(cfg, np.ones(m * k, dt), np.ones(k * n, dt), c)
+        assert np.max(np.abs(c - case["expect"])) <= case["tol_abs"], v
+        # device-buffer flavour, as gemm_bench calls it
+        c2 = _gemm_dev(handle, case["op"], v, cfg, np.ones(m * k, dt), np.ones(k * n, dt), np.zeros(m * n, dt))
+        assert np.max(np.abs(c2 - case["expect"])) <= case["tol_abs"], v
+
+
+def test_known_answer_strided_and_batched(handle):
+    import b2blas
+
+    for case in load_golden("known_answers.json")["cases"]:
+        if case["op"] not in ("strided_batched_sgemm", "batched_sgemm"):
+            continue
+        b, m, n, k = case["batch"], case["m"], case["n"], case["k"]
+        cfg = b2blas.GemmConfig(m, n, k, 1.0, 0.0)
+        if case["op"] == "strided_batched_sgemm":
+            c = np.zeros(b * m * n, np.float32)
+            handle.strided_batched_sgemm_simple(cfg, b, np.ones(b * m * k, np.float32), m * k,
+                                                np.ones(b * k * n, np.float32), k * n, c, m * n)
+            assert np.max(np.abs(c - case["expect"])) <= case["tol_abs"]
+        else:
+            cs = [np.zeros(m * n, np.float32) for _ in range(b)]
+            handle.batched_sgemm(cfg, b, [np.ones(m * k, np.float32)] * b, [np.ones(k * n, np.float32)] * b, cs)
+            assert max(np.max(np.abs(x - case["expect"])) for x in cs) <= case["tol_abs"]
+
+
+# --------------------------------------------------------- random parity
+
+SHAPES = [(512, 512, 512), (1, 1, 1), (15, 17, 33), (129, 257, 65), (300, 200, 100), (128, 128, 8), (64, 96, 1000),
+          (1000, 8, 16), (7, 1023, 9)]
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("alpha,beta", [(1.0, 0.0), (1.5, 0.5), (-0.75, 2.0)])
+def test_sgemm_random_parity(handle, oracle, m, n, k, alpha, beta):
+    A = oracle.uniform_f32(m * k, 42, 1)
+    B = oracle.uniform_f32(k * n, 42, 2)
+    C = oracle.uniform_f32(m * n, 42, 3)
+    ref = oracle.sgemm_f64(m, n, k, alpha, A, B, beta, C)
+    got = _gemm_dev(handle, "sgemm", None, _cfg(m, n, k, alpha, beta), A, B, C)
+    assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f32")
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("alpha,beta", [(1.0, 0.0), (1.5, 0.5)])
+def test_dgemm_random_parity(handle, oracle, m, n, k, alpha, beta):
+    A = oracle.uniform_f64(m * k, 42, 1)
+    B = oracle.uniform_f64(k * n, 42, 2)
+    C = oracle.uniform_f64(m * n, 42, 3)
+    ref = oracle.dgemm_f64(m, n, k, alpha, A, B, beta, C)
+    got = _gemm_dev(handle, "dgemm", None, _cfg(m, n, k, alpha, beta), A, B, C)
+    assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f64")
+
+
+def test_sgemm_unaligned_pointers_take_scalar_path(handle, oracle):
+    # Operands that start one element past a 16-byte boundary must still be
+    # correct (the vector path needs 16-byte alignment).
+    import b2blas
+
+    m, n, k = 70, 90, 50
+    A = oracle.uniform_f32(m * k + 1, 5, 1)
+    B = oracle.uniform_f32(k * n + 1, 5, 2)
+    C = oracle.uniform_f32(m * n + 1, 5, 3)
+    a, b, c = handle.upload(A), handle.upload(B), handle.upload(C)
+    av = b2blas.DeviceBuffer.from_ptr(handle, a.ptr + 4, m * k, np.float32)
+    bv = b2blas.DeviceBuffer.from_ptr(handle, b.ptr + 4, k * n, np.float32)
+    cv = b2blas.DeviceBuffer.from_ptr(handle, c.ptr + 4, m * n, np.float32)
+    handle.sgemm(_cfg(m, n, k, 1.25, -0.5), av, bv, cv)
+    handle.synchronize()
+    got = handle.download(c)[1:]
+    ref = oracle.sgemm_f64(m, n, k, 1.25, A[1:], B[1:], -0.5, C[1:])
+    assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f32")
+
+
+def test_beta_zero_does_not_read_c(handle, oracle):
+    # beta == 0: C is write-only, so NaN in C does not propagate.
+    m, n, k = 64, 64, 64
+    A = oracle.uniform_f32(m * k, 1, 1)
+    B = oracle.uniform_f32(k * n, 1, 2)
+    C = np.full(m * n, np.nan, np.float32)
+    got = _gemm_dev(handle, "sgemm", None, _cfg(m, n, k, 1.0, 0.0), A, B, C)
+    assert np.all(np.isfinite(got))
+
+
+def test_zero_dims_leave_c_untouched(handle):
+    c = handle.upload(np.full(16, 7.0, np.float32))
+    z = handle.upload(np.zeros(16, np.float32))
+    handle.sgemm(_cfg(4, 4, 0, 1.0, 0.0), z, z, c)
+    handle.synchronize()
+    assert np.all(handle.download(c) == 7.0)
+
+
+def test_simple_equals_device_flavour_bitwise(handle, oracle):
+    m, n, k = 200, 160, 96
+    A = oracle.uniform_f32(m * k, 9, 1)
+    B = oracle.uniform_f32(k * n, 9, 2)
+    C = oracle.uniform_f32(m * n, 9, 3)
+    cfg = _cfg(m, n, k, 1.5, 0.5)
+    dev = _gemm_dev(handle, "sgemm", None, cfg, A, B, C)
+    host = C.copy()
+    handle.sgemm_simple(cfg, A, B, host)
+    assert np.array_equal(dev, host)
+
+
+def test_sgemm_8192_full_size_sampled(handle, oracle):
+    # The 8192^3 configuration (alpha 1.5, beta 0.5): sampled rows against the
+    # FP64 oracle, plus a column check C[:, j] against A @ B[:, j].
+    import b2blas
+
+    m = n = k = 8192
+    A = oracle.uniform_f32(m * k, 42, 1)
+    B = oracle.uniform_f32(k * n, 42, 2)
+    C = oracle.uniform_f32(m * n, 42, 3)
+    got = _gemm_dev(handle, "sgemm", None, b2blas.GemmConfig(m, n, k, 1.5, 0.5), A, B, C).reshape(m, n)
+    tol = oracle.tol_normwise(k, "f32")
+    for r in (0, 1, 4095, 8191):
+        ref = oracle.sgemm_f64(m, n, k, 1.5, A, B, 0.5, C, row0=r, nrows=1)
+        assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= tol, r
+    A2 = A.reshape(m, k).astype(np.float64)
+    for j in (0, 777, 8191):
+        ref = 1.5 * (A2 @ B.reshape(k, n)[:, j].astype(np.float64)) + 0.5 * C.reshape(m, n)[:, j]
+        assert oracle.rel_err(np.ascontiguousarray(got[:, j]), ref) <= tol, j
+
+
+def test_dgemm_4096_full_size_sampled(handle, oracle):
+    import b2blas
+
+    m = n = k = 4096
+    A = oracle.uniform_f64(m * k, 42, 1)
+    B = oracle.uniform_f64(k * n, 42, 2)
+    C = oracle.uniform_f64(m * n, 42, 3)
+    got = _gemm_dev(handle, "dgemm", None, b2blas.GemmConfig(m, n, k, 1.5, 0.5), A, B, C).reshape(m, n)
+    for r in (0, 2049, 4095):
+        ref = oracle.dgemm_f64(m, n, k, 1.5, A, B, 0.5, C, row0=r, nrows=1)
+        assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= oracle.tol_normwise(k, "f64"), r
+
+
+# ------------------------------------------------------- batched family
+
+@pytest.mark.parametrize("batch,m,n,k,gap", [(8, 64, 64, 64, 0), (33, 17, 29, 13, 3), (4, 256, 256, 256, 0),
+                                             (70000, 2, 3, 4, 1)])
+def test_strided_batched_parity(handle, oracle, batch, m, n, k, gap):
+    import b2blas
+
+    sa, sb, sc = m * k + gap, k * n + 2 * gap, m * n + gap
+    A = oracle.uniform_f32(batch * sa, 11, 1)
+    B = oracle.uniform_f32(batch * sb, 11, 2)
+    C = oracle.uniform_f32(batch * sc, 11, 3)
+    cfg = b2blas.GemmConfig(m, n, k, 0.75, 0.25)
+    ref = oracle.sgemm_strided_batched_f64(m, n, k, 0.75, A, sa, B, sb, 0.25, C, sc, batch)
+    a, b, c = handle.upload(A), handle.upload(B), handle.upload(C)
+    handle.strided_batched_sgemm(cfg, batch, a, sa, b, sb, c, sc)
+    handle.synchronize()
+    got = handle.download(c)
+    gotp = np.concatenate([got[i * sc:i * sc + m * n] for i in range(batch)]) if gap else got
+    assert oracle.rel_err(gotp, ref) <= oracle.tol_normwise(k, "f32")
+    if gap:  # elements between batches are untouched
+        for i in range(min(batch, 50)):
+            assert np.array_equal(got[i * sc + m * n:(i + 1) * sc], C[i * sc + m * n:(i + 1) * sc])
+    # the host-slice flavour gives the same bits
+    host = C.copy()
+    handle.strided_batched_sgemm_simple(cfg, batch, A, sa, B, sb, host, sc)
+    assert np.array_equal(host, got)
+
+
+def test_strided_batched_4096x256_sampled(handle, oracle):
+    import b2blas
+
+    batch, m = 4096, 256
+    A = oracle.uniform_f32(batch * m * m, 42, 1)
+    B = oracle.uniform_f32(batch * m * m, 42, 2)
+    a, b = handle.upload(A), handle.upload(B)
+    c = handle.zeroed(batch * m * m)
+    handle.strided_batched_sgemm(b2blas.GemmConfig(m, m, m, 1.0, 0.0), batch, a, m * m, b, m * m, c, m * m)
+    handle.synchronize()
+    got = handle.download(c)
+    for bi in (0, 1, 2047, 4095):
+        s = bi * m * m
+        ref = oracle.sgemm_f64(m, m, m, 1.0, A[s:s + m * m], B[s:s + m * m])
+        assert oracle.rel_err(got[s:s + m * m], ref) <= oracle.tol_normwise(m, "f32"), bi
+
+
+def test_batched_sgemm_list_api(handle, oracle):
+    import b2blas
+
+    batch, m, n, k = 5, 31, 40, 23
+    As = [oracle.uniform_f32(m * k, 20 + i, 1) for i in range(batch)]
+    Bs = [oracle.uniform_f32(k * n, 20 + i, 2) for i in range(batch)]
+    Cs = [oracle.uniform_f32(m * n, 20 + i, 3) for i in range(batch)]
+    refs = [oracle.sgemm_f64(m, n, k, 2.0, As[i], Bs[i], -1.0, Cs[i]) for i in range(batch)]
+    outs = [c.copy() for c in Cs]
+    handle.batched_sgemm(b2blas.GemmConfig(m, n, k, 2.0, -1.0), batch, As, Bs, outs)
+    for o, r in zip(outs, refs):
+        assert oracle.rel_err(o, r) <= oracle.tol_normwise(k, "f32")

@@ -1,0 +1,107 @@
+"""HGEMM parity on the GPU (tcgen05 path and the generic path), through the C
+ABI, against the CPU oracle.  Tolerance: 2e-2 normwise relative error
+against the FP64 evaluation of the exact f16 inputs (FP16 in / FP32
+accumulate); the reference's own truncating arithmetic is checked to the
+same bound."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+def _run(handle, m, n, k, alpha, beta, A, B, C):
+    import b2blas
+
+    a, b, c = handle.upload(A), handle.upload(B), handle.upload(C)
+    handle.hgemm(b2blas.GemmConfig(m, n, k, alpha, beta), a, b, c)
+    handle.synchronize()
+    return handle.download(c)
+
+
+def test_known_answer_128(handle):
+    import b2blas
+
+    m = n = k = 128
+    c = np.zeros(m * n, np.float16)
+    handle.hgemm_half(b2blas.GemmConfig(m, n, k, 1.0, 0.0), np.ones(m * k, np.float16), np.ones(k * n, np.float16), c)
+    assert np.max(np.abs(c.astype(np.float64) - 128.0) / 128.0) <= 5e-3
+    c2 = np.zeros(m * n, np.float16)
+    handle.hgemm_tensor_core(b2blas.GemmConfig(m, n, k, 1.0, 0.0), np.ones(m * k, np.float16),
+                             np.ones(k * n, np.float16), c2)
+    assert np.array_equal(c, c2)
+
+
+# tcgen05-eligible (K, N multiples of 8) and generic-path shapes
+SHAPES = [(128, 256, 64), (256, 512, 192), (128, 256, 8), (200, 264, 72), (1, 8, 8), (130, 300, 1000),
+          (512, 512, 512), (1024, 768, 4096), (37, 41, 43), (64, 100, 7)]
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("alpha,beta", [(1.0, 0.0), (0.5, -1.5)])
+def test_hgemm_random_parity(handle, oracle, m, n, k, alpha, beta):
+    A = oracle.normal_f16(m * k, 42, 1, 0.0, 0.1)
+    B = oracle.normal_f16(k * n, 42, 2, 0.0, 0.1)
+    C = oracle.normal_f16(m * n, 42, 3, 0.0, 0.1)
+    ref = oracle.hgemm_f64(m, n, k, alpha, A, B, beta, C)
+    got = _run(handle, m, n, k, alpha, beta, A, B, C)
+    err = oracle.rel_err(got, ref)
+    assert err <= TOL, err
+    # f32 accumulation + one f16 rounding: far inside the bound in practice.
+    assert err <= 2e-3, err
+
+
+def test_hgemm_matches_reference_arithmetic(handle, oracle):
+    # Against the reference's own scalar arithmetic (flush + truncation):
+    # within the tolerance, and within 1 f16 ulp-ish everywhere.
+    m, n, k = 96, 128, 256
+    A = oracle.normal_f16(m * k, 3, 1, 0.0, 0.1)
+    B = oracle.normal_f16(k * n, 3, 2, 0.0, 0.1)
+    C = np.zeros(m * n, np.uint16)
+    refc = oracle.hgemm_ref(m, n, k, 1.0, A, B, 0.0, C)
+    got = _run(handle, m, n, k, 1.0, 0.0, A, B, C)
+    ref64 = refc.view(np.float16).astype(np.float64)
+    assert oracle.rel_err(got, ref64) <= TOL
+
+
+def test_hgemm_8192_full_size_sampled(handle, oracle):
+    # The 8192^3 configuration: rows and columns sampled against FP64.
+    m = n = k = 8192
+    A = oracle.normal_f16(m * k, 42, 1, 0.0, 0.1)
+    B = oracle.normal_f16(k * n, 42, 2, 0.0, 0.1)
+    got = _run(handle, m, n, k, 1.0, 0.0, A, B, np.zeros(m * n, np.uint16)).reshape(m, n)
+    for r in (0, 127, 128, 4000, 8191):
+        ref = oracle.hgemm_f64(m, n, k, 1.0, A, B, row0=r, nrows=1)
+        assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= TOL, r
+    A32 = A.view(np.float16).astype(np.float32).reshape(m, k)
+    B16 = B.view(np.float16).reshape(k, n)
+    for j in (0, 255, 256, 5000, 8191):
+        ref = A32.astype(np.float64) @ B16[:, j].astype(np.float64)
+        assert oracle.rel_err(np.ascontiguousarray(got[:, j]), ref) <= TOL, j
+    # the whole output is finite and not trivially zero
+    g = got.view(np.float16)
+    assert np.all(np.isfinite(g)) and np.count_nonzero(g) > 0.99 * g.size
+
+
+def test_hgemm_repeatable_bitwise(handle, oracle):
+    m, n, k = 384, 512, 320
+    A = oracle.normal_f16(m * k, 8, 1, 0.0, 0.1)
+    B = oracle.normal_f16(k * n, 8, 2, 0.0, 0.1)
+    C = np.zeros(m * n, np.uint16)
+    g1 = _run(handle, m, n, k, 1.0, 0.0, A, B, C)
+    g2 = _run(handle, m, n, k, 1.0, 0.0, A, B, C)
+    assert np.array_equal(g1, g2)
+
+
+def test_hgemm_simple_equals_device(handle, oracle):
+    import b2blas
+
+    m, n, k = 2048, 1024, 512  # large enough for the pipelined host-slice path
+    A = oracle.normal_f16(m * k, 4, 1, 0.0, 0.1)
+    B = oracle.normal_f16(k * n, 4, 2, 0.0, 0.1)
+    C = oracle.normal_f16(m * n, 4, 3, 0.0, 0.1)
+    dev = _run(handle, m, n, k, 1.0, 0.5, A, B, C)
+    host = C.copy()
+    handle.hgemm_simple(b2blas.GemmConfig(m, n, k, 1.0, 0.5), A, B, host)
+    assert np.array_equal(dev, host)

@@ -78,7 +78,7 @@ _REASONS = [
 class ClockSampler:
     """Polls NVML (SM clock, event reasons) every few ms while running."""
 
-    def __init__(self, cuda_index: int, period_s: float = 0.005):
+    def __init__(self, cuda_index: int, period_s: float = 0.002):
         self.samples = []
         self.max_mhz = None
         self.ok = False
@@ -553,12 +553,18 @@ class MlpWorkload(Workload):
 
 
 def make_workload(name, h, rank, world, args):
+    def dims(d):
+        return (args.m or d, args.n or d, args.k or d)
+
     if name == "hgemm":
-        return GemmWorkload(h, rank, world, args, "hgemm", 8192, 8192, 8192, 1.0, 0.0, weak=True)
+        m, n, k = dims(8192)
+        return GemmWorkload(h, rank, world, args, "hgemm", m, n, k, 1.0, 0.0, weak=True)
     if name == "sgemm":
-        return GemmWorkload(h, rank, world, args, "sgemm", 8192, 8192, 8192, 1.5, 0.5, weak=False)
+        m, n, k = dims(8192)
+        return GemmWorkload(h, rank, world, args, "sgemm", m, n, k, 1.5, 0.5, weak=False)
     if name == "dgemm":
-        return GemmWorkload(h, rank, world, args, "dgemm", 4096, 4096, 4096, 1.5, 0.5, weak=False)
+        m, n, k = dims(4096)
+        return GemmWorkload(h, rank, world, args, "dgemm", m, n, k, 1.5, 0.5, weak=False)
     if name == "batched":
         return BatchedWorkload(h, rank, world, args)
     if name == "sgemv":
@@ -714,18 +720,43 @@ def run_reference(args, rank, world):
     return 0
 
 
+def run_e2e(w, h, stream, steps, world, dist, barrier):
+    """The same metric through the host-slice API: page-locked host inputs
+    copied in and the result copied out inside every timed step."""
+    import torch
+
+    h2d, d2h = w.e2e_setup()
+    w.e2e_step()  # warm (staging allocation)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        w.e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    value = w.scale(w.units_per_step() * world * steps / (float(t.item()) / 1e3))
+    return {"value": value, "unit": w.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "api": "host-slice (_simple) calls on page-locked host buffers"}
+
+
 # ------------------------------------------------------------------ main
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b2blas", "reference"], default="b2blas")
     ap.add_argument("--workload", choices=["hgemm", "sgemm", "dgemm", "batched", "sgemv", "mlp"], default="hgemm")
     ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
     ap.add_argument("--gather", action="store_true", help="column-sharded GEMMs: all-gather C every step")
-    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--e2e-steps", type=int, default=None, help="0 skips the end-to-end pass")
+    ap.add_argument("--m", type=int, default=None, help="GEMM size override (profiling small cases)")
+    ap.add_argument("--n", type=int, default=None)
+    ap.add_argument("--k", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
@@ -753,7 +784,10 @@ def main():
     import b2blas
 
     h = b2blas.Handle(local)
-    stream = torch.cuda.current_stream()
+    # One dedicated stream for torch and the library: the CUDA events that
+    # time the steps are recorded on the stream the kernels are launched on.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     h.set_stream(stream.cuda_stream)
     w = make_workload(args.workload, h, rank, world, args)
     torch.cuda.synchronize()
@@ -821,22 +855,9 @@ def main():
 
     # end to end through the host-slice API
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(3, min(args.steps, 10))
-    h2d, d2h = w.e2e_setup()
-    w.e2e_step()  # warm (staging allocation)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        w.e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = w.scale(w.units_per_step() * world * e2e_steps / (float(t.item()) / 1e3))
-    e2e = {"value": e2e_value, "unit": w.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-           "steps": e2e_steps, "api": "host-slice (_simple) calls on page-locked host buffers"}
+    e2e = None
+    if e2e_steps > 0:
+        e2e = run_e2e(w, h, stream, e2e_steps, world, dist, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

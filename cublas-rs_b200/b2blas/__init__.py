@@ -223,8 +223,16 @@ class Handle:
         return s.value or 0
 
     def set_stream(self, stream: int | None) -> None:
-        """Issue subsequent work on a caller-owned cudaStream_t (None = own)."""
-        _check(self._lib.b2b_set_stream(self._h, ctypes.c_void_p(stream or 0)))
+        """Issue subsequent work on a caller-owned cudaStream_t.  None selects
+        the handle's own stream; 0 (what torch reports for its default
+        stream) selects the legacy default stream."""
+        if stream is None:
+            ptr = 0
+        elif int(stream) == 0:
+            ptr = 1  # cudaStreamLegacy
+        else:
+            ptr = int(stream)
+        _check(self._lib.b2b_set_stream(self._h, ctypes.c_void_p(ptr)))
 
     def synchronize(self) -> None:
         _check(self._lib.b2b_synchronize(self._h))

@@ -79,9 +79,10 @@ B2B_API int b2b_create(int device, b2b_handle **out);
 B2B_API int b2b_destroy(b2b_handle *h);
 /* Handle::stream (lib.rs:72-74).  Returns the cudaStream_t as void*. */
 B2B_API int b2b_get_stream(b2b_handle *h, void **stream);
-/* Run subsequent calls on a caller-owned cudaStream_t (NULL = the handle's
- * own stream).  No reference counterpart; the cuBLAS equivalent is
- * cublasSetStream.  Used to share a stream with torch / NCCL. */
+/* Run subsequent calls on a caller-owned cudaStream_t.  NULL selects the
+ * handle's own stream again; the legacy default stream is selected with
+ * cudaStreamLegacy ((void *)0x1).  No reference counterpart; the cuBLAS
+ * equivalent is cublasSetStream.  Used to share a stream with torch / NCCL. */
 B2B_API int b2b_set_stream(b2b_handle *h, void *stream);
 /* Handle::synchronize (lib.rs:79-82): blocks on the stream, then reports a
  * device-side bounded-wait timeout, if one was recorded, as

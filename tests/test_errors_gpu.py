@@ -92,6 +92,9 @@ def test_set_stream_roundtrip(handle):
     assert handle.stream() == s.cuda_stream
     handle.set_stream(None)
     assert handle.stream() == own
+    handle.set_stream(0)  # torch's default stream -> the legacy default stream
+    assert handle.stream() == 1
+    handle.set_stream(None)
 
 
 def test_device_info(handle):

@@ -51,6 +51,7 @@ SIGNATURES = {
     "b2b_sgemm_batched_simple": (_i, [_vp, _sz, _sz, _sz, _f, _vpp, _szp, _vpp, _szp, _f, _vpp, _szp, _sz]),
     "b2b_sgemv": (_i, [_vp, _i, _i, _sz, _sz, _f, _vp, _vp, _f, _vp]),
     "b2b_sgemv_simple": (_i, [_vp, _i, _i, _sz, _sz, _f, _vp, _sz, _vp, _sz, _f, _vp, _sz]),
+    "b2b_sgemv_noalloc": (_i, [_vp, _i, _sz, _sz, _f, _vp, _vp, _f, _vp]),
     "b2b_saxpy": (_i, [_vp, _sz, _f, _vp, _vp]),
     "b2b_saxpy_simple": (_i, [_vp, _sz, _f, _vp, _sz, _vp, _sz]),
     "b2b_panels_to_rowmajor": (_i, [_vp, _sz, _sz, _sz, _szp, _vp, _vp]),

@@ -20,6 +20,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <string>
+
 #include "internal.h"
 
 namespace {
@@ -242,3 +245,102 @@ int launch_sgemv(b2b_handle *h, int trans, size_t m_, size_t n_, float alpha, co
 }
 
 }  // namespace b2b
+
+// ---------------------------------------------------------------------------
+// b2b_sgemv_noalloc: SGEMV whose split-row partials live in a fixed device
+// array instead of handle workspace, for callers that must not allocate
+// device memory (see the declaration in b2blas.h).
+//
+// The array below is file-scope device memory of kNoAllocScratchFloats
+// floats (1 MiB); every GPU that loads this library holds it until the
+// process exits.  Every call shares it and it keeps the last call's
+// contents.  Nothing in it has to start at zero: pass 1 writes every
+// (slice, column) partial before pass 2 reads it.  Calls that overlap on the
+// GPU (two streams, or two handles, at once) race on it.
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 18;
+static __device__ __align__(256) float g_sgemv_noalloc_scratch[kNoAllocScratchFloats];
+
+// Host code cannot use the array's name as a device address, so the address
+// is looked up once per device (with that device current) and cached.
+constexpr int kNoAllocMaxDevices = 64;
+float *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(int device, float **out) {
+    if (device < 0 || device >= kNoAllocMaxDevices)
+        return b2b::fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_sgemv_noalloc_scratch);
+        if (e != cudaSuccess) return b2b::fail_cuda(e, "b2b_sgemv_noalloc: cudaGetSymbolAddress");
+        g_noalloc_ptr[device] = static_cast<float *>(p);
+    }
+    *out = g_noalloc_ptr[device];
+    return B2B_OK;
+}
+
+}  // namespace
+
+extern "C" int b2b_sgemv_noalloc(b2b_handle *h, int trans, size_t m_, size_t n_, float alpha, const float *A,
+                                 const float *x, float beta, float *y) {
+    using namespace b2b;
+    if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: NULL handle");
+    if (trans != B2B_OP_N && trans != B2B_OP_T)
+        return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: trans must be B2B_OP_N or B2B_OP_T");
+    if (m_ == 0 || n_ == 0) return B2B_OK;
+    if (!A || !x || !y) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: NULL operand");
+    if (m_ > (size_t(1) << 62) / n_) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: sizes overflow");
+    DeviceGuard g(h);
+    const int64_t m = static_cast<int64_t>(m_), n = static_cast<int64_t>(n_);
+    cudaError_t e;
+    if (trans == B2B_OP_N) {  // the N kernel needs no scratch
+        const int64_t blocks = (m + kWarps - 1) / kWarps;
+        if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: m too large");
+        if ((n % 4 == 0) && aligned16(A) && aligned16(x))
+            sgemv_n_kernel<8, true><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
+        else
+            sgemv_n_kernel<8, false><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
+        e = cudaGetLastError();
+        return e == cudaSuccess ? B2B_OK : fail_cuda(e, "b2b_sgemv_noalloc: N launch");
+    }
+    // T: the same slicing as b2b_sgemv, so both give the same bits.
+    const bool vec_t = (n % 4 == 0) && aligned16(A);
+    const int64_t col_blocks = (n + 127) / 128;
+    if (col_blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: n too large");
+    int64_t slices = (4LL * h->sm_count + col_blocks - 1) / col_blocks;
+    const int64_t max_slices = (m + 63) / 64;
+    if (slices > max_slices) slices = max_slices;
+    if (slices > 65535) slices = 65535;
+    if (slices < 1) slices = 1;
+    const int64_t rows_per = (m + slices - 1) / slices;
+    slices = (m + rows_per - 1) / rows_per;
+    if (slices == 1) {
+        dim3 grid((unsigned)col_blocks, 1);
+        if (vec_t)
+            sgemv_t_partial_kernel<true, true><<<grid, kThreads, 0, h->stream>>>(A, x, y, m, n, rows_per, alpha, beta);
+        else
+            sgemv_t_partial_kernel<false, true><<<grid, kThreads, 0, h->stream>>>(A, x, y, m, n, rows_per, alpha, beta);
+        e = cudaGetLastError();
+        return e == cudaSuccess ? B2B_OK : fail_cuda(e, "b2b_sgemv_noalloc: T launch");
+    }
+    if (static_cast<uint64_t>(slices) * static_cast<uint64_t>(n) > kNoAllocScratchFloats)
+        return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: this shape needs " + std::to_string(slices) + " x " +
+                                             std::to_string(n) + " partial sums, more than the " +
+                                             std::to_string(kNoAllocScratchFloats) +
+                                             "-float fixed scratch holds; use b2b_sgemv");
+    float *partial = nullptr;
+    if (int rc = noalloc_scratch(h->device, &partial)) return rc;
+    dim3 grid((unsigned)col_blocks, (unsigned)slices);
+    if (vec_t)
+        sgemv_t_partial_kernel<true, false><<<grid, kThreads, 0, h->stream>>>(A, x, partial, m, n, rows_per, alpha, beta);
+    else
+        sgemv_t_partial_kernel<false, false><<<grid, kThreads, 0, h->stream>>>(A, x, partial, m, n, rows_per, alpha, beta);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "b2b_sgemv_noalloc: T partial launch");
+    sgemv_t_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, h->stream>>>(partial, y, n, (int)slices, alpha, beta);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "b2b_sgemv_noalloc: T reduce launch");
+}

@@ -184,6 +184,26 @@ B2B_API int b2b_sgemv(b2b_handle *h, int algo, int trans, size_t m, size_t n, fl
 B2B_API int b2b_sgemv_simple(b2b_handle *h, int algo, int trans, size_t m, size_t n, float alpha, const float *A,
                              size_t a_len, const float *x, size_t x_len, float beta, float *y, size_t y_len);
 
+/* SGEMV that allocates no device memory.  No counterpart in the reference.
+ * Some callers cannot call cudaMalloc or cudaFree: a process whose device
+ * memory is already reserved by another allocator (a framework's caching
+ * pool), a service with a fixed memory budget set at start-up, or a loop
+ * that must not stall on the device-wide synchronisation cudaFree implies.
+ * b2b_sgemv's transposed path keeps its split-row partial sums in handle
+ * workspace, which it grows with cudaMallocAsync; this variant keeps them in
+ * a fixed 1 MiB device array built into the library (held by every GPU that
+ * loads it until the process exits).  Same arguments and results as b2b_sgemv.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - All calls share the array, which keeps the last call's contents;
+ *     nothing in it needs clearing (every partial is written before it is
+ *     read), but calls that overlap on the GPU race on it.
+ *   - A shape whose partial sums do not fit the array is rejected with
+ *     B2B_ERR_INVALID_ARG and a message naming the sizes. */
+B2B_API int b2b_sgemv_noalloc(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A,
+                              const float *x, float beta, float *y);
+
 /* -------------------------------------------------------- Level 1: SAXPY */
 
 /* Handle::saxpy (lib.rs:110-118) -> crates/cublas-l1/src/saxpy.rs:25-40:

@@ -141,6 +141,8 @@ int b2b_create(int device, b2b_handle **out) {
         long v = atol(lim);
         if (v > 0) h->wait_limit_ns = static_cast<uint64_t>(v) * 1000000ull;
     }
+    const char *single = getenv("B2B_HGEMM_SINGLE_CTA");
+    h->force_single_cta = single && single[0] == '1';
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
     *out = h;
     return B2B_OK;

@@ -82,6 +82,57 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
     tn = r / gm;
 }
 
+// Writes 32 consecutive f16 outputs of one row (alpha already applied to v):
+// 4 x 16-byte stores when the whole chunk is in range, else element-wise.
+__device__ __forceinline__ void store_c_chunk(uint16_t *crow, int col0, int N, float (&v)[32], bool read_c,
+                                              float beta) {
+    if (col0 + 32 <= N) {
+        uint4 *dst = reinterpret_cast<uint4 *>(crow + col0);
+        if (read_c) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint4 old = dst[j];
+                const __half2 *oh = reinterpret_cast<const __half2 *>(&old);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float2 of = __half22float2(oh[e]);
+                    v[j * 8 + e * 2 + 0] = fmaf(beta, of.x, v[j * 8 + e * 2 + 0]);
+                    v[j * 8 + e * 2 + 1] = fmaf(beta, of.y, v[j * 8 + e * 2 + 1]);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint4 o;
+            __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(v[j * 8 + e * 2], v[j * 8 + e * 2 + 1]);
+            dst[j] = o;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (col0 + i < N) {
+                float x = v[i];
+                if (read_c) x = fmaf(beta, __half2float(__ushort_as_half(crow[col0 + i])), x);
+                crow[col0 + i] = __half_as_ushort(__float2half_rn(x));
+            }
+        }
+    }
+}
+
+// Grouped raster over a tiles_m x tiles_n grid: `group` consecutive M tiles
+// sweep the N tiles together, so their A and B panels stay in L2.
+__device__ __forceinline__ void tile_coords_g(int t, int tiles_m, int tiles_n, int group, int &tm, int &tn) {
+    const int span = group * tiles_n;
+    const int g = t / span;
+    const int first = g * group;
+    const int gm = min(tiles_m - first, group);
+    const int r = t - g * span;
+    tm = first + r % gm;
+    tn = r / gm;
+}
+
 __global__ void __launch_bounds__(hg::THREADS, 1)
     hgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     HgemmArgs args) {
@@ -252,7 +303,7 @@ __global__ void __launch_bounds__(hg::THREADS, 1)
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int tm, tn;
             tile_coords(t, tiles_m, tiles_n, tm, tn);
-            bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 4, args.wait_ns);
+            bool ok = mbar_wait_sleepy(&tfull[acc], acc_phase, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 4, args.wait_ns);
             // tcgen05.ld is warp-collective: all lanes take the same branch.
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
@@ -275,39 +326,7 @@ __global__ void __launch_bounds__(hg::THREADS, 1)
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = args.alpha * __uint_as_float(r[i]);
-                if (col0 + 32 <= args.N) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(crow + col0);
-                    if (read_c) {
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            uint4 old = dst[j];
-                            const __half2 *oh = reinterpret_cast<const __half2 *>(&old);
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                float2 of = __half22float2(oh[e]);
-                                v[j * 8 + e * 2 + 0] = fmaf(args.beta, of.x, v[j * 8 + e * 2 + 0]);
-                                v[j * 8 + e * 2 + 1] = fmaf(args.beta, of.y, v[j * 8 + e * 2 + 1]);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint4 o;
-                        __half2 *oh = reinterpret_cast<__half2 *>(&o);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(v[j * 8 + e * 2], v[j * 8 + e * 2 + 1]);
-                        dst[j] = o;
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        if (col0 + i < args.N) {
-                            float x = v[i];
-                            if (read_c) x = fmaf(args.beta, __half2float(__ushort_as_half(crow[col0 + i])), x);
-                            crow[col0 + i] = __half_as_ushort(__float2half_rn(x));
-                        }
-                    }
-                }
+                store_c_chunk(crow, col0, args.N, v, read_c, args.beta);
             }
             if (++acc == 2) {
                 acc = 0;
@@ -321,6 +340,264 @@ __global__ void __launch_bounds__(hg::THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, hg::TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=16).  CTA r of the pair holds
+// rows [128r, 128r+128) of the A tile and columns [128r, 128r+128) of the B
+// tile in its own shared memory, and its 128 x 256 slice of the accumulator
+// in its own TMEM.  Per CTA and 64-wide k-block that is 32 KiB of operands
+// for 128x256x64 MACs (the single-CTA kernel moves 48 KiB for the same
+// work), which is what relieves the L2 -> SM operand traffic.
+//   * Both CTAs' TMA loads (.cta_group::2, no multicast) count their bytes on
+//     the leader's (rank 0) "full" barrier, which expects 64 KiB per stage.
+//   * The leader's single MMA thread issues every MMA of the pair and commits
+//     to both CTAs' "empty" / "tmem full" barriers.
+//   * The leader's "tmem empty" barriers count one arrival per epilogue warp
+//     of both CTAs (8); the partner's warps arrive remotely.
+namespace hg2 {
+constexpr int BM = 128;      // rows per CTA (256 per pair)
+constexpr int BN = 256;      // columns per pair tile
+constexpr int BN_CTA = 128;  // B columns each CTA loads
+constexpr int BK = 64;
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BM * BK * 2;           // 16 KiB
+constexpr int B_BOX_N = 64;
+constexpr int B_BOX_BYTES = B_BOX_N * BK * 2;  // 8 KiB
+constexpr int B_BYTES = BK * BN_CTA * 2;       // 16 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int PAIR_STAGE_BYTES = 2 * STAGE_BYTES;
+constexpr int ACC_COLS = BN;
+constexpr int TMEM_COLS = 2 * ACC_COLS;
+constexpr int THREADS = 192;
+constexpr int EPI_WARPS_PAIR = 8;
+constexpr int GROUP_M = 16;  // raster group, in 256-row pair tiles
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr uint32_t IDESC = sm100::idesc_f32acc(0, 0, 1, 256, BN);
+}  // namespace hg2
+
+__global__ void __launch_bounds__(hg2::THREADS, 1)
+    hgemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     HgemmArgs args) {
+    using namespace sm100;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + hg2::STAGES * hg2::A_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + hg2::STAGES * hg2::STAGE_BYTES);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + hg2::STAGES;
+    uint64_t *tfull = bars + 2 * hg2::STAGES;
+    uint64_t *tempty = bars + 2 * hg2::STAGES + 2;
+    uint64_t *drain = bars + 2 * hg2::STAGES + 4;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * hg2::STAGES + 5);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = static_cast<int>(blockIdx.x >> 1);
+    const int npairs = static_cast<int>(gridDim.x >> 1);
+    const int tiles_m = (args.M + 2 * hg2::BM - 1) / (2 * hg2::BM);
+    const int tiles_n = (args.N + hg2::BN - 1) / hg2::BN;
+    const int num_tiles = tiles_m * tiles_n;
+    const int kblocks = (args.K + hg2::BK - 1) / hg2::BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < hg2::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], hg2::EPI_WARPS_PAIR);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, hg2::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    // Both CTAs' barriers must be initialised before either signals the other.
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0;
+            bool ok = true;
+            for (int t = pair; t < num_tiles && ok; t += npairs) {
+                int tm, tn;
+                tile_coords_g(t, tiles_m, tiles_n, hg2::GROUP_M, tm, tn);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x11,
+                                   args.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
+                    if (leader) mbar_arrive_expect_tx(&full[stage], hg2::PAIR_STAGE_BYTES);
+                    uint8_t *a_dst = sA + stage * hg2::A_BYTES;
+                    uint8_t *b_dst = sB + stage * hg2::B_BYTES;
+                    tma_load_2d_pair(a_dst, &tmA, full_leader, kb * hg2::BK,
+                                     tm * 2 * hg2::BM + static_cast<int>(rank) * hg2::BM);
+#pragma unroll
+                    for (int j = 0; j < hg2::BN_CTA / hg2::B_BOX_N; ++j)
+                        tma_load_2d_pair(b_dst + j * hg2::B_BOX_BYTES, &tmB, full_leader,
+                                         tn * hg2::BN + static_cast<int>(rank) * hg2::BN_CTA + j * hg2::B_BOX_N,
+                                         kb * hg2::BK);
+                    ++issued;
+                    if (++stage == hg2::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok && issued) {
+                if (leader) {
+                    // Loads in flight complete on this CTA's full barriers.
+                    const uint32_t n = issued < (uint32_t)hg2::STAGES ? issued : (uint32_t)hg2::STAGES;
+                    int s = stage;
+                    uint32_t ph = phase;
+                    for (uint32_t i = 0; i < n; ++i) {
+                        if (--s < 0) {
+                            s = hg2::STAGES - 1;
+                            ph ^= 1u;
+                        }
+                        mbar_wait_drain(&full[s], ph, 1000000000ull);
+                    }
+                } else {
+                    // The partner's loads complete on the leader's barriers,
+                    // which it cannot poll: give them a bounded grace period.
+                    const uint64_t t0 = globaltimer_ns();
+                    while (globaltimer_ns() - t0 < 2000000ull) {
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer (leader only)
+        if (leader && lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            bool issued_any = false;
+            for (int t = pair; t < num_tiles && ok; t += npairs) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x12,
+                               args.wait_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * hg2::ACC_COLS);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x13,
+                                   args.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(sA + stage * hg2::A_BYTES);
+                    const uint32_t b_base = smem_u32(sB + stage * hg2::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < hg2::BK / 16; ++kk) {
+                        const uint64_t adesc = sdesc_sw128(a_base + kk * 32, 16, 1024);
+                        const uint64_t bdesc = sdesc_sw128(b_base + kk * 2048, hg2::B_BOX_BYTES, 1024);
+                        umma_f16_pair(d_tmem, adesc, bdesc, hg2::IDESC, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    umma_commit_pair(&empty[stage], 0x3);
+                    issued_any = true;
+                    if (++stage == hg2::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair(&tfull[acc], 0x3);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (!ok && issued_any) {
+                umma_commit_pair(drain, 0x1);
+                mbar_wait_drain(drain, 0, 1000000000ull);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue (both CTAs)
+        const int q = warp & 3;
+        const int row_in_tile = static_cast<int>(rank) * hg2::BM + q * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+        const bool read_c = args.beta != 0.0f;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = pair; t < num_tiles; t += npairs) {
+            int tm, tn;
+            tile_coords_g(t, tiles_m, tiles_n, hg2::GROUP_M, tm, tn);
+            bool ok = mbar_wait_sleepy(&tfull[acc], acc_phase, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x14,
+                                args.wait_ns);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const int row = tm * 2 * hg2::BM + row_in_tile;
+            const bool row_ok = row < args.M;
+            uint16_t *crow = args.C + static_cast<int64_t>(row) * args.N;
+#pragma unroll 1
+            for (int c = 0; c < hg2::BN / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(tmem_base + lane_off + static_cast<uint32_t>(acc * hg2::ACC_COLS + c * 32), r);
+                tmem_ld_wait();
+                if (c == hg2::BN / 32 - 1) {
+                    // This warp's share of the accumulator is in registers:
+                    // one arrival per warp on the leader's barrier.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (leader)
+                            mbar_arrive(&tempty[acc]);
+                        else
+                            mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+                    }
+                }
+                const int col0 = tn * hg2::BN + c * 32;
+                if (!row_ok || col0 >= args.N) continue;
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = args.alpha * __uint_as_float(r[i]);
+                store_c_chunk(crow, col0, args.N, v, read_c, args.beta);
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, hg2::TMEM_COLS);
     }
 }
 
@@ -416,6 +693,55 @@ bool hgemm_tc_eligible(size_t m, size_t n, size_t k, const void *A, const void *
            n < (1ull << 31) && k < (1ull << 31) && ((m + 127) / 128) * ((n + 255) / 256) < (1ull << 31);
 }
 
+namespace {
+
+struct DeviceLaunchState {
+    bool attr1 = false, attr2 = false;
+    int max_pairs = 0;  // co-resident CTA pairs of hgemm_tc2_kernel
+};
+DeviceLaunchState g_hgemm_state[64];
+std::mutex g_hgemm_mu;
+
+int launch_pair_kernel(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, const HgemmArgs &args,
+                       size_t m, size_t n) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(hg2::THREADS);
+    cfg.dynamicSmemBytes = hg2::SMEM_BYTES;
+    cfg.stream = h->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int max_pairs;
+    {
+        std::lock_guard<std::mutex> lk(g_hgemm_mu);
+        DeviceLaunchState &st = g_hgemm_state[h->device & 63];
+        if (!st.attr2) {
+            cudaError_t e =
+                cudaFuncSetAttribute(hgemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hg2::SMEM_BYTES);
+            if (e != cudaSuccess) return fail_cuda(e, "hgemm pair smem attribute");
+            cfg.gridDim = dim3(2 * (h->sm_count / 2));
+            int clusters = 0;
+            e = cudaOccupancyMaxActiveClusters(&clusters, (void *)hgemm_tc2_kernel, &cfg);
+            if (e != cudaSuccess) return fail_cuda(e, "cudaOccupancyMaxActiveClusters");
+            st.max_pairs = clusters > 0 ? clusters : h->sm_count / 2;
+            st.attr2 = true;
+        }
+        max_pairs = st.max_pairs;
+    }
+    const size_t tiles = ((m + 255) / 256) * ((n + hg2::BN - 1) / hg2::BN);
+    const int pairs = static_cast<int>(tiles < static_cast<size_t>(max_pairs) ? tiles : max_pairs);
+    cfg.gridDim = dim3(2 * pairs);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, hgemm_tc2_kernel, tmA, tmB, args);
+    if (e != cudaSuccess) return fail_cuda(e, "hgemm tcgen05 pair launch");
+    return B2B_OK;
+}
+
+}  // namespace
+
 int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A, const uint16_t *B,
                  float beta, uint16_t *C) {
     if (hgemm_tc_eligible(m, n, k, A, B, C)) {
@@ -424,16 +750,21 @@ int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const
         if (rc) return rc;
         rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
         if (rc) return rc;
-        static bool attr_set[64] = {};
-        if (h->device >= 64 || !attr_set[h->device]) {
-            cudaError_t e =
-                cudaFuncSetAttribute(hgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hg::SMEM_BYTES);
-            if (e != cudaSuccess) return fail_cuda(e, "hgemm smem attribute");
-            if (h->device < 64) attr_set[h->device] = true;
+        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns};
+        // More than one 128-row tile: CTA pairs with 256 x 256 tiles.
+        if (m > static_cast<size_t>(hg::BM) && !h->force_single_cta) return launch_pair_kernel(h, tmA, tmB, args, m, n);
+        {
+            std::lock_guard<std::mutex> lk(g_hgemm_mu);
+            DeviceLaunchState &st = g_hgemm_state[h->device & 63];
+            if (!st.attr1) {
+                cudaError_t e =
+                    cudaFuncSetAttribute(hgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hg::SMEM_BYTES);
+                if (e != cudaSuccess) return fail_cuda(e, "hgemm smem attribute");
+                st.attr1 = true;
+            }
         }
         const int tiles = static_cast<int>(((m + hg::BM - 1) / hg::BM) * ((n + hg::BN - 1) / hg::BN));
         const int grid = tiles < h->sm_count ? tiles : h->sm_count;
-        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns};
         hgemm_tc_kernel<<<grid, hg::THREADS, hg::SMEM_BYTES, h->stream>>>(tmA, tmB, args);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "hgemm tcgen05 launch");

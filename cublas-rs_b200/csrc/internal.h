@@ -31,6 +31,9 @@ struct b2b_handle {
     cudaStream_t copy_stream = nullptr;
     // Upper bound on any single bounded device wait, in nanoseconds.
     uint64_t wait_limit_ns = 2000000000ull;
+    // HGEMM: use the single-CTA tensor-core kernel even where the CTA-pair
+    // kernel applies (B2B_HGEMM_SINGLE_CTA=1; for comparisons and tests).
+    bool force_single_cta = false;
 };
 
 namespace b2b {

@@ -34,8 +34,11 @@ def test_known_answer_128(handle):
 
 
 # tcgen05-eligible (K, N multiples of 8) and generic-path shapes
+# tcgen05-eligible (K, N multiples of 8; M <= 128 runs the single-CTA kernel,
+# M > 128 the CTA-pair kernel) and generic-path shapes
 SHAPES = [(128, 256, 64), (256, 512, 192), (128, 256, 8), (200, 264, 72), (1, 8, 8), (130, 300, 1000),
-          (512, 512, 512), (1024, 768, 4096), (37, 41, 43), (64, 100, 7)]
+          (512, 512, 512), (1024, 768, 4096), (37, 41, 43), (64, 100, 7), (300, 264, 72), (257, 520, 1000),
+          (384, 128, 64), (129, 8, 8), (4096, 4096, 64)]
 
 
 @pytest.mark.parametrize("m,n,k", SHAPES)
@@ -105,3 +108,27 @@ def test_hgemm_simple_equals_device(handle, oracle):
     host = C.copy()
     handle.hgemm_simple(b2blas.GemmConfig(m, n, k, 1.0, 0.5), A, B, host)
     assert np.array_equal(dev, host)
+
+
+def test_pair_kernel_matches_single_cta_kernel(oracle, monkeypatch):
+    # The CTA-pair kernel (M > 128) and the single-CTA kernel (forced with
+    # B2B_HGEMM_SINGLE_CTA=1) agree, both within the tolerance of FP64.
+    import b2blas
+
+    m, n, k = 1024, 1280, 768
+    A = oracle.normal_f16(m * k, 5, 1, 0.0, 0.1)
+    B = oracle.normal_f16(k * n, 5, 2, 0.0, 0.1)
+    C = oracle.normal_f16(m * n, 5, 3, 0.0, 0.1)
+    outs = []
+    for single in ("0", "1"):
+        monkeypatch.setenv("B2B_HGEMM_SINGLE_CTA", single)
+        h = b2blas.Handle(0)
+        try:
+            outs.append(_run(h, m, n, k, 1.25, 0.5, A, B, C))
+        finally:
+            h.close()
+    ref = oracle.hgemm_f64(m, n, k, 1.25, A, B, 0.5, C)
+    for o in outs:
+        assert oracle.rel_err(o, ref) <= 2e-3
+    diff = np.abs(outs[0].view(np.float16).astype(np.float64) - outs[1].view(np.float16).astype(np.float64))
+    assert np.max(diff) <= 2 * np.max(np.abs(ref)) * 2 ** -10

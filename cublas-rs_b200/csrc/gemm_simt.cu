@@ -372,30 +372,279 @@ int run_simt(b2b_handle *h, int64_t M, int64_t N, int64_t K, T alpha, T beta, co
     return B2B_OK;
 }
 
+// ---------------------------------------------------------------------------
+// FP32 GEMM with a multi-stage cp.async pipeline (16-byte vector path only:
+// K, N and the strides multiples of 4, operands 16-byte aligned).
+//
+// Same thread layout and register blocking as gemm_simt_kernel, but global
+// -> shared copies are asynchronous (cp.async), STAGES k-tiles deep, so no
+// registers hold tiles in transit and the copies of k-tiles kt+1..kt+S-1
+// overlap the FMAs of k-tile kt.  A is transposed on the way in with 4-byte
+// copies (As[k][m], padded); B is copied as 16-byte vectors (Bs[k][n]).
+// Out-of-range elements are zero-filled by the copy (src-size 0).
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool ok) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(ok ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, int STAGES>
+struct AsyncCfg {
+    static constexpr int NT = WARPS_M * WARPS_N * 32;
+    static constexpr int BM = WARPS_M * (TM / 4) * 16;
+    static constexpr int BN = WARPS_N * (TN / 4) * 32;
+    static constexpr int VW = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte copy
+    static constexpr int LDA_S = BM + 4;                          // As[k][m]
+    static constexpr int LDB_S = BN;                              // Bs[k][n]
+    static constexpr int A_STAGE = BK * LDA_S;
+    static constexpr int B_STAGE = BK * LDB_S;
+    static constexpr int A_COPIES = BM * BK / NT;         // element copies per thread
+    static constexpr int A_ROWS_PER_PASS = NT / BK;       // rows covered by one pass of the CTA
+    static constexpr int B_COPIES = BK * BN / VW / NT;    // 16-byte copies per thread
+    static constexpr int B_VECS_PER_ROW = BN / VW;
+    static constexpr int B_ROWS_PER_PASS = NT / B_VECS_PER_ROW;
+    static constexpr int SMEM = STAGES * (A_STAGE + B_STAGE) * static_cast<int>(sizeof(T));
+    static_assert(NT % BK == 0 && A_COPIES * NT == BM * BK, "A tile divides");
+    static_assert(NT % B_VECS_PER_ROW == 0 && B_COPIES * NT * VW == BK * BN, "B tile divides");
+};
+
+template <typename T>
+__device__ __forceinline__ void cp_async_elem(uint32_t dst, const T *src, bool ok) {
+    if constexpr (sizeof(T) == 4)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(ok ? 4 : 0) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(ok ? 8 : 0) : "memory");
+}
+
+template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, int STAGES, int MINB>
+__global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
+    gemm_async_kernel(const T *__restrict__ A, const T *__restrict__ B, T *__restrict__ C, int64_t M, int64_t N,
+                      int64_t K, T alpha, T beta, int64_t sA, int64_t sB, int64_t sC, TileMap tmap) {
+    using Cf = AsyncCfg<T, TM, TN, WARPS_M, WARPS_N, BK, STAGES>;
+    constexpr int BM = Cf::BM, BN = Cf::BN, NT = Cf::NT, VW = Cf::VW;
+    constexpr int ES = static_cast<int>(sizeof(T));
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T *As = reinterpret_cast<T *>(smem_raw);
+    T *Bs = As + STAGES * Cf::A_STAGE;
+
+    int64_t batch, bm, bn;
+    map_tile(blockIdx.x, tmap, batch, bm, bn);
+    A += batch * sA;
+    B += batch * sB;
+    C += batch * sC;
+    const int64_t m0 = bm * BM, n0 = bn * BN;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int wm = warp / WARPS_N, wn = warp % WARPS_N;
+    const int ty = lane >> 3, tx = lane & 7;
+    const int row_base = wm * (TM / 4) * 16 + ty * 4;
+    const int col_base = wn * (TN / 4) * 32 + tx * 4;
+
+    // Copy assignment.  A: this thread copies element (r0 + p*A_ROWS_PER_PASS,
+    // ka) of the A tile for p = 0..A_COPIES-1; B: 16-byte vector
+    // (kb0 + p*B_ROWS_PER_PASS, cb) of the B tile.  Only two global base
+    // pointers and a few scalars live across the main loop.
+    const int ka = tid % BK, r0 = tid / BK;
+    const int cb = (tid % Cf::B_VECS_PER_ROW) * VW, kb0 = tid / Cf::B_VECS_PER_ROW;
+    const int64_t rows_left = M - m0 - r0;  // copy p is in range iff p*A_ROWS_PER_PASS < rows_left
+    const bool col_ok = n0 + cb < N;        // N % VW == 0: a vector is all in or all out
+    const T *ga = A + (rows_left > 0 ? (m0 + r0) * K : 0) + ka;
+    const T *gb = B + static_cast<int64_t>(kb0) * N + (col_ok ? n0 + cb : 0);
+    const uint32_t sa0 = static_cast<uint32_t>(__cvta_generic_to_shared(As)) + (ka * Cf::LDA_S + r0) * ES;
+    const uint32_t sb0 = static_cast<uint32_t>(__cvta_generic_to_shared(Bs)) + (kb0 * Cf::LDB_S + cb) * ES;
+    const int64_t a_pass = static_cast<int64_t>(Cf::A_ROWS_PER_PASS) * K;
+    const int64_t b_pass = static_cast<int64_t>(Cf::B_ROWS_PER_PASS) * N;
+    const int64_t ktiles = (K + BK - 1) / BK;
+
+    auto load_stage = [&](int stage, int64_t kt) {
+        const int64_t k0 = kt * BK;
+        const uint32_t a_st = sa0 + static_cast<uint32_t>(stage * Cf::A_STAGE * ES);
+        const uint32_t b_st = sb0 + static_cast<uint32_t>(stage * Cf::B_STAGE * ES);
+        const bool ka_ok = k0 + ka < K;
+        const T *pa = ga + k0;
+#pragma unroll
+        for (int p = 0; p < Cf::A_COPIES; ++p) {
+            const bool ok = ka_ok && p * Cf::A_ROWS_PER_PASS < rows_left;
+            cp_async_elem<T>(a_st + p * Cf::A_ROWS_PER_PASS * ES, ok ? pa + p * a_pass : A, ok);
+        }
+        const T *pb = gb + k0 * N;
+#pragma unroll
+        for (int p = 0; p < Cf::B_COPIES; ++p) {
+            const bool ok = col_ok && k0 + kb0 + p * Cf::B_ROWS_PER_PASS < K;
+            cp_async16(b_st + p * Cf::B_ROWS_PER_PASS * Cf::LDB_S * ES, ok ? pb + p * b_pass : B, ok);
+        }
+    };
+
+    T acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = T(0);
+
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < ktiles) load_stage(s, s);
+        cp_async_commit();
+    }
+
+    auto load_frags = [&](const T *as, const T *bs, int kk, T (&af)[TM], T (&bf)[TN]) {
+#pragma unroll
+        for (int g = 0; g < TM / 4; ++g) {
+            T t[4];
+            Vec4<T>::load(as + kk * Cf::LDA_S + row_base + g * 16, t);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) af[g * 4 + e] = t[e];
+        }
+#pragma unroll
+        for (int g = 0; g < TN / 4; ++g) {
+            T t[4];
+            Vec4<T>::load(bs + kk * Cf::LDB_S + col_base + g * 32, t);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) bf[g * 4 + e] = t[e];
+        }
+    };
+
+    for (int64_t kt = 0; kt < ktiles; ++kt) {
+        cp_async_wait<STAGES - 2>();
+        __syncthreads();
+        const int64_t pre = kt + STAGES - 1;
+        if (pre < ktiles) load_stage(static_cast<int>(pre % STAGES), pre);
+        cp_async_commit();
+        const int stage = static_cast<int>(kt % STAGES);
+        const T *as = As + stage * Cf::A_STAGE;
+        const T *bs = Bs + stage * Cf::B_STAGE;
+        // Fragments double-buffered in registers: step kk+1's shared loads
+        // are issued before step kk's FMAs.
+        T af[2][TM], bf[2][TN];
+        load_frags(as, bs, 0, af[0], bf[0]);
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            if (kk + 1 < BK) load_frags(as, bs, kk + 1, af[(kk + 1) & 1], bf[(kk + 1) & 1]);
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fma(af[kk & 1][i], bf[kk & 1][j], acc[i][j]);
+        }
+    }
+    cp_async_wait<0>();
+
+    const bool read_c = beta != T(0);
+#pragma unroll
+    for (int gi = 0; gi < TM / 4; ++gi) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t r = m0 + row_base + gi * 16 + i;
+            if (r >= M) continue;
+            T *crow = C + r * N;
+#pragma unroll
+            for (int gj = 0; gj < TN / 4; ++gj) {
+                const int64_t c = n0 + col_base + gj * 32;
+                if (c >= N) continue;  // N % 4 == 0: the 4-vector is all in or all out
+                T out[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) out[e] = alpha * acc[gi * 4 + i][gj * 4 + e];
+                if (read_c) {
+                    T old[4];
+                    Vec4<T>::load(crow + c, old);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) out[e] = fma(beta, old[e], out[e]);
+                }
+                Vec4<T>::store(crow + c, out);
+            }
+        }
+    }
+}
+
+template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, int STAGES, int MINB>
+int run_async(b2b_handle *h, int64_t M, int64_t N, int64_t K, T alpha, T beta, const T *A, int64_t sA, const T *B,
+              int64_t sB, T *C, int64_t sC, int64_t batch) {
+    using Cf = AsyncCfg<T, TM, TN, WARPS_M, WARPS_N, BK, STAGES>;
+    TileMap tm;
+    tm.tiles_m = (M + Cf::BM - 1) / Cf::BM;
+    tm.tiles_n = (N + Cf::BN - 1) / Cf::BN;
+    tm.tiles_per_batch = tm.tiles_m * tm.tiles_n;
+    const int64_t blocks = tm.tiles_per_batch * batch;
+    if (blocks > 0x7fffffffLL) return b2b::fail(B2B_ERR_INVALID_ARG, "GEMM grid exceeds 2^31-1 tiles");
+    auto kern = gemm_async_kernel<T, TM, TN, WARPS_M, WARPS_N, BK, STAGES, MINB>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+    if (e == cudaSuccess) {
+        kern<<<static_cast<unsigned>(blocks), Cf::NT, Cf::SMEM, h->stream>>>(A, B, C, M, N, K, alpha, beta, sA, sB, sC,
+                                                                           tm);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return b2b::fail_cuda(e, "GEMM launch");
+    return B2B_OK;
+}
+
+
+bool vec_ok(int64_t K, int64_t N, int64_t sA, int64_t sB, int64_t sC, const void *A, const void *B, const void *C) {
+    return (K % 4 == 0) && (N % 4 == 0) && (sA % 4 == 0) && (sB % 4 == 0) && (sC % 4 == 0) && b2b::aligned16(A) &&
+           b2b::aligned16(B) && b2b::aligned16(C);
+}
+
+// FP32 GEMM dispatch: kernel `variant` (0 = default choice).
+int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
+              int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch) {
+    if (!vec_ok(K, N, sA, sB, sC, A, B, C) || variant == 1)
+        return run_simt<float, 8, 8, 4, 2, 8, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+    switch (variant) {
+        case 5: return run_async<float, 8, 8, 4, 2, 16, 2, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        case 6: return run_async<float, 8, 8, 4, 2, 16, 3, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        case 7: return run_async<float, 8, 16, 4, 2, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        case 8: return run_async<float, 16, 8, 2, 4, 16, 3, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        case 9: return run_async<float, 8, 16, 2, 4, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        case 10: return run_async<float, 16, 8, 2, 4, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        case 11: return run_async<float, 16, 8, 2, 4, 8, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        case 12: return run_async<float, 8, 8, 4, 4, 16, 3, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        default: return run_async<float, 16, 8, 2, 4, 8, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+    }
+}
+
+// FP64 GEMM dispatch.
+int run_dgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, double alpha, double beta,
+              const double *A, const double *B, double *C) {
+    const bool vec = (K % 4 == 0) && (N % 4 == 0) && b2b::aligned16(A) && b2b::aligned16(B) && b2b::aligned16(C);
+    if (!vec || variant == 1)
+        return run_simt<double, 4, 4, 4, 2, 16, 2>(h, M, N, K, alpha, beta, A, 0, B, 0, C, 0, 1);
+    switch (variant) {
+        case 2: return run_async<double, 8, 8, 4, 2, 8, 3, 1>(h, M, N, K, alpha, beta, A, 0, B, 0, C, 0, 1);
+        case 3: return run_async<double, 4, 8, 4, 2, 16, 3, 2>(h, M, N, K, alpha, beta, A, 0, B, 0, C, 0, 1);
+        case 4: return run_async<double, 8, 4, 4, 2, 16, 3, 2>(h, M, N, K, alpha, beta, A, 0, B, 0, C, 0, 1);
+        case 5: return run_async<double, 4, 4, 4, 2, 16, 3, 2>(h, M, N, K, alpha, beta, A, 0, B, 0, C, 0, 1);
+        case 6: return run_async<double, 8, 8, 2, 4, 8, 3, 1>(h, M, N, K, alpha, beta, A, 0, B, 0, C, 0, 1);
+        default: return run_async<double, 8, 8, 2, 4, 8, 3, 1>(h, M, N, K, alpha, beta, A, 0, B, 0, C, 0, 1);
+    }
+}
+
 }  // namespace
 
 namespace b2b {
 
-// SGEMM: 128x128 CTA tile, 8x8 per thread, BK=8, two CTAs per SM.
+// SGEMM: 128x128 CTA tile, 8x8 per thread, cp.async pipeline.
 int launch_sgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
                  float beta, float *C) {
-    return run_simt<float, 8, 8, 4, 2, 8, 2>(h, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, 0, B, 0, C, 0,
-                                             1);
+    return run_sgemm(h, h->sgemm_variant, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, 0, B, 0, C, 0, 1);
 }
 
 int launch_sgemm_strided_batched(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
                                  size_t sa, const float *B, size_t sb, float beta, float *C, size_t sc,
                                  size_t batch) {
-    return run_simt<float, 8, 8, 4, 2, 8, 2>(h, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, (int64_t)sa, B,
-                                             (int64_t)sb, C, (int64_t)sc, (int64_t)batch);
+    return run_sgemm(h, h->sgemm_variant, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, (int64_t)sa, B,
+                     (int64_t)sb, C, (int64_t)sc, (int64_t)batch);
 }
 
 // DGEMM: 64x64 CTA tile, 4x4 per thread, BK=16; the FP64 pipe issues at half
 // the FP32 rate, so a smaller register block keeps three CTAs resident.
 int launch_dgemm(b2b_handle *h, size_t m, size_t n, size_t k, double alpha, const double *A, const double *B,
                  double beta, double *C) {
-    return run_simt<double, 4, 4, 4, 2, 16, 2>(h, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, 0, B, 0, C,
-                                               0, 1);
+    return run_dgemm(h, h->dgemm_variant, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, B, C);
 }
 
 }  // namespace b2b

@@ -34,6 +34,10 @@ struct b2b_handle {
     // HGEMM: use the single-CTA tensor-core kernel even where the CTA-pair
     // kernel applies (B2B_HGEMM_SINGLE_CTA=1; for comparisons and tests).
     bool force_single_cta = false;
+    // SGEMM kernel configuration (B2B_SGEMM_VARIANT; 0 = the default).
+    int sgemm_variant = 0;
+    // DGEMM kernel configuration (B2B_DGEMM_VARIANT; 0 = the default).
+    int dgemm_variant = 0;
 };
 
 namespace b2b {

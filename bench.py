@@ -121,7 +121,11 @@ class ClockSampler:
                     rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
                 except AttributeError:
                     rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
-                self.samples.append((clk, rs))
+                try:
+                    pw = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0
+                except Exception:
+                    pw = None
+                self.samples.append((clk, rs, pw))
             except Exception:
                 pass
             self._stop.wait(self._period)
@@ -141,13 +145,16 @@ class ClockSampler:
         if not self.ok or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
                     "source": "nvml" if self.ok else "unavailable"}
-        clks = [c for c, _ in self.samples]
+        clks = [c for c, _, _ in self.samples]
         mask = 0
-        for _, r in self.samples:
+        for _, r, _ in self.samples:
             mask |= int(r)
         reasons = [name for bit, name in _REASONS if mask & bit and name != "gpu_idle"]
-        return {"sm_mhz": statistics.median(clks), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(self.samples), "source": "nvml"}
+        pws = [p for _, _, p in self.samples if p is not None]
+        return {"sm_mhz": statistics.median(clks), "sm_min_mhz": min(clks), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples),
+                "power_w_median": statistics.median(pws) if pws else None,
+                "power_w_max": max(pws) if pws else None, "source": "nvml"}
 
 
 # ------------------------------------------------------------ workloads
@@ -224,9 +231,9 @@ class GemmWorkload(Workload):
         self.cfg = b2blas.GemmConfig(m, self.n, k, alpha, beta)
         self.fn = {"hgemm": h.hgemm, "sgemm": h.sgemm, "dgemm": h.dgemm}[kind]
         self.simple = {"hgemm": h.hgemm_simple, "sgemm": h.sgemm_simple, "dgemm": h.dgemm_simple}[kind]
-        self.kernel = {"hgemm": "hgemm_tc_kernel", "sgemm": "gemm_simt_kernel<float>",
-                       "dgemm": "gemm_simt_kernel<double>"}[kind]
-        self.bound = "tensor" if kind == "hgemm" else "fma"
+        self.kernel = {"hgemm": "hgemm_tc2_kernel" if m > 128 else "hgemm_tc_kernel",
+                       "sgemm": "gemm_async_kernel<float>", "dgemm": "dgemm_dmma_kernel"}[kind]
+        self.bound = {"hgemm": "tensor", "sgemm": "fma", "dgemm": "fp64"}[kind]
         self.gather = bool(args.gather) and world > 1
         if self.gather:
             self.panels = torch.empty(sum(self.widths) * m, device=dev, dtype=tdt)
@@ -336,7 +343,7 @@ class BatchedWorkload(Workload):
         self.b = b2blas.DeviceBuffer.from_ptr(h, self.B.data_ptr(), self.batch * mk, "float32", owner=self.B)
         self.c = b2blas.DeviceBuffer.from_ptr(h, self.C.data_ptr(), self.batch * mk, "float32", owner=self.C)
         self.cfg = b2blas.GemmConfig(m, m, m, 1.0, 0.0)
-        self.kernel = "gemm_simt_kernel<float> (batched)"
+        self.kernel = "gemm_async_kernel<float> (batched)"
         self.bound = "fma"
 
     def step(self):
@@ -492,7 +499,7 @@ class MlpWorkload(Workload):
         self.bb = [wrap(t) for t in self.bias]
         self.zb = [wrap(t) for t in self.Z]
         self.launches_per_step = 8
-        self.kernel = "gemm_simt_kernel<float>"
+        self.kernel = "gemm_async_kernel<float>"
         self.bound = "fma"
 
     def forward(self, xb):
@@ -586,8 +593,9 @@ def roofline_peak(w, peaks, handle_info):
     sms = handle_info["sm_count"]
     mhz = float(peaks.get("sm_max_mhz", 1965.0))
     lanes = 64 if w.dtype == "f64" else 128
+    what = "FP64 (DMMA = DFMA rate)" if w.bound == "fp64" else "FP32 FFMA"
     return sms * lanes * 2 * mhz * 1e6 / 1e12, "TFLOP/s", \
-        f"computed FP{'64' if lanes == 64 else '32'} vector peak: {sms} SMs x {lanes} lanes x 2 x {mhz:.0f} MHz"
+        f"computed {what} peak: {sms} SMs x {lanes} FMA/clk x 2 x {mhz:.0f} MHz (no measured figure in MEASURED_PEAKS.json)"
 
 
 # ------------------------------------------------------------ reference
@@ -847,7 +855,7 @@ def main():
     else:
         achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
     traffic = load_traffic().get(args.workload)
-    roof = {"bound": "hbm" if w.bound == "hbm" else "tensor" if w.bound == "tensor" else "fma",
+    roof = {"bound": {"hbm": "hbm", "tensor": "tensor", "fp64": "tensor"}.get(w.bound, "fma"),
             "kernel": w.kernel, "achieved": achieved, "peak": peak, "unit": punit, "frac": achieved / peak,
             "peak_source": psrc, "traffic": traffic,
             "algorithmic_units_per_launch": w.units_per_step(),

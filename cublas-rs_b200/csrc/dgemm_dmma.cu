@@ -1,0 +1,203 @@
+// dgemm_dmma.cu -- DGEMM on the FP64 tensor path (mma.sync m8n8k4 .f64).
+//
+// C <- alpha * A * B + beta * C, row-major f64 operands, the operation of
+// cublas-rs's dgemm_* kernels (crates/cublas-l3/src/dgemm.rs:25-334).
+// tcgen05 has no f64 kind, so the FP64 matrix instruction on sm_100 is the
+// warp-level mma.sync .f64: one m8n8k4 instruction is 256 double FMAs for a
+// warp, fed from registers that each hold one element, so a warp loads 12
+// doubles from shared memory for 32 instructions (8192 FMAs) per 4-wide k
+// step -- about 20 times fewer operand loads per FMA than a DFMA outer
+// product.
+//
+//   * CTA tile 128 x 128, 8 warps as 2 (M) x 4 (N); each warp owns 64 x 32 =
+//     8 x 4 tiles of 8 x 8 accumulators (two doubles per thread per tile).
+//   * k-tiles of 16 in a 3-stage cp.async ring: A as As[m][k] (k contiguous,
+//     row pitch 20 doubles), B as Bs[k][n] (row pitch 132 doubles); both
+//     pitches are 32 bytes mod 128, so the fragment loads (thread t reads row
+//     t/4, element t%4 of A; row t%4, column t/4 of B) hit 16 distinct 8-byte
+//     bank slots per half-warp -- no conflicts.
+//   * Fragments are double-buffered in registers across k steps.
+// Fragment layout of m8n8k4 .f64: A (8x4, row): thread t holds A[t/4][t%4];
+// B (4x8, col): B[t%4][t/4]; C/D (8x8): C[t/4][2(t%4)], C[t/4][2(t%4)+1].
+// Requires K and N even and 16-byte aligned operands (else the CUDA-core
+// kernel in gemm_simt.cu runs).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+namespace {
+
+constexpr int kWarpsM = 2, kWarpsN = 4;
+constexpr int kThreads = kWarpsM * kWarpsN * 32;
+constexpr int kMT = 8, kNT = 4;          // 8x8 tiles per warp along M, N
+constexpr int kBM = kWarpsM * kMT * 8;   // 128
+constexpr int kBN = kWarpsN * kNT * 8;   // 128
+constexpr int kBK = 16;
+constexpr int kStages = 3;
+constexpr int kLdA = kBK + 4;            // As[m][k]
+constexpr int kLdB = kBN + 4;            // Bs[k][n]
+constexpr int kAStage = kBM * kLdA;
+constexpr int kBStage = kBK * kLdB;
+constexpr int kSmem = kStages * (kAStage + kBStage) * 8;
+constexpr int kACopies = kBM * kBK / 2 / kThreads;  // 16-byte copies per thread
+constexpr int kBCopies = kBK * kBN / 2 / kThreads;
+static_assert(kACopies * kThreads * 2 == kBM * kBK, "A tile divides");
+static_assert(kBCopies * kThreads * 2 == kBK * kBN, "B tile divides");
+
+__device__ __forceinline__ void cp16(uint32_t dst, const void *src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+
+__device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d[0]), "+d"(d[1])
+                 : "d"(a), "d"(b));
+}
+
+struct DTileMap {
+    int64_t tiles_m, tiles_n;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    dgemm_dmma_kernel(const double *__restrict__ A, const double *__restrict__ B, double *__restrict__ C, int64_t M,
+                      int64_t N, int64_t K, double alpha, double beta, DTileMap tmap) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    double *As = reinterpret_cast<double *>(smem_raw);
+    double *Bs = As + kStages * kAStage;
+
+    // Grouped raster (8 M tiles sweep the N tiles) for L2 reuse.
+    const int64_t t = blockIdx.x;
+    const int64_t span = 8 * tmap.tiles_n;
+    const int64_t g = t / span;
+    const int64_t first = g * 8;
+    const int64_t gm = tmap.tiles_m - first < 8 ? tmap.tiles_m - first : 8;
+    const int64_t r = t - g * span;
+    const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * kBN;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm0 = (warp / kWarpsN) * kMT * 8, wn0 = (warp % kWarpsN) * kNT * 8;
+    const int fr = lane >> 2, fc = lane & 3;  // fragment row / column in an 8x4 (A) or 4x8 (B) tile
+
+    // Copy assignment: A vector (ar + p*32, ak) and B vector (bk + p*4, bc).
+    const int ak = (tid % (kBK / 2)) * 2, ar = tid / (kBK / 2);           // 8 vectors per A row
+    const int bc = (tid % (kBN / 2)) * 2, bk = tid / (kBN / 2);           // 64 vectors per B row
+    constexpr int kARowsPerPass = kThreads / (kBK / 2);                   // 32
+    constexpr int kBRowsPerPass = kThreads / (kBN / 2);                   // 4
+    const int64_t rows_left = M - m0 - ar;
+    const bool col_ok = n0 + bc < N;
+    const double *ga = A + (rows_left > 0 ? (m0 + ar) * K : 0) + ak;
+    const double *gb = B + static_cast<int64_t>(bk) * N + (col_ok ? n0 + bc : 0);
+    const uint32_t sa0 = static_cast<uint32_t>(__cvta_generic_to_shared(As)) + (ar * kLdA + ak) * 8;
+    const uint32_t sb0 = static_cast<uint32_t>(__cvta_generic_to_shared(Bs)) + (bk * kLdB + bc) * 8;
+    const int64_t a_pass = static_cast<int64_t>(kARowsPerPass) * K;
+    const int64_t b_pass = static_cast<int64_t>(kBRowsPerPass) * N;
+    const int64_t ktiles = (K + kBK - 1) / kBK;
+
+    auto load_stage = [&](int stage, int64_t kt) {
+        const int64_t k0 = kt * kBK;
+        const uint32_t a_st = sa0 + static_cast<uint32_t>(stage * kAStage * 8);
+        const uint32_t b_st = sb0 + static_cast<uint32_t>(stage * kBStage * 8);
+        const bool ka_ok = k0 + ak < K;  // K even: the 2-vector is all in or all out
+#pragma unroll
+        for (int p = 0; p < kACopies; ++p) {
+            const bool ok = ka_ok && p * kARowsPerPass < rows_left;
+            cp16(a_st + p * kARowsPerPass * kLdA * 8, ok ? ga + k0 + p * a_pass : A, ok);
+        }
+        const double *pb = gb + k0 * N;
+#pragma unroll
+        for (int p = 0; p < kBCopies; ++p) {
+            const bool ok = col_ok && k0 + bk + p * kBRowsPerPass < K;
+            cp16(b_st + p * kBRowsPerPass * kLdB * 8, ok ? pb + p * b_pass : B, ok);
+        }
+    };
+
+    double acc[kMT][kNT][2];
+#pragma unroll
+    for (int i = 0; i < kMT; ++i)
+#pragma unroll
+        for (int j = 0; j < kNT; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+        if (s < ktiles) load_stage(s, s);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+
+    for (int64_t kt = 0; kt < ktiles; ++kt) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 2) : "memory");
+        __syncthreads();
+        const int64_t pre = kt + kStages - 1;
+        if (pre < ktiles) load_stage(static_cast<int>(pre % kStages), pre);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const int stage = static_cast<int>(kt % kStages);
+        const double *as = As + stage * kAStage + (wm0 + fr) * kLdA + fc;
+        const double *bs = Bs + stage * kBStage + fc * kLdB + wn0 + fr;
+        double af[2][kMT], bf[2][kNT];
+#pragma unroll
+        for (int i = 0; i < kMT; ++i) af[0][i] = as[i * 8 * kLdA];
+#pragma unroll
+        for (int j = 0; j < kNT; ++j) bf[0][j] = bs[j * 8];
+#pragma unroll
+        for (int ks = 0; ks < kBK / 4; ++ks) {
+            const int cur = ks & 1;
+            if (ks + 1 < kBK / 4) {
+#pragma unroll
+                for (int i = 0; i < kMT; ++i) af[cur ^ 1][i] = as[i * 8 * kLdA + (ks + 1) * 4];
+#pragma unroll
+                for (int j = 0; j < kNT; ++j) bf[cur ^ 1][j] = bs[(ks + 1) * 4 * kLdB + j * 8];
+            }
+#pragma unroll
+            for (int i = 0; i < kMT; ++i)
+#pragma unroll
+                for (int j = 0; j < kNT; ++j) dmma_8x8x4(acc[i][j], af[cur][i], bf[cur][j]);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+
+    const bool read_c = beta != 0.0;
+#pragma unroll
+    for (int i = 0; i < kMT; ++i) {
+        const int64_t row = m0 + wm0 + i * 8 + fr;
+        if (row >= M) continue;
+        double *crow = C + row * N;
+#pragma unroll
+        for (int j = 0; j < kNT; ++j) {
+            const int64_t col = n0 + wn0 + j * 8 + 2 * fc;
+            if (col >= N) continue;  // N even: both columns in range
+            double2 o = make_double2(alpha * acc[i][j][0], alpha * acc[i][j][1]);
+            double2 *dst = reinterpret_cast<double2 *>(crow + col);
+            if (read_c) {
+                const double2 old = *dst;
+                o.x = fma(beta, old.x, o.x);
+                o.y = fma(beta, old.y, o.y);
+            }
+            *dst = o;
+        }
+    }
+}
+
+}  // namespace
+
+namespace b2b {
+
+bool dgemm_dmma_eligible(int64_t N, int64_t K, const void *A, const void *B, const void *C) {
+    return (K % 2 == 0) && (N % 2 == 0) && aligned16(A) && aligned16(B) && aligned16(C);
+}
+
+int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
+                      const double *B, double *C) {
+    DTileMap tm{(M + kBM - 1) / kBM, (N + kBN - 1) / kBN};
+    const int64_t blocks = tm.tiles_m * tm.tiles_n;
+    if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "dgemm: grid exceeds 2^31-1 tiles");
+    cudaError_t e = cudaFuncSetAttribute(dgemm_dmma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e == cudaSuccess) {
+        dgemm_dmma_kernel<<<static_cast<unsigned>(blocks), kThreads, kSmem, h->stream>>>(A, B, C, M, N, K, alpha,
+                                                                                        beta, tm);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return fail_cuda(e, "dgemm launch");
+    return B2B_OK;
+}
+
+}  // namespace b2b

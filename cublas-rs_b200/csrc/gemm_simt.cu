@@ -607,9 +607,13 @@ int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float
     }
 }
 
-// FP64 GEMM dispatch.
+// FP64 GEMM dispatch: the FP64 tensor path (dgemm_dmma.cu) by default; the
+// CUDA-core DFMA kernels where its alignment rules do not hold (or when a
+// variant is forced, for comparisons).
 int run_dgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, double alpha, double beta,
               const double *A, const double *B, double *C) {
+    if (variant == 0 && b2b::dgemm_dmma_eligible(N, K, A, B, C))
+        return b2b::launch_dgemm_dmma(h, M, N, K, alpha, beta, A, B, C);
     const bool vec = (K % 4 == 0) && (N % 4 == 0) && b2b::aligned16(A) && b2b::aligned16(B) && b2b::aligned16(C);
     if (!vec || variant == 1)
         return run_simt<double, 4, 4, 4, 2, 16, 2>(h, M, N, K, alpha, beta, A, 0, B, 0, C, 0, 1);

@@ -73,6 +73,9 @@ int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const
                  float beta, uint16_t *C);
 int launch_sgemm_3xtf32(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
                         const float *B, float beta, float *C);
+bool dgemm_dmma_eligible(int64_t N, int64_t K, const void *A, const void *B, const void *C);
+int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
+                      const double *B, double *C);
 int launch_sgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A, const float *x,
                  float beta, float *y);
 int launch_saxpy(b2b_handle *h, size_t n, float alpha, const float *x, float *y);

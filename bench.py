@@ -786,6 +786,11 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        # Keep stdout to the one JSON line: NCCL's version banner goes away,
+        # warnings still reach stderr.
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
+
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
 

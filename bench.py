@@ -229,11 +229,14 @@ class GemmWorkload(Workload):
         self.b = b2blas.DeviceBuffer.from_ptr(h, self.B.data_ptr(), k * self.n, bdt, owner=self.B)
         self.c = b2blas.DeviceBuffer.from_ptr(h, self.C.data_ptr(), m * self.n, bdt, owner=self.C)
         self.cfg = b2blas.GemmConfig(m, self.n, k, alpha, beta)
-        self.fn = {"hgemm": h.hgemm, "sgemm": h.sgemm, "dgemm": h.dgemm}[kind]
-        self.simple = {"hgemm": h.hgemm_simple, "sgemm": h.sgemm_simple, "dgemm": h.dgemm_simple}[kind]
+        self.fn = {"hgemm": h.hgemm, "sgemm": h.sgemm_3xtf32 if args.tf32x3 else h.sgemm, "dgemm": h.dgemm}[kind]
+        self.simple = {"hgemm": h.hgemm_simple, "dgemm": h.dgemm_simple,
+                       "sgemm": h.sgemm_3xtf32_simple if args.tf32x3 else h.sgemm_simple}[kind]
         self.kernel = {"hgemm": "hgemm_tc2_kernel" if m > 128 else "hgemm_tc_kernel",
                        "sgemm": "gemm_async_kernel<float>", "dgemm": "dgemm_dmma_kernel"}[kind]
         self.bound = {"hgemm": "tensor", "sgemm": "fma", "dgemm": "fp64"}[kind]
+        if kind == "sgemm" and args.tf32x3:
+            self.kernel, self.bound = "sgemm_3xtf32_kernel", "tf32x3"
         self.gather = bool(args.gather) and world > 1
         if self.gather:
             self.panels = torch.empty(sum(self.widths) * m, device=dev, dtype=tdt)
@@ -588,6 +591,11 @@ def roofline_peak(w, peaks, handle_info):
     if w.bound == "tensor":
         return peaks["bf16_tflops"], "TFLOP/s", \
             f"dense f16/bf16 tensor, cuBLAS bf16 burst, {peaks['_source']}"
+    if w.bound == "tf32x3":
+        # three tf32 MMAs per product: the dense tf32 rate (half the f16/bf16
+        # rate) divided by 3, in FP32-equivalent flops
+        return peaks["bf16_tflops"] / 2 / 3, "TFLOP/s", \
+            f"dense tf32 = bf16/2 of the cuBLAS bf16 burst, /3 for the three MMAs, {peaks['_source']}"
     if w.bound == "hbm":
         return peaks["hbm_gbs"], "GB/s", f"HBM copy bandwidth, {peaks['_source']}"
     sms = handle_info["sm_count"]
@@ -761,6 +769,7 @@ def main():
     ap.add_argument("--workload", choices=["hgemm", "sgemm", "dgemm", "batched", "sgemv", "mlp"], default="hgemm")
     ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
     ap.add_argument("--gather", action="store_true", help="column-sharded GEMMs: all-gather C every step")
+    ap.add_argument("--tf32x3", action="store_true", help="sgemm: the opt-in 3xTF32 tensor-core kernel")
     ap.add_argument("--e2e-steps", type=int, default=None, help="0 skips the end-to-end pass")
     ap.add_argument("--m", type=int, default=None, help="GEMM size override (profiling small cases)")
     ap.add_argument("--n", type=int, default=None)
@@ -860,7 +869,7 @@ def main():
     else:
         achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
     traffic = load_traffic().get(args.workload)
-    roof = {"bound": {"hbm": "hbm", "tensor": "tensor", "fp64": "tensor"}.get(w.bound, "fma"),
+    roof = {"bound": {"hbm": "hbm", "tensor": "tensor", "fp64": "tensor", "tf32x3": "tensor"}.get(w.bound, "fma"),
             "kernel": w.kernel, "achieved": achieved, "peak": peak, "unit": punit, "frac": achieved / peak,
             "peak_source": psrc, "traffic": traffic,
             "algorithmic_units_per_launch": w.units_per_step(),

@@ -653,35 +653,9 @@ __global__ void __launch_bounds__(256) hgemm_simt_kernel(const uint16_t *__restr
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// Row-major [rows x cols] f16 matrix, box of box_cols (inner) x box_rows,
-// 128-byte swizzle, out-of-range elements read as zero.
 int encode_2d_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_cols,
                   uint32_t box_rows) {
-    auto enc = get_encode_fn();
-    if (!enc) return b2b::fail(B2B_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-    cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols * 2};
-    cuuint32_t box[2] = {box_cols, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return b2b::fail(B2B_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
-    return B2B_OK;
+    return b2b::encode_tma_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, rows, cols, box_cols, box_rows);
 }
 
 }  // namespace

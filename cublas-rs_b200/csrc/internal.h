@@ -2,6 +2,7 @@
 // shared by the translation units of libb2blas.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -60,6 +61,13 @@ int workspace(b2b_handle *h, size_t bytes, void **ptr);
 int staging(b2b_handle *h, size_t bytes, void **ptr);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Tensor map of a row-major [rows x cols] matrix for 2-D TMA tile loads:
+// box of box_cols (inner, contiguous) x box_rows, 128-byte swizzle (by default),
+// out-of-range elements read as zero (tma_host.cu).
+int encode_tma_2d(CUtensorMap *map, CUtensorMapDataType dtype, size_t elem_bytes, const void *base, uint64_t rows,
+                  uint64_t cols, uint32_t box_cols, uint32_t box_rows,
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // ---- kernel launchers (each returns a b2b_status) --------------------------
 int launch_sgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,

@@ -231,3 +231,42 @@ def test_batched_sgemm_list_api(handle, oracle):
     handle.batched_sgemm(b2blas.GemmConfig(m, n, k, 2.0, -1.0), batch, As, Bs, outs)
     for o, r in zip(outs, refs):
         assert oracle.rel_err(o, r) <= oracle.tol_normwise(k, "f32")
+
+
+# ------------------------------------------------- opt-in 3xTF32 SGEMM
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 32), (512, 512, 512), (300, 264, 72), (1, 4, 4), (129, 260, 1000),
+                                   (1024, 768, 4096), (15, 17, 33)])
+@pytest.mark.parametrize("alpha,beta", [(1.0, 0.0), (1.5, 0.5)])
+def test_sgemm_3xtf32_parity(handle, oracle, m, n, k, alpha, beta):
+    # Same FP32 bound as the FFMA kernel: ||C - C*|| / ||C*|| <= 4*K*eps(f32).
+    A = oracle.uniform_f32(m * k, 43, 1)
+    B = oracle.uniform_f32(k * n, 43, 2)
+    C = oracle.uniform_f32(m * n, 43, 3)
+    ref = oracle.sgemm_f64(m, n, k, alpha, A, B, beta, C)
+    a, b, c = handle.upload(A), handle.upload(B), handle.upload(C)
+    handle.sgemm_3xtf32(_cfg(m, n, k, alpha, beta), a, b, c)
+    handle.synchronize()
+    got = handle.download(c)
+    err = oracle.rel_err(got, ref)
+    assert err <= oracle.tol_normwise(k, "f32"), err
+    # Far tighter than a plain TF32 GEMM (~1e-3 at K=4096): the three-term
+    # split leaves the tensor core's f32 accumulation as the main error
+    # (measured ~3e-5 at K=4096; the FFMA kernel is ~1e-6).
+    assert err <= 1e-4, err
+
+
+def test_sgemm_3xtf32_8192_sampled(handle, oracle):
+    import b2blas
+
+    m = n = k = 8192
+    A = oracle.uniform_f32(m * k, 42, 1)
+    B = oracle.uniform_f32(k * n, 42, 2)
+    C = oracle.uniform_f32(m * n, 42, 3)
+    a, b, c = handle.upload(A), handle.upload(B), handle.upload(C)
+    handle.sgemm_3xtf32(b2blas.GemmConfig(m, n, k, 1.5, 0.5), a, b, c)
+    handle.synchronize()
+    got = handle.download(c).reshape(m, n)
+    for r in (0, 255, 256, 8191):
+        ref = oracle.sgemm_f64(m, n, k, 1.5, A, B, 0.5, C, row0=r, nrows=1)
+        assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= oracle.tol_normwise(k, "f32"), r

@@ -141,6 +141,7 @@ int b2b_create(int device, b2b_handle **out) {
         long v = atol(lim);
         if (v > 0) h->wait_limit_ns = static_cast<uint64_t>(v) * 1000000ull;
     }
+    if (const char *cm = getenv("B2B_COPY_MODE")) h->copy_mode_forced = (cm[0] == '1') ? 1 : (cm[0] == '0' ? 0 : -1);
     const char *single = getenv("B2B_HGEMM_SINGLE_CTA");
     h->force_single_cta = single && single[0] == '1';
     if (const char *v = getenv("B2B_SGEMM_VARIANT")) h->sgemm_variant = atoi(v);
@@ -156,6 +157,10 @@ int b2b_destroy(b2b_handle *h) {
     if (h->own_stream) cudaStreamSynchronize(h->own_stream);
     if (h->stream && h->stream != h->own_stream) cudaStreamSynchronize(h->stream);
     if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);
+    if (h->down_stream) cudaStreamSynchronize(h->down_stream);
+    for (int i = 0; i < h->pipe_event_count; ++i) cudaEventDestroy(h->pipe_events[i]);
+    delete[] h->pipe_events;
+    if (h->down_stream) cudaStreamDestroy(h->down_stream);
     if (h->workspace) cudaFree(h->workspace);
     if (h->staging) cudaFree(h->staging);
     if (h->d_status) cudaFree(h->d_status);

@@ -14,13 +14,18 @@
 //   * C is not uploaded when beta == 0 (it is not read).
 //   * The GEMMs split M into row panels and pipeline them over three
 //     streams: B goes up first, then panel p's rows of A (and C) go up on the
-//     copy stream while panel p-1 computes and panel p-2's C comes back on
-//     the return stream.  With page-locked host buffers the host<->device
-//     copies in both directions overlap the tensor-core work.
+//     upload stream while panel p-1 computes; each panel's C comes back on
+//     the download stream.  Whether downloads may run while uploads are
+//     still going (full duplex) or should wait for the last upload (phased)
+//     depends on the host: some PCIe/host-memory paths lose most of their
+//     bandwidth when both directions run at once.  Large calls therefore try
+//     each schedule once and keep the faster.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
 
+#include <chrono>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -37,27 +42,28 @@ int dim_err(const char *fn, const char *what, size_t expected, size_t got) {
                                        std::to_string(expected) + ", got " + std::to_string(got));
 }
 
-// Per-call stream/event set for the pipelined copies.
-struct Pipe {
-    cudaStream_t up = nullptr, down = nullptr;
-    std::vector<cudaEvent_t> ev;
-    ~Pipe() {
-        for (auto e : ev) cudaEventDestroy(e);
-        if (up) cudaStreamDestroy(up);
-        if (down) cudaStreamDestroy(down);
-    }
-    int init(int nev) {
-        cudaError_t e = cudaStreamCreateWithFlags(&up, cudaStreamNonBlocking);
-        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&down, cudaStreamNonBlocking);
-        for (int i = 0; i < nev && e == cudaSuccess; ++i) {
-            cudaEvent_t ev1;
-            e = cudaEventCreateWithFlags(&ev1, cudaEventDisableTiming);
-            if (e == cudaSuccess) ev.push_back(ev1);
+// The handle's copy streams and at least `nev` events (created on first use).
+int pipe_setup(b2b_handle *h, int nev) {
+    cudaError_t e = cudaSuccess;
+    if (!h->down_stream) e = cudaStreamCreateWithFlags(&h->down_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess && h->pipe_event_count < nev) {
+        cudaEvent_t *ev = new (std::nothrow) cudaEvent_t[nev];
+        if (!ev) return fail(B2B_ERR_ALLOC, "pipeline events: out of host memory");
+        int i = 0;
+        for (; i < h->pipe_event_count; ++i) ev[i] = h->pipe_events[i];
+        for (; i < nev && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            for (int j = h->pipe_event_count; j < i - 1; ++j) cudaEventDestroy(ev[j]);
+            delete[] ev;
+        } else {
+            delete[] h->pipe_events;
+            h->pipe_events = ev;
+            h->pipe_event_count = nev;
         }
-        if (e != cudaSuccess) return fail_cuda(e, "pipeline setup");
-        return B2B_OK;
     }
-};
+    if (e != cudaSuccess) return fail_cuda(e, "pipeline setup");
+    return B2B_OK;
+}
 
 int finish(b2b_handle *h) {
     cudaError_t e = cudaStreamSynchronize(h->stream);
@@ -104,43 +110,72 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     if (prow > m) prow = m;
     panels = static_cast<int>((m + prow - 1) / prow);
 
-    Pipe p;
-    if ((rc = p.init(2 * panels + 1))) return rc;
+    if ((rc = pipe_setup(h, 2 * panels + 2))) return rc;
+    cudaEvent_t *ev = h->pipe_events;
+    cudaStream_t up = h->copy_stream, down = h->down_stream;
+    // Copy schedule (see b2b_handle::copy_mode_*): try each mode once on large
+    // calls, then keep the faster.
+    const bool large = bytes >= (size_t(64) << 20);
+    int mode = 0;
+    if (h->copy_mode_forced >= 0)
+        mode = h->copy_mode_forced;
+    else if (large && h->copy_mode_ms_per_gb[0] == 0.0)
+        mode = 0;
+    else if (large && h->copy_mode_ms_per_gb[1] == 0.0)
+        mode = 1;
+    else if (large)
+        mode = h->copy_mode_ms_per_gb[1] < h->copy_mode_ms_per_gb[0] ? 1 : 0;
+    const auto t_start = std::chrono::steady_clock::now();
     cudaError_t e = cudaSuccess;
     cudaStream_t cs = h->stream;
     // The compute stream's earlier work (e.g. a previous call still using
     // the staging buffer) must finish before the copies overwrite it.
-    cudaEvent_t start_ev = p.ev[2 * panels];
+    cudaEvent_t start_ev = ev[2 * panels];
+    cudaEvent_t up_done = ev[2 * panels + 1];
     e = cudaEventRecord(start_ev, cs);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(p.up, start_ev, 0);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(dB, B, eb, cudaMemcpyHostToDevice, p.up);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(up, start_ev, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dB, B, eb, cudaMemcpyHostToDevice, up);
     for (int i = 0; i < panels && e == cudaSuccess; ++i) {
         const size_t r0 = static_cast<size_t>(i) * prow;
         const size_t rows = (r0 + prow <= m) ? prow : m - r0;
-        e = cudaMemcpyAsync(dA + r0 * k, A + r0 * k, rows * k * sizeof(T), cudaMemcpyHostToDevice, p.up);
+        e = cudaMemcpyAsync(dA + r0 * k, A + r0 * k, rows * k * sizeof(T), cudaMemcpyHostToDevice, up);
         if (e == cudaSuccess && up_c)
-            e = cudaMemcpyAsync(dC + r0 * n, C + r0 * n, rows * n * sizeof(T), cudaMemcpyHostToDevice, p.up);
-        if (e == cudaSuccess) e = cudaEventRecord(p.ev[2 * i], p.up);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, p.ev[2 * i], 0);
+            e = cudaMemcpyAsync(dC + r0 * n, C + r0 * n, rows * n * sizeof(T), cudaMemcpyHostToDevice, up);
+        if (e == cudaSuccess) e = cudaEventRecord(ev[2 * i], up);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ev[2 * i], 0);
         if (e != cudaSuccess) break;
         rc = launch(h, rows, n, k, alpha, dA + r0 * k, dB, beta, dC + r0 * n);
         if (rc) {
-            cudaStreamSynchronize(p.up);
+            cudaStreamSynchronize(up);
             cudaStreamSynchronize(cs);
             return rc;
         }
-        e = cudaEventRecord(p.ev[2 * i + 1], cs);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(p.down, p.ev[2 * i + 1], 0);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(C + r0 * n, dC + r0 * n, rows * n * sizeof(T), cudaMemcpyDeviceToHost, p.down);
+        e = cudaEventRecord(ev[2 * i + 1], cs);
     }
-    cudaError_t e2 = cudaStreamSynchronize(p.up);
-    cudaError_t e3 = cudaStreamSynchronize(p.down);
+    // Phased mode: the device-to-host copies wait for the last upload.
+    if (e == cudaSuccess) e = cudaEventRecord(up_done, up);
+    if (e == cudaSuccess && mode == 0) e = cudaStreamWaitEvent(down, up_done, 0);
+    for (int i = 0; i < panels && e == cudaSuccess; ++i) {
+        const size_t r0 = static_cast<size_t>(i) * prow;
+        const size_t rows = (r0 + prow <= m) ? prow : m - r0;
+        e = cudaStreamWaitEvent(down, ev[2 * i + 1], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(C + r0 * n, dC + r0 * n, rows * n * sizeof(T), cudaMemcpyDeviceToHost, down);
+    }
+    cudaError_t e2 = cudaStreamSynchronize(up);
+    cudaError_t e3 = cudaStreamSynchronize(down);
     if (e == cudaSuccess) e = e2;
     if (e == cudaSuccess) e = e3;
     if (e != cudaSuccess) {
         cudaStreamSynchronize(cs);
         return fail_cuda(e, fn);
+    }
+    if (large && h->copy_mode_forced < 0) {
+        const double ms =
+            std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_start).count();
+        const double per_gb = ms / (static_cast<double>(bytes) / 1e9);
+        double &slot = h->copy_mode_ms_per_gb[mode];
+        slot = slot == 0.0 ? per_gb : (slot < per_gb ? slot : per_gb);
     }
     return finish(h);
 }

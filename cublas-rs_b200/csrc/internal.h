@@ -27,9 +27,19 @@ struct b2b_handle {
     // Grow-only device staging for the host-slice calls (operands copied in).
     void *staging = nullptr;
     size_t staging_bytes = 0;
-    // Second stream and events for overlapping host<->device copies with
-    // compute inside the host-slice calls.
-    cudaStream_t copy_stream = nullptr;
+    // Streams and events of the host-slice calls' copy pipeline (created on
+    // first use): `up` carries host-to-device copies, `down` device-to-host.
+    cudaStream_t copy_stream = nullptr;  // up
+    cudaStream_t down_stream = nullptr;
+    cudaEvent_t *pipe_events = nullptr;
+    int pipe_event_count = 0;
+    // Copy scheduling of large host-slice GEMMs: 0 = phased (device-to-host
+    // copies start after the last host-to-device copy), 1 = full duplex (both
+    // directions at once).  Which is faster depends on the host's PCIe/memory
+    // path, so the first two large calls try one each and later calls use the
+    // faster (B2B_COPY_MODE=0/1 forces one).
+    int copy_mode_forced = -1;
+    double copy_mode_ms_per_gb[2] = {0.0, 0.0};
     // Upper bound on any single bounded device wait, in nanoseconds.
     uint64_t wait_limit_ns = 2000000000ull;
     // HGEMM: use the single-CTA tensor-core kernel even where the CTA-pair

@@ -501,17 +501,28 @@ class MlpWorkload(Workload):
         self.wb = [wrap(t) for t in self.W]
         self.bb = [wrap(t) for t in self.bias]
         self.zb = [wrap(t) for t in self.Z]
-        self.launches_per_step = 8
+        self.bias_vec = [t[0].contiguous() for t in self.bias]
+        self.bvec = [wrap(t) for t in self.bias_vec]
+        self.fused = bool(args.fused)
+        self.algo = b2blas.Algo.Tf32x3 if args.tf32x3 else b2blas.Algo.Default
+        self.launches_per_step = 4 if self.fused else 8
         self.kernel = "gemm_async_kernel<float>"
         self.bound = "fma"
 
     def forward(self, xb):
+        import b2blas
+
         inp = xb
         for i in range(4):
             fi, fo = self.dims[i], self.dims[i + 1]
-            self.h.sgemm_tiled(__import__("b2blas").GemmConfig(self.batch, fo, fi, 1.0, 0.0), inp, self.wb[i],
-                               self.zb[i])
-            self.h.saxpy(self.batch * fo, 1.0, self.bb[i], self.zb[i])
+            cfg = b2blas.GemmConfig(self.batch, fo, fi, 1.0, 0.0)
+            if self.fused:
+                # bias (and, for hidden layers, ReLU) in the GEMM epilogue
+                self.h.sgemm_bias(cfg, inp, self.wb[i], self.zb[i], self.bvec[i], relu=i < 3, algo=self.algo)
+            else:
+                # the example's pattern: sgemm + saxpy of the pre-broadcast bias
+                self.h.sgemm_tiled(cfg, inp, self.wb[i], self.zb[i])
+                self.h.saxpy(self.batch * fo, 1.0, self.bb[i], self.zb[i])
             inp = self.zb[i]
 
     def step(self):
@@ -536,7 +547,9 @@ class MlpWorkload(Workload):
         torch.cuda.current_stream().synchronize()
 
     def config(self):
-        return {"workload": "mlp forward 1024-4096-4096-4096-1024, batch 4096, sgemm + saxpy bias"
+        how = ("fused sgemm+bias+ReLU epilogue" if self.fused else "sgemm + saxpy bias") + \
+            (", 3xTF32" if self.algo == __import__("b2blas").Algo.Tf32x3 else "")
+        return {"workload": f"mlp forward 1024-4096-4096-4096-1024, batch 4096, {how}"
                             + (", one replica per GPU" if self.world > 1 else ""),
                 "layers": self.dims, "batch": self.batch, "parallelism": f"replicas x{self.world}",
                 "l2": "weights + activations larger than L2: no flush needed"}
@@ -772,7 +785,8 @@ def main():
     ap.add_argument("--workload", choices=["hgemm", "sgemm", "dgemm", "batched", "sgemv", "mlp"], default="hgemm")
     ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
     ap.add_argument("--gather", action="store_true", help="column-sharded GEMMs: all-gather C every step")
-    ap.add_argument("--tf32x3", action="store_true", help="sgemm: the opt-in 3xTF32 tensor-core kernel")
+    ap.add_argument("--tf32x3", action="store_true", help="sgemm/mlp: the opt-in 3xTF32 tensor-core kernel")
+    ap.add_argument("--fused", action="store_true", help="mlp: bias (+ReLU) fused into the SGEMM epilogue")
     ap.add_argument("--e2e-steps", type=int, default=None, help="0 skips the end-to-end pass")
     ap.add_argument("--m", type=int, default=None, help="GEMM size override (profiling small cases)")
     ap.add_argument("--n", type=int, default=None)

@@ -319,6 +319,21 @@ class Handle:
     def sgemm_double_buf_simple(self, config, a, b, c):
         self.sgemm_simple(config, a, b, c, Algo.DoubleBuf)
 
+    def sgemm_bias(self, config, a, b, c, bias=None, relu=False, algo=Algo.Default):
+        """C = act(alpha*A*B + beta*C + bias[col]) with the bias broadcast and
+        the optional ReLU in the GEMM epilogue (the mlp example's
+        sgemm + saxpy(pre-broadcast bias) pair in one kernel)."""
+        m, n, k = config.m, config.n, config.k
+        if m and n and k:
+            self._need(a, m * k, "A", np.float32)
+            self._need(b, k * n, "B", np.float32)
+            self._need(c, m * n, "C", np.float32)
+            if bias is not None:
+                self._need(bias, n, "bias", np.float32)
+        _check(self._lib.b2b_sgemm_bias(self._h, int(algo), m, n, k, config.alpha, ctypes.c_void_p(a.ptr),
+                                        ctypes.c_void_p(b.ptr), config.beta, ctypes.c_void_p(c.ptr),
+                                        ctypes.c_void_p(bias.ptr if bias is not None else 0), 1 if relu else 0))
+
     def sgemm_3xtf32(self, config, a, b, c):
         """Opt-in split-precision tensor-core SGEMM (no reference counterpart)."""
         self.sgemm(config, a, b, c, Algo.Tf32x3)

@@ -52,6 +52,20 @@ int b2b_sgemm(b2b_handle *h, int algo, size_t m, size_t n, size_t k, float alpha
     return launch_sgemm(h, m, n, k, alpha, A, B, beta, C);
 }
 
+int b2b_sgemm_bias(b2b_handle *h, int algo, size_t m, size_t n, size_t k, float alpha, const float *A,
+                   const float *B, float beta, float *C, const float *bias, int relu) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemm_bias: NULL handle");
+    if (int rc = check_algo(algo, "b2b_sgemm_bias", true)) return rc;
+    if (m == 0 || n == 0 || k == 0) return B2B_OK;
+    if (!A || !B || !C) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemm_bias: NULL operand");
+    if (!bytes_ok(m, k, 4) || !bytes_ok(k, n, 4) || !bytes_ok(m, n, 4))
+        return fail(B2B_ERR_INVALID_ARG, "b2b_sgemm_bias: sizes overflow");
+    DeviceGuard g(h);
+    const int r = relu ? 1 : 0;
+    if (algo == B2B_ALGO_3XTF32) return launch_sgemm_3xtf32_bias(h, m, n, k, alpha, A, B, beta, C, bias, r);
+    return launch_sgemm_bias(h, m, n, k, alpha, A, B, beta, C, bias, r);
+}
+
 int b2b_dgemm(b2b_handle *h, int algo, size_t m, size_t n, size_t k, double alpha, const double *A,
               const double *B, double beta, double *C) {
     if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_dgemm: NULL handle");

@@ -110,6 +110,21 @@ struct TileMap {
     int64_t tiles_m, tiles_n, tiles_per_batch;
 };
 
+// Optional epilogue additions: C = act(alpha*A*B + beta*C + bias[col]) with
+// act = ReLU when relu != 0 (bias == nullptr: no bias).
+template <typename T>
+struct EpiArgs {
+    const T *bias;
+    int relu;
+};
+
+template <typename T>
+__device__ __forceinline__ T epi_apply(T v, const EpiArgs<T> &epi, int64_t col) {
+    if (epi.bias) v += epi.bias[col];
+    if (epi.relu) v = v > T(0) ? v : T(0);
+    return v;
+}
+
 // Grouped raster: GROUP consecutive M tiles sweep the N tiles together, so
 // the A and B panels of the CTAs resident at one time stay in L2.
 __device__ __forceinline__ void map_tile(int64_t t, const TileMap &tm, int64_t &batch, int64_t &bm, int64_t &bn) {
@@ -128,7 +143,8 @@ __device__ __forceinline__ void map_tile(int64_t t, const TileMap &tm, int64_t &
 template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, bool VEC, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB)
     gemm_simt_kernel(const T *__restrict__ A, const T *__restrict__ B, T *__restrict__ C, int64_t M, int64_t N,
-                     int64_t K, T alpha, T beta, int64_t sA, int64_t sB, int64_t sC, TileMap tmap) {
+                     int64_t K, T alpha, T beta, int64_t sA, int64_t sB, int64_t sC, TileMap tmap,
+                     EpiArgs<T> epi) {
     using Cf = Cfg<T, TM, TN, WARPS_M, WARPS_N, BK>;
     constexpr int BM = Cf::BM, BN = Cf::BN, W = Cf::W;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -320,6 +336,10 @@ __global__ void __launch_bounds__(kThreads, MINB)
 #pragma unroll
                         for (int e = 0; e < 4; ++e) out[e] = fma(beta, old[e], out[e]);
                     }
+                    if (epi.bias || epi.relu) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) out[e] = epi_apply(out[e], epi, c + e);
+                    }
                     Vec4<T>::store(crow + c, out);
                 } else {
 #pragma unroll
@@ -327,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
                         if (c + e < N) {
                             T v = out[e];
                             if (read_c) v = fma(beta, crow[c + e], v);
-                            crow[c + e] = v;
+                            crow[c + e] = epi_apply(v, epi, c + e);
                         }
                     }
                 }
@@ -338,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
 
 template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, int MINB>
 int run_simt(b2b_handle *h, int64_t M, int64_t N, int64_t K, T alpha, T beta, const T *A, int64_t sA, const T *B,
-             int64_t sB, T *C, int64_t sC, int64_t batch) {
+             int64_t sB, T *C, int64_t sC, int64_t batch, EpiArgs<T> epi = EpiArgs<T>{nullptr, 0}) {
     using Cf = Cfg<T, TM, TN, WARPS_M, WARPS_N, BK>;
     TileMap tm;
     tm.tiles_m = (M + Cf::BM - 1) / Cf::BM;
@@ -356,7 +376,7 @@ int run_simt(b2b_handle *h, int64_t M, int64_t N, int64_t K, T alpha, T beta, co
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
         if (e == cudaSuccess) {
             kern<<<static_cast<unsigned>(blocks), kThreads, Cf::SMEM, h->stream>>>(A, B, C, M, N, K, alpha, beta,
-                                                                                   sA, sB, sC, tm);
+                                                                                   sA, sB, sC, tm, epi);
             e = cudaGetLastError();
         }
     } else {
@@ -364,7 +384,7 @@ int run_simt(b2b_handle *h, int64_t M, int64_t N, int64_t K, T alpha, T beta, co
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
         if (e == cudaSuccess) {
             kern<<<static_cast<unsigned>(blocks), kThreads, Cf::SMEM, h->stream>>>(A, B, C, M, N, K, alpha, beta,
-                                                                                   sA, sB, sC, tm);
+                                                                                   sA, sB, sC, tm, epi);
             e = cudaGetLastError();
         }
     }
@@ -425,7 +445,8 @@ __device__ __forceinline__ void cp_async_elem(uint32_t dst, const T *src, bool o
 template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, int STAGES, int MINB>
 __global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
     gemm_async_kernel(const T *__restrict__ A, const T *__restrict__ B, T *__restrict__ C, int64_t M, int64_t N,
-                      int64_t K, T alpha, T beta, int64_t sA, int64_t sB, int64_t sC, TileMap tmap) {
+                      int64_t K, T alpha, T beta, int64_t sA, int64_t sB, int64_t sC, TileMap tmap,
+                     EpiArgs<T> epi) {
     using Cf = AsyncCfg<T, TM, TN, WARPS_M, WARPS_N, BK, STAGES>;
     constexpr int BM = Cf::BM, BN = Cf::BN, NT = Cf::NT, VW = Cf::VW;
     constexpr int ES = static_cast<int>(sizeof(T));
@@ -556,6 +577,10 @@ __global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) out[e] = fma(beta, old[e], out[e]);
                 }
+                if (epi.bias || epi.relu) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) out[e] = epi_apply(out[e], epi, c + e);
+                }
                 Vec4<T>::store(crow + c, out);
             }
         }
@@ -564,7 +589,7 @@ __global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
 
 template <typename T, int TM, int TN, int WARPS_M, int WARPS_N, int BK, int STAGES, int MINB>
 int run_async(b2b_handle *h, int64_t M, int64_t N, int64_t K, T alpha, T beta, const T *A, int64_t sA, const T *B,
-              int64_t sB, T *C, int64_t sC, int64_t batch) {
+              int64_t sB, T *C, int64_t sC, int64_t batch, EpiArgs<T> epi = EpiArgs<T>{nullptr, 0}) {
     using Cf = AsyncCfg<T, TM, TN, WARPS_M, WARPS_N, BK, STAGES>;
     TileMap tm;
     tm.tiles_m = (M + Cf::BM - 1) / Cf::BM;
@@ -576,7 +601,7 @@ int run_async(b2b_handle *h, int64_t M, int64_t N, int64_t K, T alpha, T beta, c
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
     if (e == cudaSuccess) {
         kern<<<static_cast<unsigned>(blocks), Cf::NT, Cf::SMEM, h->stream>>>(A, B, C, M, N, K, alpha, beta, sA, sB, sC,
-                                                                           tm);
+                                                                           tm, epi);
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) return b2b::fail_cuda(e, "GEMM launch");
@@ -591,19 +616,20 @@ bool vec_ok(int64_t K, int64_t N, int64_t sA, int64_t sB, int64_t sC, const void
 
 // FP32 GEMM dispatch: kernel `variant` (0 = default choice).
 int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
-              int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch) {
+              int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch,
+              EpiArgs<float> epi = EpiArgs<float>{nullptr, 0}) {
     if (!vec_ok(K, N, sA, sB, sC, A, B, C) || variant == 1)
-        return run_simt<float, 8, 8, 4, 2, 8, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        return run_simt<float, 8, 8, 4, 2, 8, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
     switch (variant) {
-        case 5: return run_async<float, 8, 8, 4, 2, 16, 2, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
-        case 6: return run_async<float, 8, 8, 4, 2, 16, 3, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
-        case 7: return run_async<float, 8, 16, 4, 2, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
-        case 8: return run_async<float, 16, 8, 2, 4, 16, 3, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
-        case 9: return run_async<float, 8, 16, 2, 4, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
-        case 10: return run_async<float, 16, 8, 2, 4, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
-        case 11: return run_async<float, 16, 8, 2, 4, 8, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
-        case 12: return run_async<float, 8, 8, 4, 4, 16, 3, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
-        default: return run_async<float, 16, 8, 2, 4, 8, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch);
+        case 5: return run_async<float, 8, 8, 4, 2, 16, 2, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        case 6: return run_async<float, 8, 8, 4, 2, 16, 3, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        case 7: return run_async<float, 8, 16, 4, 2, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        case 8: return run_async<float, 16, 8, 2, 4, 16, 3, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        case 9: return run_async<float, 8, 16, 2, 4, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        case 10: return run_async<float, 16, 8, 2, 4, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        case 11: return run_async<float, 16, 8, 2, 4, 8, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        case 12: return run_async<float, 8, 8, 4, 4, 16, 3, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        default: return run_async<float, 16, 8, 2, 4, 8, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
     }
 }
 
@@ -635,6 +661,12 @@ namespace b2b {
 int launch_sgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
                  float beta, float *C) {
     return run_sgemm(h, h->sgemm_variant, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, 0, B, 0, C, 0, 1);
+}
+
+int launch_sgemm_bias(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
+                      float beta, float *C, const float *bias, int relu) {
+    return run_sgemm(h, h->sgemm_variant, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, 0, B, 0, C, 0, 1,
+                     EpiArgs<float>{bias, relu});
 }
 
 int launch_sgemm_strided_batched(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,

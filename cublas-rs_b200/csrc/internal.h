@@ -82,6 +82,10 @@ int encode_tma_2d(CUtensorMap *map, CUtensorMapDataType dtype, size_t elem_bytes
 // ---- kernel launchers (each returns a b2b_status) --------------------------
 int launch_sgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
                  float beta, float *C);
+int launch_sgemm_bias(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
+                      float beta, float *C, const float *bias, int relu);
+int launch_sgemm_3xtf32_bias(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
+                             const float *B, float beta, float *C, const float *bias, int relu);
 int launch_dgemm(b2b_handle *h, size_t m, size_t n, size_t k, double alpha, const double *A, const double *B,
                  double beta, double *C);
 int launch_sgemm_strided_batched(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,

@@ -69,6 +69,8 @@ struct X3Args {
     float alpha, beta;
     int *status;
     uint64_t wait_ns;
+    const float *bias;  // optional per-column bias (nullptr: none)
+    int relu;           // apply max(0, .) last
 };
 
 __device__ __forceinline__ void x3_tile(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
@@ -81,7 +83,14 @@ __device__ __forceinline__ void x3_tile(int t, int tiles_m, int tiles_n, int &tm
     tn = r / gm;
 }
 
-__device__ __forceinline__ void store_c_f32(float *crow, int col0, int N, float (&v)[32], bool read_c, float beta) {
+__device__ __forceinline__ float x3_epi(float x, const float *bias, int relu, int col) {
+    if (bias) x += bias[col];
+    if (relu) x = x > 0.0f ? x : 0.0f;
+    return x;
+}
+
+__device__ __forceinline__ void store_c_f32(float *crow, int col0, int N, float (&v)[32], bool read_c, float beta,
+                                            const float *bias, int relu) {
     if (col0 + 32 <= N) {
         float4 *dst = reinterpret_cast<float4 *>(crow + col0);
 #pragma unroll
@@ -94,6 +103,13 @@ __device__ __forceinline__ void store_c_f32(float *crow, int col0, int N, float 
                 o.z = fmaf(beta, old.z, o.z);
                 o.w = fmaf(beta, old.w, o.w);
             }
+            if (bias || relu) {
+                const int c = col0 + 4 * j;
+                o.x = x3_epi(o.x, bias, relu, c);
+                o.y = x3_epi(o.y, bias, relu, c + 1);
+                o.z = x3_epi(o.z, bias, relu, c + 2);
+                o.w = x3_epi(o.w, bias, relu, c + 3);
+            }
             dst[j] = o;
         }
     } else {
@@ -102,7 +118,7 @@ __device__ __forceinline__ void store_c_f32(float *crow, int col0, int N, float 
             if (col0 + i < N) {
                 float x = v[i];
                 if (read_c) x = fmaf(beta, crow[col0 + i], x);
-                crow[col0 + i] = x;
+                crow[col0 + i] = x3_epi(x, bias, relu, col0 + i);
             }
         }
     }
@@ -350,7 +366,7 @@ __global__ void __launch_bounds__(x3::THREADS, 1)
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = args.alpha * __uint_as_float(r[i]);
-                store_c_f32(crow, col0, args.N, v, read_c, args.beta);
+                store_c_f32(crow, col0, args.N, v, read_c, args.beta, args.bias, args.relu);
             }
             if (++acc == 2) {
                 acc = 0;
@@ -376,10 +392,15 @@ namespace b2b {
 
 int launch_sgemm_3xtf32(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
                         float beta, float *C) {
+    return launch_sgemm_3xtf32_bias(h, m, n, k, alpha, A, B, beta, C, nullptr, 0);
+}
+
+int launch_sgemm_3xtf32_bias(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
+                             const float *B, float beta, float *C, const float *bias, int relu) {
     const bool eligible = (k % 4 == 0) && (n % 4 == 0) && aligned16(A) && aligned16(B) && aligned16(C) &&
                           m < (1ull << 31) && n < (1ull << 31) && k < (1ull << 31);
     // Shapes TMA cannot describe run the FFMA SGEMM (same result contract).
-    if (!eligible) return launch_sgemm(h, m, n, k, alpha, A, B, beta, C);
+    if (!eligible) return launch_sgemm_bias(h, m, n, k, alpha, A, B, beta, C, bias, relu);
     CUtensorMap tmA, tmB;
     int rc = encode_tma_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, A, m, k, x3::BK, x3::BM);
     if (rc) return rc;
@@ -416,7 +437,7 @@ int launch_sgemm_3xtf32(b2b_handle *h, size_t m, size_t n, size_t k, float alpha
     const size_t tiles = ((m + 255) / 256) * ((n + x3::BN - 1) / x3::BN);
     const int pairs = static_cast<int>(tiles < static_cast<size_t>(max_pairs) ? tiles : max_pairs);
     cfg.gridDim = dim3(2 * pairs);
-    X3Args args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns};
+    X3Args args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns, bias, relu};
     cudaError_t e = cudaLaunchKernelEx(&cfg, sgemm_3xtf32_kernel, tmA, tmB, args);
     if (e != cudaSuccess) return fail_cuda(e, "3xtf32 launch");
     return B2B_OK;

@@ -124,6 +124,15 @@ B2B_API int b2b_sgemm(b2b_handle *h, int algo, size_t m, size_t n, size_t k, flo
 B2B_API int b2b_sgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t k, float alpha, const float *A,
                              size_t a_len, const float *B, size_t b_len, float beta, float *C, size_t c_len);
 
+/* SGEMM with the bias broadcast and ReLU folded into the epilogue:
+ * C <- act(alpha*A*B + beta*C + bias[j]) for every row, act = max(0, .) when
+ * relu != 0; bias is a device vector of n floats or NULL.  Replaces the
+ * mlp example's sgemm + saxpy-of-a-pre-broadcast-bias pair
+ * (examples/mlp/src/main.rs:130-144, bias materialised at :52) and its
+ * pending ReLU step (:146); no counterpart in the reference library. */
+B2B_API int b2b_sgemm_bias(b2b_handle *h, int algo, size_t m, size_t n, size_t k, float alpha, const float *A,
+                           const float *B, float beta, float *C, const float *bias, int relu);
+
 /* ------------------------------------------------------ Level 3: DGEMM */
 
 /* Handle::dgemm_* (lib.rs:527-612) -> crates/cublas-l3/src/dgemm.rs:342-569. */

@@ -270,3 +270,49 @@ def test_sgemm_3xtf32_8192_sampled(handle, oracle):
     for r in (0, 255, 256, 8191):
         ref = oracle.sgemm_f64(m, n, k, 1.5, A, B, 0.5, C, row0=r, nrows=1)
         assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= oracle.tol_normwise(k, "f32"), r
+
+
+# -------------------------------------------- fused bias + ReLU epilogue
+
+@pytest.mark.parametrize("algo", [0, 5])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 200, 100), (4096, 1024, 1024), (15, 17, 33), (130, 264, 72)])
+@pytest.mark.parametrize("relu", [False, True])
+def test_sgemm_bias_relu(handle, oracle, algo, m, n, k, relu):
+    # C = act(alpha*A*B + beta*C + bias[col]), the mlp layer in one kernel;
+    # same FP32 bound as SGEMM.
+    import b2blas
+
+    A = oracle.uniform_f32(m * k, 61, 1)
+    B = oracle.uniform_f32(k * n, 61, 2)
+    C = oracle.uniform_f32(m * n, 61, 3)
+    bias = oracle.normal_f32(n, 61, 5, 0.0, 0.5)
+    ref = oracle.sgemm_f64(m, n, k, 1.25, A, B, 0.5, C).reshape(m, n) + bias.astype(np.float64)[None, :]
+    if relu:
+        ref = np.maximum(ref, 0.0)
+    a, b, c, bd = handle.upload(A), handle.upload(B), handle.upload(C), handle.upload(bias)
+    handle.sgemm_bias(_cfg(m, n, k, 1.25, 0.5), a, b, c, bd, relu=relu, algo=b2blas.Algo(algo))
+    handle.synchronize()
+    got = handle.download(c)
+    assert oracle.rel_err(got, ref.ravel()) <= oracle.tol_normwise(k, "f32")
+    if relu:
+        assert np.all(got >= 0.0)
+
+
+def test_sgemm_bias_equals_sgemm_plus_saxpy(handle, oracle):
+    # The fused layer matches the reference's two-call pattern
+    # (examples/mlp/src/main.rs:130-144): sgemm then saxpy of the
+    # pre-broadcast bias.
+    import b2blas
+
+    m, n, k = 256, 512, 128
+    A = oracle.uniform_f32(m * k, 3, 1)
+    B = oracle.uniform_f32(k * n, 3, 2)
+    bias = oracle.normal_f32(n, 3, 5, 0.0, 0.01)
+    cfg = b2blas.GemmConfig(m, n, k, 1.0, 0.0)
+    a, b, bd = handle.upload(A), handle.upload(B), handle.upload(bias)
+    c1, c2 = handle.zeroed(m * n), handle.zeroed(m * n)
+    handle.sgemm_tiled(cfg, a, b, c1)
+    handle.saxpy(m * n, 1.0, handle.upload(np.tile(bias, m)), c1)
+    handle.sgemm_bias(cfg, a, b, c2, bd)
+    handle.synchronize()
+    np.testing.assert_allclose(handle.download(c2), handle.download(c1), rtol=0, atol=1e-5)

@@ -18,8 +18,10 @@ through the host-slice API (b2b_hgemm_simple): every step copies A and B from
 page-locked host memory and C back.
 
 Other workloads (--workload): sgemm (8192^3, alpha 1.5, beta 0.5), dgemm
-(4096^3), batched (4096 x 256^3 strided, batch-sharded), sgemv (16384^2, N),
-mlp (4 layers 1024-4096-4096-4096-1024, batch 4096, sgemm + saxpy bias).
+(4096^3), batched (4096 x 256^3 strided, batch-sharded), sgemv / dgemv /
+hgemv (16384^2, N, or T with --trans), reduce (sdot by default, --op
+nrm2|asum|iamax; 2^28-element f32 vectors), mlp (4 layers
+1024-4096-4096-4096-1024, batch 4096, sgemm + saxpy bias).
 
 --impl reference times the CPU restatement of the reference's algorithm
 (the oracle's host triple loop) on this machine's cores, rank 0 only, with a
@@ -398,38 +400,48 @@ class BatchedWorkload(Workload):
         return out
 
 
-class SgemvWorkload(Workload):
-    """SGEMV 16384 x 16384, N, alpha 1, beta 0 (replicas on N GPUs)."""
+class GemvWorkload(Workload):
+    """GEMV 16384 x 16384, N or T, alpha 1, beta 0 (replicas on N GPUs), in
+    f32 (sgemv), f64 (dgemv) or f16 with f32 accumulate (hgemv)."""
 
     unit = "GB/s"
     bound = "hbm"
 
-    def __init__(self, h, rank, world, args):
+    def __init__(self, h, rank, world, args, prec="s"):
+        import numpy as np
         import torch
 
         import b2blas
 
-        self.h, self.world = h, world
+        self.h, self.world, self.prec = h, world, prec
         self.m = self.n = 16384
         self.trans = 1 if args.trans else 0
+        tdt, ndt, self.esize, self.dtype = {"s": (torch.float32, "float32", 4, "f32"),
+                                           "d": (torch.float64, "float64", 8, "f64"),
+                                           "h": (torch.float16, "uint16", 2, "f16")}[prec]
         dev = torch.device("cuda", torch.cuda.current_device())
         g = torch.Generator(device=dev).manual_seed(42 + rank)
-        self.A = torch.rand(self.m, self.n, device=dev, generator=g) * 2 - 1
+        mk = lambda *shape: (torch.rand(*shape, device=dev, generator=g, dtype=torch.float32) * 2 - 1).to(tdt)  # noqa: E731
+        self.A = mk(self.m, self.n)
         xl, yl = (self.n, self.m) if self.trans == 0 else (self.m, self.n)
-        self.x = torch.rand(xl, device=dev, generator=g) * 2 - 1
-        self.y = torch.zeros(yl, device=dev)
-        self.a = b2blas.DeviceBuffer.from_ptr(h, self.A.data_ptr(), self.m * self.n, "float32", owner=self.A)
-        self.xd = b2blas.DeviceBuffer.from_ptr(h, self.x.data_ptr(), xl, "float32", owner=self.x)
-        self.yd = b2blas.DeviceBuffer.from_ptr(h, self.y.data_ptr(), yl, "float32", owner=self.y)
-        self.kernel = "sgemv_n_kernel" if self.trans == 0 else "sgemv_t_partial_kernel"
+        self.x = mk(xl)
+        self.y = torch.zeros(yl, device=dev, dtype=tdt)
+        buf = lambda t, n: b2blas.DeviceBuffer.from_ptr(h, t.data_ptr(), n, ndt, owner=t)  # noqa: E731
+        self.a, self.xd, self.yd = buf(self.A, self.m * self.n), buf(self.x, xl), buf(self.y, yl)
+        if prec == "s":
+            self.kernel = "sgemv_n_kernel" if self.trans == 0 else "sgemv_t_partial_kernel"
+            self.fn = h.sgemv
+        else:
+            self.kernel = "gemvx_n_kernel" if self.trans == 0 else "gemvx_t_partial_kernel"
+            self.fn = h.dgemv if prec == "d" else h.hgemv_dev
         self.launches_per_step = 1 if self.trans == 0 else 2
-        self.dtype = "f32"
+        self._np = np
 
     def step(self):
-        self.h.sgemv(self.trans, self.m, self.n, 1.0, self.a, self.xd, 0.0, self.yd)
+        self.fn(self.trans, self.m, self.n, 1.0, self.a, self.xd, 0.0, self.yd)
 
     def units_per_step(self):
-        return 4.0 * (self.m * self.n + self.m + self.n)
+        return float(self.esize) * (self.m * self.n + self.m + self.n)
 
     def scale(self, v):
         return v / 1e9
@@ -439,40 +451,137 @@ class SgemvWorkload(Workload):
         self._hx, self.hx = _pinned_numpy(self.x)
         self._hy, self.hy = _pinned_numpy(self.y)
         self.hA = self.hA.reshape(-1)
-        return 4 * (self.m * self.n + len(self.hx)), 4 * len(self.hy)
+        if self.prec == "h":  # numpy float16 views of the pinned buffers
+            self.hA, self.hx, self.hy = (a.view(self._np.float16) for a in (self.hA, self.hx, self.hy))
+        e = self.esize
+        return e * (self.m * self.n + len(self.hx)), e * len(self.hy)
 
     def e2e_step(self):
-        self.h.sgemv_simple(self.trans, self.m, self.n, 1.0, self.hA, self.hx, 0.0, self.hy)
+        fn = {"s": self.h.sgemv_simple, "d": self.h.dgemv_simple, "h": self.h.hgemv}[self.prec]
+        fn(self.trans, self.m, self.n, 1.0, self.hA, self.hx, 0.0, self.hy)
 
     def config(self):
-        return {"workload": f"sgemv {self.m}x{self.n} {'NT'[self.trans]}"
+        gib = self.m * self.n * self.esize / 2 ** 30
+        return {"workload": f"{self.prec}gemv {self.m}x{self.n} {'NT'[self.trans]}"
                             + (f", one replica per GPU" if self.world > 1 else ""),
                 "m": self.m, "n": self.n, "trans": "NT"[self.trans], "alpha": 1.0, "beta": 0.0,
-                "parallelism": f"replicas x{self.world}", "l2": "A is 1 GiB, larger than L2: no flush needed"}
+                "parallelism": f"replicas x{self.world}",
+                "l2": f"A is {gib:g} GiB, larger than L2: no flush needed"}
 
     def cpu_sample(self, oracle, target_s):
-        import numpy as np
-
+        np = self._np
         n = self.n
         x = self.x.cpu().numpy()
+        if self.prec == "h":
+            x = x.view(np.uint16)
+        xf = np.empty(n, np.float32)
         rows = 256
         out = {}
         for attempt in range(2):
             A = np.ascontiguousarray(self.A[:rows].cpu().numpy()).reshape(-1)
-            y = np.zeros(rows, np.float32)
+            if self.prec == "h":
+                A = A.view(np.uint16)
+            y = np.zeros(rows, A.dtype)
             t0 = time.perf_counter()
             reps = 0
             while True:
-                oracle.cpu_sgemv_rows(rows, n, 1.0, A, x, 0.0, y)
+                if self.prec == "s":
+                    oracle.cpu_sgemv_rows(rows, n, 1.0, A, x, 0.0, y)
+                elif self.prec == "d":
+                    oracle.cpu_dgemv_rows(rows, n, 1.0, A, x, 0.0, y)
+                else:
+                    oracle.cpu_hgemv_rows(rows, n, 1.0, A, x, 0.0, y, xf)
                 reps += 1
                 if time.perf_counter() - t0 > (0.2 if attempt == 0 else target_s):
                     break
             dt = time.perf_counter() - t0
-            out = {"value": reps * 4.0 * (rows * n + n + rows) / dt / 1e9, "seconds": dt, "rows": rows}
+            out = {"value": reps * float(self.esize) * (rows * n + n + rows) / dt / 1e9, "seconds": dt,
+                   "rows": rows}
             if attempt == 0:
                 rows = min(self.m, 4096)
         out["sample"] = f"{out['rows']} rows x {n} (repeated for ~{target_s:.0f} s), row loop"
         return out
+
+
+class ReduceWorkload(Workload):
+    """Level-1 reduction (sdot by default) over 2^28-element f32 vectors
+    (1 GiB each), result kept on the device (b2b_sreduce_async)."""
+
+    unit = "GB/s"
+    bound = "hbm"
+    kernel = "sreduce_kernel"
+
+    def __init__(self, h, rank, world, args):
+        import torch
+
+        import b2blas
+
+        self.h, self.world = h, world
+        self.op = args.op
+        self.n = args.n or (1 << 28)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(42 + rank)
+        self.x = torch.rand(self.n, device=dev, generator=g) * 2 - 1
+        self.y = torch.rand(self.n, device=dev, generator=g) * 2 - 1 if self.op == "dot" else None
+        self.res = torch.zeros(1, device=dev, dtype=torch.int64 if self.op == "iamax" else torch.float32)
+        self.xd = b2blas.DeviceBuffer.from_ptr(h, self.x.data_ptr(), self.n, "float32", owner=self.x)
+        self.yd = (b2blas.DeviceBuffer.from_ptr(h, self.y.data_ptr(), self.n, "float32", owner=self.y)
+                   if self.y is not None else None)
+        self.rd = b2blas.DeviceBuffer.from_ptr(h, self.res.data_ptr(), 1,
+                                               "uint64" if self.op == "iamax" else "float32", owner=self.res)
+        self.opcode = {"dot": 0, "nrm2": 1, "asum": 2, "iamax": 3}[self.op]
+        self.vectors = 2 if self.op == "dot" else 1
+        self.dtype = "f32"
+
+    def step(self):
+        self.h.sreduce_async(self.opcode, self.n, self.xd, self.yd, self.rd)
+
+    def units_per_step(self):
+        return 4.0 * self.n * self.vectors
+
+    def scale(self, v):
+        return v / 1e9
+
+    def e2e_setup(self):
+        self._hx, self.hx = _pinned_numpy(self.x)
+        if self.y is not None:
+            self._hy, self.hy = _pinned_numpy(self.y)
+        return 4 * self.n * self.vectors, 8 if self.op == "iamax" else 4
+
+    def e2e_step(self):
+        h = self.h
+        if self.op == "dot":
+            h.sdot_simple(self.n, self.hx, self.hy)
+        else:
+            getattr(h, {"nrm2": "snrm2_simple", "asum": "sasum_simple", "iamax": "isamax_simple"}[self.op])(
+                self.n, self.hx)
+
+    def config(self):
+        return {"workload": f"s{self.op} n={self.n}" + (f", one replica per GPU" if self.world > 1 else ""),
+                "n": self.n, "parallelism": f"replicas x{self.world}",
+                "l2": f"{self.vectors} x {self.n * 4 / 2 ** 30:g} GiB inputs, larger than L2: no flush needed"}
+
+    def cpu_sample(self, oracle, target_s):
+        import numpy as np
+
+        n = min(self.n, 1 << 26)
+        x = self.x[:n].cpu().numpy()
+        y = self.y[:n].cpu().numpy() if self.y is not None else x
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < target_s:
+            if self.op == "dot":
+                oracle.cpu_sdot(n, x, y)
+            elif self.op == "iamax":
+                oracle.isamax(n, x)
+            else:
+                oracle.sreduce_ref(self.op, n, x)
+            reps += 1
+        dt = time.perf_counter() - t0
+        threads = oracle.num_threads() if self.op == "dot" else 1
+        return {"value": reps * 4.0 * n * self.vectors / dt / 1e9, "seconds": dt, "threads": threads,
+                "sample": f"first {n} elements (repeated for ~{target_s:.0f} s), "
+                          + ("threaded f32 partial sums" if self.op == "dot" else "single-thread loop")}
 
 
 class MlpWorkload(Workload):
@@ -590,8 +699,10 @@ def make_workload(name, h, rank, world, args):
         return GemmWorkload(h, rank, world, args, "dgemm", m, n, k, 1.5, 0.5, weak=False)
     if name == "batched":
         return BatchedWorkload(h, rank, world, args)
-    if name == "sgemv":
-        return SgemvWorkload(h, rank, world, args)
+    if name in ("sgemv", "dgemv", "hgemv"):
+        return GemvWorkload(h, rank, world, args, prec=name[0])
+    if name == "reduce":
+        return ReduceWorkload(h, rank, world, args)
     if name == "mlp":
         return MlpWorkload(h, rank, world, args)
     raise SystemExit(f"unknown workload {name}")
@@ -709,6 +820,54 @@ def run_reference(args, rank, world):
         unit, scale, dtype = "GB/s", 1e9, "f32"
         sample = f"{rows} of 16384 rows per step, row loop, {nt} threads"
         cfg = {"workload": "sgemv 16384x16384 N", "m": 16384, "n": n}
+    elif wl in ("dgemv", "hgemv"):
+        n = 16384
+        rows = 2048
+        if wl == "dgemv":
+            A = rng.random(rows * n) * 2 - 1
+            x = rng.random(n) * 2 - 1
+            y = np.zeros(rows)
+        else:
+            A = (rng.random(rows * n, dtype=np.float32) * 2 - 1).astype(np.float16).view(np.uint16)
+            x = (rng.random(n, dtype=np.float32) * 2 - 1).astype(np.float16).view(np.uint16)
+            y = np.zeros(rows, np.uint16)
+            xf = np.empty(n, np.float32)
+        es = 8 if wl == "dgemv" else 2
+
+        def step():
+            t0 = time.perf_counter()
+            if wl == "dgemv":
+                oracle.cpu_dgemv_rows(rows, n, 1.0, A, x, 0.0, y)
+            else:
+                oracle.cpu_hgemv_rows(rows, n, 1.0, A, x, 0.0, y, xf)
+            return time.perf_counter() - t0, float(es) * (rows * n + n + rows)
+
+        unit, scale, dtype = "GB/s", 1e9, "f64" if wl == "dgemv" else "f16"
+        sample = f"{rows} of 16384 rows per step, row loop, {nt} threads"
+        cfg = {"workload": f"{wl} 16384x16384 N", "m": 16384, "n": n}
+    elif wl == "reduce":
+        n = 1 << 26
+        x = (rng.random(n, dtype=np.float32) * 2 - 1)
+        y = (rng.random(n, dtype=np.float32) * 2 - 1)
+        op = args.op
+        vec = 2 if op == "dot" else 1
+
+        def step():
+            t0 = time.perf_counter()
+            if op == "dot":
+                oracle.cpu_sdot(n, x, y)
+            elif op == "iamax":
+                oracle.isamax_ref(n, x)
+            else:
+                oracle.sreduce_ref(op, n, x)
+            return time.perf_counter() - t0, 4.0 * n * vec
+
+        unit, scale, dtype = "GB/s", 1e9, "f32"
+        if op != "dot":
+            nt = 1
+        sample = (f"first {n} elements per step, "
+                  + (f"threaded f32 partial sums, {nt} threads" if op == "dot" else "the reference's 32-lane loop, 1 thread"))
+        cfg = {"workload": f"s{op} n={1 << 28}", "n": 1 << 28}
     else:
         dims = [1024, 4096, 4096, 4096, 1024]
         Ws = [(rng.standard_normal(dims[i] * dims[i + 1], dtype=np.float32) / dims[i] ** 0.5) for i in range(4)]
@@ -782,7 +941,9 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b2blas", "reference"], default="b2blas")
-    ap.add_argument("--workload", choices=["hgemm", "sgemm", "dgemm", "batched", "sgemv", "mlp"], default="hgemm")
+    ap.add_argument("--workload", choices=["hgemm", "sgemm", "dgemm", "batched", "sgemv", "dgemv", "hgemv", "reduce",
+                                           "mlp"], default="hgemm")
+    ap.add_argument("--op", choices=["dot", "nrm2", "asum", "iamax"], default="dot", help="reduce: which reduction")
     ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
     ap.add_argument("--gather", action="store_true", help="column-sharded GEMMs: all-gather C every step")
     ap.add_argument("--tf32x3", action="store_true", help="sgemm/mlp: the opt-in 3xTF32 tensor-core kernel")
@@ -881,7 +1042,7 @@ def main():
         torch.cuda.synchronize()
         per_launch_ms = e0.elapsed_time(e1) / args.steps
         achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
-    elif isinstance(w, SgemvWorkload) or (isinstance(w, GemmWorkload) and w.gather):
+    elif isinstance(w, GemvWorkload) or (isinstance(w, GemmWorkload) and w.gather):
         achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
     else:
         achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
@@ -904,7 +1065,7 @@ def main():
 
         oracle.set_num_threads(os.cpu_count() or 1)
         s = w.cpu_sample(oracle, args.cpu_seconds)
-        cpu = {"value": s["value"], "unit": w.unit, "cores": oracle.num_threads(), "kind": "port",
+        cpu = {"value": s["value"], "unit": w.unit, "cores": s.get("threads", oracle.num_threads()), "kind": "port",
                "sample": s["sample"], "seconds": round(s["seconds"], 2)}
 
     if dist is not None:

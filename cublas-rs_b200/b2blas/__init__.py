@@ -447,6 +447,39 @@ class Handle:
     def sgemv_tiled_simple(self, trans, m, n, alpha, a, x, beta, y):
         self.sgemv_simple(trans, m, n, alpha, a, x, beta, y, Algo.Tiled)
 
+    # ---- Level 2: DGEMV, HGEMV (lib.rs:312-366)
+    def dgemv(self, trans, m, n, alpha, a, x, beta, y):
+        xl, yl = (n, m) if int(trans) == 0 else (m, n)
+        if m and n:
+            self._need(a, m * n, "A", np.float64)
+            self._need(x, xl, "x", np.float64)
+            self._need(y, yl, "y", np.float64)
+        _check(self._lib.b2b_dgemv(self._h, int(trans), m, n, alpha, ctypes.c_void_p(a.ptr),
+                                   ctypes.c_void_p(x.ptr), beta, ctypes.c_void_p(y.ptr)))
+
+    def dgemv_simple(self, trans, m, n, alpha, a, x, beta, y):
+        a, x, y = _host(a, np.float64), _host(x, np.float64), _host(y, np.float64)
+        _check(self._lib.b2b_dgemv_simple(self._h, int(trans), m, n, alpha, _hp(a), a.size, _hp(x), x.size, beta,
+                                          _hp(y), y.size))
+
+    def hgemv(self, trans, m, n, alpha, a, x, beta, y):
+        """Handle::hgemv: host slices of f16 (np.float16 or uint16 bit
+        patterns).  alpha and beta are f16 values in the reference, so they
+        are rounded to f16 first and passed on as f32 (gemv.rs:648-649)."""
+        a, x, y = _host(a, np.uint16), _host(x, np.uint16), _host(y, np.uint16)
+        _check(self._lib.b2b_hgemv_simple(self._h, int(trans), m, n, float(np.float16(alpha)), _hp(a), a.size,
+                                          _hp(x), x.size, float(np.float16(beta)), _hp(y), y.size))
+
+    def hgemv_dev(self, trans, m, n, alpha, a, x, beta, y):
+        """Device-buffer HGEMV (f16 bit patterns, f32 alpha/beta)."""
+        xl, yl = (n, m) if int(trans) == 0 else (m, n)
+        if m and n:
+            self._need(a, m * n, "A", np.uint16)
+            self._need(x, xl, "x", np.uint16)
+            self._need(y, yl, "y", np.uint16)
+        _check(self._lib.b2b_hgemv(self._h, int(trans), m, n, alpha, ctypes.c_void_p(a.ptr),
+                                   ctypes.c_void_p(x.ptr), beta, ctypes.c_void_p(y.ptr)))
+
     # ---- Level 1: SAXPY (lib.rs:110-129)
     def saxpy(self, n, alpha, x, y):
         if n:
@@ -457,6 +490,77 @@ class Handle:
     def saxpy_simple(self, n, alpha, x, y):
         x, y = _host(x, np.float32), _host(y, np.float32)
         _check(self._lib.b2b_saxpy_simple(self._h, n, alpha, _hp(x), x.size, _hp(y), y.size))
+
+    # ---- Level 1 reductions (lib.rs:157-195)
+    class ReduceOp(enum.IntEnum):
+        Dot = 0
+        Nrm2 = 1
+        Asum = 2
+        Iamax = 3
+
+    def _reduce_dev(self, fn, n, x, y=None):
+        if n:
+            self._need(x, n, "x", np.float32)
+            if y is not None:
+                self._need(y, n, "y", np.float32)
+        out = ctypes.c_float()
+        args = [self._h, n, ctypes.c_void_p(x.ptr)] + ([ctypes.c_void_p(y.ptr)] if y is not None else [])
+        _check(fn(*args, ctypes.byref(out)))
+        return out.value
+
+    def _reduce_host(self, fn, n, x, y=None):
+        x = _host(x, np.float32)
+        args = [self._h, n, _hp(x), x.size]
+        if y is not None:
+            y = _host(y, np.float32)
+            args += [_hp(y), y.size]
+        out = ctypes.c_float()
+        _check(fn(*args, ctypes.byref(out)))
+        return out.value
+
+    def sdot(self, n, x, y) -> float:
+        return self._reduce_dev(self._lib.b2b_sdot, n, x, y)
+
+    def sdot_simple(self, n, x, y) -> float:
+        return self._reduce_host(self._lib.b2b_sdot_simple, n, x, y)
+
+    def snrm2(self, n, x) -> float:
+        return self._reduce_dev(self._lib.b2b_snrm2, n, x)
+
+    def snrm2_simple(self, n, x) -> float:
+        return self._reduce_host(self._lib.b2b_snrm2_simple, n, x)
+
+    def sasum(self, n, x) -> float:
+        return self._reduce_dev(self._lib.b2b_sasum, n, x)
+
+    def sasum_simple(self, n, x) -> float:
+        return self._reduce_host(self._lib.b2b_sasum_simple, n, x)
+
+    def isamax(self, n, x) -> int:
+        if n:
+            self._need(x, n, "x", np.float32)
+        out = ctypes.c_size_t()
+        _check(self._lib.b2b_isamax(self._h, n, ctypes.c_void_p(x.ptr), ctypes.byref(out)))
+        return out.value
+
+    def isamax_simple(self, n, x) -> int:
+        x = _host(x, np.float32)
+        out = ctypes.c_size_t()
+        _check(self._lib.b2b_isamax_simple(self._h, n, _hp(x), x.size, ctypes.byref(out)))
+        return out.value
+
+    def sreduce_async(self, op, n, x, y, result) -> None:
+        """Stream-ordered reduction into device memory: `result` is a float32
+        DeviceBuffer (Dot, Nrm2, Asum) or a uint64 one (Iamax)."""
+        want = np.uint64 if int(op) == 3 else np.float32
+        self._need(result, 1, "result", want)
+        if n:
+            self._need(x, n, "x", np.float32)
+            if int(op) == 0:
+                self._need(y, n, "y", np.float32)
+        _check(self._lib.b2b_sreduce_async(self._h, int(op), n, ctypes.c_void_p(x.ptr if x is not None else 0),
+                                           ctypes.c_void_p(y.ptr if y is not None else 0),
+                                           ctypes.c_void_p(result.ptr)))
 
     # ---- self-test of the bounded device waits
     def selftest_bounded_wait(self, limit_ns: int) -> None:

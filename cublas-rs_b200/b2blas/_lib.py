@@ -18,6 +18,7 @@ _i = ctypes.c_int
 _f = ctypes.c_float
 _d = ctypes.c_double
 _szp = ctypes.POINTER(ctypes.c_size_t)
+_fp = ctypes.POINTER(ctypes.c_float)
 _vpp = ctypes.POINTER(ctypes.c_void_p)
 
 # name -> (restype, argtypes); every entry point declared in include/b2blas.h.
@@ -53,6 +54,19 @@ SIGNATURES = {
     "b2b_sgemv": (_i, [_vp, _i, _i, _sz, _sz, _f, _vp, _vp, _f, _vp]),
     "b2b_sgemv_simple": (_i, [_vp, _i, _i, _sz, _sz, _f, _vp, _sz, _vp, _sz, _f, _vp, _sz]),
     "b2b_sgemv_noalloc": (_i, [_vp, _i, _sz, _sz, _f, _vp, _vp, _f, _vp]),
+    "b2b_dgemv": (_i, [_vp, _i, _sz, _sz, _d, _vp, _vp, _d, _vp]),
+    "b2b_dgemv_simple": (_i, [_vp, _i, _sz, _sz, _d, _vp, _sz, _vp, _sz, _d, _vp, _sz]),
+    "b2b_hgemv": (_i, [_vp, _i, _sz, _sz, _f, _vp, _vp, _f, _vp]),
+    "b2b_hgemv_simple": (_i, [_vp, _i, _sz, _sz, _f, _vp, _sz, _vp, _sz, _f, _vp, _sz]),
+    "b2b_sdot": (_i, [_vp, _sz, _vp, _vp, _fp]),
+    "b2b_sdot_simple": (_i, [_vp, _sz, _vp, _sz, _vp, _sz, _fp]),
+    "b2b_snrm2": (_i, [_vp, _sz, _vp, _fp]),
+    "b2b_snrm2_simple": (_i, [_vp, _sz, _vp, _sz, _fp]),
+    "b2b_sasum": (_i, [_vp, _sz, _vp, _fp]),
+    "b2b_sasum_simple": (_i, [_vp, _sz, _vp, _sz, _fp]),
+    "b2b_isamax": (_i, [_vp, _sz, _vp, _szp]),
+    "b2b_isamax_simple": (_i, [_vp, _sz, _vp, _sz, _szp]),
+    "b2b_sreduce_async": (_i, [_vp, _i, _sz, _vp, _vp, _vp]),
     "b2b_saxpy": (_i, [_vp, _sz, _f, _vp, _vp]),
     "b2b_saxpy_simple": (_i, [_vp, _sz, _f, _vp, _sz, _vp, _sz]),
     "b2b_panels_to_rowmajor": (_i, [_vp, _sz, _sz, _sz, _szp, _vp, _vp]),

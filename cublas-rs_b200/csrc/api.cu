@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string.h>
+
 #include <string>
 
 #include "internal.h"
@@ -113,6 +115,92 @@ int b2b_sgemv(b2b_handle *h, int algo, int trans, size_t m, size_t n, float alph
     if (!bytes_ok(m, n, 4)) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv: sizes overflow");
     DeviceGuard g(h);
     return launch_sgemv(h, trans, m, n, alpha, A, x, beta, y);
+}
+
+int b2b_dgemv(b2b_handle *h, int trans, size_t m, size_t n, double alpha, const double *A, const double *x,
+              double beta, double *y) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_dgemv: NULL handle");
+    if (trans != B2B_OP_N && trans != B2B_OP_T)
+        return fail(B2B_ERR_INVALID_ARG, "b2b_dgemv: trans must be B2B_OP_N or B2B_OP_T");
+    if (m == 0 || n == 0) return B2B_OK;  // gemv.rs:458-460
+    if (!A || !x || !y) return fail(B2B_ERR_INVALID_ARG, "b2b_dgemv: NULL operand");
+    if (!bytes_ok(m, n, 8)) return fail(B2B_ERR_INVALID_ARG, "b2b_dgemv: sizes overflow");
+    DeviceGuard g(h);
+    return launch_dgemv(h, trans, m, n, alpha, A, x, beta, y);
+}
+
+int b2b_hgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const uint16_t *A, const uint16_t *x,
+              float beta, uint16_t *y) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_hgemv: NULL handle");
+    if (trans != B2B_OP_N && trans != B2B_OP_T)
+        return fail(B2B_ERR_INVALID_ARG, "b2b_hgemv: trans must be B2B_OP_N or B2B_OP_T");
+    if (m == 0 || n == 0) return B2B_OK;
+    if (!A || !x || !y) return fail(B2B_ERR_INVALID_ARG, "b2b_hgemv: NULL operand");
+    if (!bytes_ok(m, n, 2)) return fail(B2B_ERR_INVALID_ARG, "b2b_hgemv: sizes overflow");
+    DeviceGuard g(h);
+    return launch_hgemv(h, trans, m, n, alpha, A, x, beta, y);
+}
+
+int b2b_sreduce_async(b2b_handle *h, int op, size_t n, const float *x, const float *y, void *d_result) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_sreduce_async: NULL handle");
+    if (op < B2B_REDUCE_DOT || op > B2B_REDUCE_IAMAX)
+        return fail(B2B_ERR_INVALID_ARG, "b2b_sreduce_async: unknown op " + std::to_string(op));
+    if (!d_result) return fail(B2B_ERR_INVALID_ARG, "b2b_sreduce_async: NULL result");
+    if (!bytes_ok(n, 1, 4)) return fail(B2B_ERR_INVALID_ARG, "b2b_sreduce_async: size overflows");
+    DeviceGuard g(h);
+    if (n == 0) {
+        const cudaError_t e = cudaMemsetAsync(d_result, 0, op == B2B_REDUCE_IAMAX ? 8 : 4, h->stream);
+        return e == cudaSuccess ? B2B_OK : fail_cuda(e, "b2b_sreduce_async: memset");
+    }
+    if (!x || (op == B2B_REDUCE_DOT && !y)) return fail(B2B_ERR_INVALID_ARG, "b2b_sreduce_async: NULL operand");
+    return launch_sreduce(h, op, n, x, y, d_result);
+}
+
+namespace {
+
+// Blocking flavour: reduce into the handle's result slot, copy it out on the
+// handle's stream and wait (the reference's *_dev functions return the value,
+// dot.rs:75-77).
+int reduce_to_host(b2b_handle *h, const char *fn, int op, size_t n, const float *x, const float *y, void *result) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");
+    if (!result) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL result");
+    const size_t rb = op == B2B_REDUCE_IAMAX ? 8 : 4;
+    if (n == 0) {  // dot.rs:66-68
+        memset(result, 0, rb);
+        return B2B_OK;
+    }
+    if (!x || (op == B2B_REDUCE_DOT && !y)) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL operand");
+    if (!bytes_ok(n, 1, 4)) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": size overflows");
+    DeviceGuard g(h);
+    void *slot = reinterpret_cast<char *>(h->d_status) + B2B_STATUS_REDUCE_RESULT;
+    if (int rc = launch_sreduce(h, op, n, x, y, slot)) return rc;
+    uint64_t v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, slot, rb, cudaMemcpyDeviceToHost, h->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+    if (e != cudaSuccess) return fail_cuda(e, (std::string(fn) + ": result copy").c_str());
+    memcpy(result, &v, rb);
+    return B2B_OK;
+}
+
+}  // namespace
+
+int b2b_sdot(b2b_handle *h, size_t n, const float *x, const float *y, float *result) {
+    return reduce_to_host(h, "b2b_sdot", B2B_REDUCE_DOT, n, x, y, result);
+}
+
+int b2b_snrm2(b2b_handle *h, size_t n, const float *x, float *result) {
+    return reduce_to_host(h, "b2b_snrm2", B2B_REDUCE_NRM2, n, x, nullptr, result);
+}
+
+int b2b_sasum(b2b_handle *h, size_t n, const float *x, float *result) {
+    return reduce_to_host(h, "b2b_sasum", B2B_REDUCE_ASUM, n, x, nullptr, result);
+}
+
+int b2b_isamax(b2b_handle *h, size_t n, const float *x, size_t *result) {
+    uint64_t r = 0;
+    const int rc = reduce_to_host(h, "b2b_isamax", B2B_REDUCE_IAMAX, n, x, nullptr, result ? &r : nullptr);
+    if (rc == B2B_OK) *result = static_cast<size_t>(r);
+    return rc;
 }
 
 int b2b_saxpy(b2b_handle *h, size_t n, float alpha, const float *x, float *y) {

@@ -330,6 +330,109 @@ int b2b_sgemv_simple(b2b_handle *h, int algo, int trans, size_t m, size_t n, flo
     return finish(h);
 }
 
+}  // extern "C"
+
+namespace {
+
+// dgemv / hgemv host launchers (gemv.rs:478-509, 619-673): A exactly m*n,
+// x and y at least their op lengths, zero dims return after the checks;
+// only the first x_len / y_len elements travel.
+template <typename T, typename S, typename Launch>
+int gemv_simple(b2b_handle *h, const char *fn, int trans, size_t m, size_t n, S alpha, const T *A, size_t a_len,
+                const T *x, size_t x_len, S beta, T *y, size_t y_len, Launch launch) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");
+    if (trans != B2B_OP_N && trans != B2B_OP_T)
+        return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": trans must be B2B_OP_N or B2B_OP_T");
+    if (a_len != m * n) return dim_err(fn, "A length (m*n)", m * n, a_len);
+    const size_t xl = trans == B2B_OP_N ? n : m, yl = trans == B2B_OP_N ? m : n;
+    if (x_len < xl) return dim_err(fn, "x length", xl, x_len);
+    if (y_len < yl) return dim_err(fn, "y length", yl, y_len);
+    if (m == 0 || n == 0) return B2B_OK;
+    if (!A || !x || !y) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL slice");
+    DeviceGuard g(h);
+    const size_t ea = m * n * sizeof(T), ex = xl * sizeof(T), ey = yl * sizeof(T);
+    const size_t ox = round_up(ea, 256), oy = ox + round_up(ex, 256);
+    void *stage = nullptr;
+    int rc = staging(h, oy + round_up(ey, 256), &stage);
+    if (rc) return rc;
+    T *dA = static_cast<T *>(stage);
+    T *dx = reinterpret_cast<T *>(static_cast<char *>(stage) + ox);
+    T *dy = reinterpret_cast<T *>(static_cast<char *>(stage) + oy);
+    if ((rc = h2d(h, dA, A, ea)) || (rc = h2d(h, dx, x, ex))) return rc;
+    if (beta != S(0) && (rc = h2d(h, dy, y, ey))) return rc;
+    if ((rc = launch(h, trans, m, n, alpha, dA, dx, beta, dy))) return rc;
+    if ((rc = d2h(h, y, dy, ey))) return rc;
+    return finish(h);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2b_dgemv_simple(b2b_handle *h, int trans, size_t m, size_t n, double alpha, const double *A, size_t a_len,
+                     const double *x, size_t x_len, double beta, double *y, size_t y_len) {
+    return gemv_simple(h, "b2b_dgemv_simple", trans, m, n, alpha, A, a_len, x, x_len, beta, y, y_len, launch_dgemv);
+}
+
+int b2b_hgemv_simple(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const uint16_t *A, size_t a_len,
+                     const uint16_t *x, size_t x_len, float beta, uint16_t *y, size_t y_len) {
+    return gemv_simple(h, "b2b_hgemv_simple", trans, m, n, alpha, A, a_len, x, x_len, beta, y, y_len, launch_hgemv);
+}
+
+// sdot / snrm2 / sasum / isamax host launchers (dot.rs:81-96, nrm2.rs:75-87,
+// asum.rs:74-86, iamax.rs:88-100): x (and y) at least n long, n == 0 gives
+// 0 after the checks, only x[..n] (y[..n]) travel.
+static int reduce_simple(b2b_handle *h, const char *fn, int op, size_t n, const float *x, size_t x_len,
+                         const float *y, size_t y_len, void *result) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");
+    if (!result) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL result");
+    if (x_len < n) return dim_err(fn, "x length (>= n)", n, x_len);
+    if (op == B2B_REDUCE_DOT && y_len < n) return dim_err(fn, "y length (>= n)", n, y_len);
+    const size_t rb = op == B2B_REDUCE_IAMAX ? 8 : 4;
+    if (n == 0) {
+        memset(result, 0, rb);
+        return B2B_OK;
+    }
+    if (!x || (op == B2B_REDUCE_DOT && !y)) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL slice");
+    DeviceGuard g(h);
+    const size_t oy = round_up(n * 4, 256), ores = oy + (op == B2B_REDUCE_DOT ? round_up(n * 4, 256) : 0);
+    void *stage = nullptr;
+    int rc = staging(h, ores + 256, &stage);
+    if (rc) return rc;
+    float *dx = static_cast<float *>(stage);
+    float *dy = reinterpret_cast<float *>(static_cast<char *>(stage) + oy);
+    void *dres = static_cast<char *>(stage) + ores;
+    if ((rc = h2d(h, dx, x, n * 4))) return rc;
+    if (op == B2B_REDUCE_DOT && (rc = h2d(h, dy, y, n * 4))) return rc;
+    if ((rc = launch_sreduce(h, op, n, dx, op == B2B_REDUCE_DOT ? dy : nullptr, dres))) return rc;
+    uint64_t v = 0;
+    if ((rc = d2h(h, &v, dres, rb))) return rc;
+    if ((rc = finish(h))) return rc;
+    memcpy(result, &v, rb);
+    return B2B_OK;
+}
+
+int b2b_sdot_simple(b2b_handle *h, size_t n, const float *x, size_t x_len, const float *y, size_t y_len,
+                    float *result) {
+    return reduce_simple(h, "b2b_sdot_simple", B2B_REDUCE_DOT, n, x, x_len, y, y_len, result);
+}
+
+int b2b_snrm2_simple(b2b_handle *h, size_t n, const float *x, size_t x_len, float *result) {
+    return reduce_simple(h, "b2b_snrm2_simple", B2B_REDUCE_NRM2, n, x, x_len, nullptr, 0, result);
+}
+
+int b2b_sasum_simple(b2b_handle *h, size_t n, const float *x, size_t x_len, float *result) {
+    return reduce_simple(h, "b2b_sasum_simple", B2B_REDUCE_ASUM, n, x, x_len, nullptr, 0, result);
+}
+
+int b2b_isamax_simple(b2b_handle *h, size_t n, const float *x, size_t x_len, size_t *result) {
+    uint64_t r = 0;
+    const int rc =
+        reduce_simple(h, "b2b_isamax_simple", B2B_REDUCE_IAMAX, n, x, x_len, nullptr, 0, result ? &r : nullptr);
+    if (rc == B2B_OK) *result = static_cast<size_t>(r);
+    return rc;
+}
+
 int b2b_saxpy_simple(b2b_handle *h, size_t n, float alpha, const float *x, size_t x_len, float *y, size_t y_len) {
     const char *fn = "b2b_saxpy_simple";
     if (!h) return fail(B2B_ERR_INVALID_ARG, std::string(fn) + ": NULL handle");

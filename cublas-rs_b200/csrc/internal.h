@@ -13,6 +13,12 @@
 // Device status word values written by kernels whose waits are bounded.
 // The low byte names the wait that gave up.
 #define B2B_DEVSTAT_TIMEOUT 0x100
+// Layout of the handle's 256-byte device status block (zeroed at creation):
+//   byte   0: int status word (bounded-wait timeouts)
+//   byte  64: unsigned reduction ticket counter (back to 0 after each reduction)
+//   byte 128: 8-byte result slot of the blocking reductions
+#define B2B_STATUS_REDUCE_COUNTER 64
+#define B2B_STATUS_REDUCE_RESULT 128
 
 struct b2b_handle {
     int device = 0;
@@ -20,7 +26,7 @@ struct b2b_handle {
     int sm_clock_khz = 0;
     cudaStream_t own_stream = nullptr;  // created by b2b_create
     cudaStream_t stream = nullptr;      // where work is issued (own or caller's)
-    int *d_status = nullptr;            // device status word (bounded-wait timeouts)
+    int *d_status = nullptr;            // device status block (layout above)
     // Grow-only device scratch for kernels that need it (split reductions).
     void *workspace = nullptr;
     size_t workspace_bytes = 0;
@@ -100,6 +106,11 @@ int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alp
                       const double *B, double *C);
 int launch_sgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A, const float *x,
                  float beta, float *y);
+int launch_sreduce(b2b_handle *h, int op, size_t n, const float *x, const float *y, void *d_out);
+int launch_dgemv(b2b_handle *h, int trans, size_t m, size_t n, double alpha, const double *A, const double *x,
+                 double beta, double *y);
+int launch_hgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const uint16_t *A, const uint16_t *x,
+                 float beta, uint16_t *y);
 int launch_saxpy(b2b_handle *h, size_t n, float alpha, const float *x, float *y);
 int launch_panels_to_rowmajor(b2b_handle *h, size_t elem_bytes, size_t m, size_t g, const size_t *widths,
                               const void *panels, void *C);

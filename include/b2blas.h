@@ -213,6 +213,29 @@ B2B_API int b2b_sgemv_simple(b2b_handle *h, int algo, int trans, size_t m, size_
 B2B_API int b2b_sgemv_noalloc(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A,
                               const float *x, float beta, float *y);
 
+/* ------------------------------------------------ Level 2: DGEMV, HGEMV */
+
+/* Handle::dgemv (lib.rs:312-324) -> cublas_l2::dgemv_dev
+ * (crates/cublas-l2/src/gemv.rs:446-471): y <- alpha*op(A)*x + beta*y in
+ * f64, A m x n row-major, op as in b2b_sgemv.  Device pointers. */
+B2B_API int b2b_dgemv(b2b_handle *h, int trans, size_t m, size_t n, double alpha, const double *A,
+                      const double *x, double beta, double *y);
+/* Handle::dgemv_simple (lib.rs:327-339) -> gemv.rs:478-509 (A length must
+ * equal m*n; x, y at least their op lengths). */
+B2B_API int b2b_dgemv_simple(b2b_handle *h, int trans, size_t m, size_t n, double alpha, const double *A,
+                             size_t a_len, const double *x, size_t x_len, double beta, double *y, size_t y_len);
+/* Device-pointer HGEMV.  The reference has the host-slice flavour only
+ * (lib.rs:341-343); this one is its kernel step.  f16 bit patterns, f32
+ * accumulate, f16 result rounded to nearest even; alpha/beta as f32. */
+B2B_API int b2b_hgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const uint16_t *A,
+                      const uint16_t *x, float beta, uint16_t *y);
+/* Handle::hgemv (lib.rs:344-366) -> cublas_l2::hgemv (gemv.rs:619-673):
+ * host slices of f16 bit patterns; alpha/beta are the f32 values the
+ * reference passes its kernels (alpha.to_f32(), gemv.rs:648-649). */
+B2B_API int b2b_hgemv_simple(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const uint16_t *A,
+                             size_t a_len, const uint16_t *x, size_t x_len, float beta, uint16_t *y,
+                             size_t y_len);
+
 /* -------------------------------------------------------- Level 1: SAXPY */
 
 /* Handle::saxpy (lib.rs:110-118) -> crates/cublas-l1/src/saxpy.rs:25-40:
@@ -221,6 +244,43 @@ B2B_API int b2b_saxpy(b2b_handle *h, size_t n, float alpha, const float *x, floa
 /* Handle::saxpy_simple (lib.rs:121-129) -> saxpy.rs:45-66 (x, y at least n). */
 B2B_API int b2b_saxpy_simple(b2b_handle *h, size_t n, float alpha, const float *x, size_t x_len, float *y,
                              size_t y_len);
+
+/* ------------------------------------------------- Level 1: reductions
+ * One multi-block launch each, f64 accumulation, deterministic order (the
+ * reference runs one 32-thread block, crates/cublas-l1/src/dot.rs:21-53).
+ * The device-buffer flavours take device x/y, write the result to a host
+ * pointer and block until it is there, as the reference's *_dev functions
+ * return a host value (dot.rs:59-78).  n == 0 gives 0.  The host flavours
+ * check x_len/y_len >= n and copy only the first n elements (dot.rs:81-96). */
+typedef enum b2b_reduce_op {
+    B2B_REDUCE_DOT = 0,   /* sum x[i]*y[i]                     (f32 result) */
+    B2B_REDUCE_NRM2 = 1,  /* sqrt(sum x[i]^2)                  (f32 result) */
+    B2B_REDUCE_ASUM = 2,  /* sum |x[i]|                        (f32 result) */
+    B2B_REDUCE_IAMAX = 3  /* smallest 0-based i of max |x[i]|  (uint64 result) */
+} b2b_reduce_op;
+
+/* Handle::sdot / sdot_simple (lib.rs:157-165) -> dot.rs:59-96. */
+B2B_API int b2b_sdot(b2b_handle *h, size_t n, const float *x, const float *y, float *result);
+B2B_API int b2b_sdot_simple(b2b_handle *h, size_t n, const float *x, size_t x_len, const float *y, size_t y_len,
+                            float *result);
+/* Handle::snrm2 / snrm2_simple (lib.rs:167-175) -> nrm2.rs:54-87.  The sum
+ * of squares is kept in f64, so no finite input overflows it. */
+B2B_API int b2b_snrm2(b2b_handle *h, size_t n, const float *x, float *result);
+B2B_API int b2b_snrm2_simple(b2b_handle *h, size_t n, const float *x, size_t x_len, float *result);
+/* Handle::sasum / sasum_simple (lib.rs:177-185) -> asum.rs:53-86. */
+B2B_API int b2b_sasum(b2b_handle *h, size_t n, const float *x, float *result);
+B2B_API int b2b_sasum_simple(b2b_handle *h, size_t n, const float *x, size_t x_len, float *result);
+/* Handle::isamax / isamax_simple (lib.rs:187-195) -> iamax.rs:67-100.
+ * Ties give the smallest index; NaN elements never win; all-NaN gives 0. */
+B2B_API int b2b_isamax(b2b_handle *h, size_t n, const float *x, size_t *result);
+B2B_API int b2b_isamax_simple(b2b_handle *h, size_t n, const float *x, size_t x_len, size_t *result);
+/* Stream-ordered reduction whose result stays on the device: d_result is a
+ * float (DOT, NRM2, ASUM) or a uint64_t (IAMAX) in device memory, written
+ * when the launch completes; the call returns without waiting.  No reference
+ * counterpart.  y is read by DOT only.  Reductions on one handle share a
+ * counter and partial-sum workspace, so they must not run concurrently on
+ * different streams through the same handle. */
+B2B_API int b2b_sreduce_async(b2b_handle *h, int op, size_t n, const float *x, const float *y, void *d_result);
 
 /* --------------------------------------------- multi-GPU column sharding
  * No reference counterpart (the reference is single-device,

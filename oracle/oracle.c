@@ -17,7 +17,11 @@
  *       :116-124 (epilogue)
  *   - strided batched: base offsets batch*stride, crates/cublas-l3/src/batched.rs:55-58,95-100
  *   - GEMV N / T index formulas, crates/cublas-l2/src/gemv.rs:28-81
+ *   - DGEMV (f64) and HGEMV (f16 in/out, f32 accumulate, the same
+ *     conversions as HGEMM), crates/cublas-l2/src/gemv.rs:386-437, :553-606
  *   - SAXPY y = alpha*x + y, crates/cublas-l1/src/saxpy.rs:14-19
+ *   - SDOT / SNRM2 / SASUM / ISAMAX, crates/cublas-l1/src/dot.rs:21-53,
+ *     nrm2.rs:16-48, asum.rs:15-47, iamax.rs:16-61
  *
  * The reference's device arithmetic is produced by cuda-oxide (git rev
  * 396c76aaca11de3a49c982afd94069dbbc1cb8ef, Cargo.lock:161-183), which is not
@@ -288,6 +292,96 @@ void oracle_sgemv_f64(int trans, size_t m, size_t n, double alpha, const float *
     }
 }
 
+/* DGEMV, crates/cublas-l2/src/gemv.rs:386-437 (same shapes as SGEMV), with
+ * each dot product evaluated by Ogita-Rump-Oishi Dot2 (error-free
+ * TwoProduct through fma plus TwoSum; "Accurate sum and dot product", SIAM J.
+ * Sci. Comput. 26(6), 2005), so the oracle's own rounding error is about
+ * eps_f64 * |y| + eps_f64^2 * sum |a x| and the parity bound measures the
+ * kernel alone.  beta == 0 ignores y. */
+static void dot2_acc(double *s, double *c, double a, double b) {
+    double p = a * b;
+    double pe = fma(a, b, -p);
+    double t = *s + p;
+    double z = t - *s;
+    double se = (*s - (t - z)) + (p - z);
+    *s = t;
+    *c += pe + se;
+}
+
+void oracle_dgemv_f64(int trans, size_t m, size_t n, double alpha, const double *A, const double *x, double beta,
+                      const double *y, double *out) {
+    if (!trans) {
+#pragma omp parallel for schedule(static)
+        for (long ii = 0; ii < (long)m; ++ii) {
+            size_t i = (size_t)ii;
+            double s = 0.0, c = 0.0;
+            for (size_t j = 0; j < n; ++j) dot2_acc(&s, &c, A[i * n + j], x[j]);
+            out[i] = alpha * (s + c) + (beta != 0.0 ? beta * y[i] : 0.0);
+        }
+    } else {
+#pragma omp parallel for schedule(static)
+        for (long jj = 0; jj < (long)n; ++jj) {
+            size_t j = (size_t)jj;
+            double s = 0.0, c = 0.0;
+            for (size_t i = 0; i < m; ++i) dot2_acc(&s, &c, A[i * n + j], x[i]);
+            out[j] = alpha * (s + c) + (beta != 0.0 ? beta * y[j] : 0.0);
+        }
+    }
+}
+
+/* HGEMV in f64 from the exact f16 inputs (gemv.rs:553-606 shapes):
+ * out = alpha*op(A)x + beta*y, unrounded. */
+void oracle_hgemv_f64(int trans, size_t m, size_t n, double alpha, const uint16_t *A, const uint16_t *x,
+                      double beta, const uint16_t *y, double *out) {
+    size_t len = trans ? n : m;
+#pragma omp parallel for schedule(static)
+    for (long oo = 0; oo < (long)len; ++oo) {
+        size_t o = (size_t)oo;
+        double s = 0.0, c = 0.0;
+        if (!trans)
+            for (size_t j = 0; j < n; ++j) dot2_acc(&s, &c, oracle_f16_to_f64(A[o * n + j]), oracle_f16_to_f64(x[j]));
+        else
+            for (size_t i = 0; i < m; ++i) dot2_acc(&s, &c, oracle_f16_to_f64(A[i * n + o]), oracle_f16_to_f64(x[i]));
+        out[o] = alpha * (s + c) + (beta != 0.0 ? beta * oracle_f16_to_f64(y[o]) : 0.0);
+    }
+}
+
+/* Level-1 reductions in f64 (crates/cublas-l1/src/dot.rs:21-53,
+ * nrm2.rs:16-48, asum.rs:15-47), each sum Dot2-compensated so the oracle is
+ * accurate to about eps_f64 of the result. */
+double oracle_sdot_f64(size_t n, const float *x, const float *y) {
+    double s = 0.0, c = 0.0;
+    for (size_t i = 0; i < n; ++i) dot2_acc(&s, &c, x[i], y[i]);
+    return s + c;
+}
+
+double oracle_snrm2_f64(size_t n, const float *x) {
+    double s = 0.0, c = 0.0;
+    for (size_t i = 0; i < n; ++i) dot2_acc(&s, &c, x[i], x[i]);
+    return sqrt(s + c);
+}
+
+double oracle_sasum_f64(size_t n, const float *x) {
+    double s = 0.0, c = 0.0;
+    for (size_t i = 0; i < n; ++i) dot2_acc(&s, &c, fabs((double)x[i]), 1.0);
+    return s + c;
+}
+
+/* ISAMAX as the BLAS defines it: the smallest index of the largest |x[i]|.
+ * NaN never compares greater (as in iamax.rs:26-31); all-NaN or n == 0 -> 0. */
+size_t oracle_isamax(size_t n, const float *x) {
+    float best = -1.0f;
+    size_t idx = 0;
+    for (size_t i = 0; i < n; ++i) {
+        float a = fabsf(x[i]);
+        if (a > best) {
+            best = a;
+            idx = i;
+        }
+    }
+    return idx;
+}
+
 /* SAXPY, crates/cublas-l1/src/saxpy.rs:14-19 */
 void oracle_saxpy_f64(size_t n, double alpha, const float *x, const float *y, double *out) {
     for (size_t i = 0; i < n; ++i) out[i] = alpha * (double)x[i] + (double)y[i];
@@ -329,6 +423,74 @@ void oracle_hgemm_ref(size_t m, size_t n, size_t k, float alpha, const uint16_t 
             C[i * n + j] = oracle_ref_f32_to_f16(alpha * sum + beta * cur);
         }
     }
+}
+
+/* The reference's HGEMV arithmetic (gemv.rs:553-606): flushing decode, f32
+ * accumulate in index order, f32_to_f16(alpha*sum + beta*f16_to_f32(y)) with
+ * the truncating encode.  y is updated in place. */
+void oracle_hgemv_ref(int trans, size_t m, size_t n, float alpha, const uint16_t *A, const uint16_t *x, float beta,
+                      uint16_t *y) {
+    size_t len = trans ? n : m;
+    for (size_t o = 0; o < len; ++o) {
+        float sum = 0.0f;
+        if (!trans)
+            for (size_t j = 0; j < n; ++j) sum += oracle_ref_f16_to_f32(A[o * n + j]) * oracle_ref_f16_to_f32(x[j]);
+        else
+            for (size_t i = 0; i < m; ++i) sum += oracle_ref_f16_to_f32(A[i * n + o]) * oracle_ref_f16_to_f32(x[i]);
+        float cur = oracle_ref_f16_to_f32(y[o]);
+        y[o] = oracle_ref_f32_to_f16(alpha * sum + beta * cur);
+    }
+}
+
+/* The reference's reduction arithmetic: 32 lanes, lane t visits i = t,
+ * t+32, ... accumulating in f32, then the shared-memory tree for stride 16,
+ * 8, 4, 2, 1 adds slot t+stride into slot t (dot.rs:24-45; nrm2.rs and
+ * asum.rs likewise; nrm2's sqrt is taken on the host in f32, nrm2.rs:69-70).
+ * op: 0 dot, 1 sum of squares then sqrt, 2 sum of |x|. */
+float oracle_sreduce_ref(int op, size_t n, const float *x, const float *y) {
+    float lane[32];
+    for (size_t t = 0; t < 32; ++t) {
+        float acc = 0.0f;
+        for (size_t i = t; i < n; i += 32) {
+            float v = x[i];
+            float term = op == 0 ? v * y[i] : op == 1 ? v * v : (v < 0.0f ? -v : v);
+            acc += term;
+        }
+        lane[t] = acc;
+    }
+    for (size_t stride = 16; stride > 0; stride /= 2)
+        for (size_t t = 0; t < stride; ++t) lane[t] += lane[t + stride];
+    return op == 1 ? sqrtf(lane[0]) : lane[0];
+}
+
+/* The reference's ISAMAX (iamax.rs:16-61): per lane the first index of its
+ * largest |x| (strict >, start value -1, index 0), then the tree keeps the
+ * higher slot only when strictly greater.  With ties across lanes the
+ * winner is decided by lane position, not by index. */
+size_t oracle_isamax_ref(size_t n, const float *x) {
+    float val[32];
+    uint32_t idx[32];
+    for (size_t t = 0; t < 32; ++t) {
+        float bv = -1.0f;
+        uint32_t bi = 0;
+        for (size_t i = t; i < n; i += 32) {
+            float v = x[i];
+            float av = v < 0.0f ? -v : v;
+            if (av > bv) {
+                bv = av;
+                bi = (uint32_t)i;
+            }
+        }
+        val[t] = bv;
+        idx[t] = bi;
+    }
+    for (size_t stride = 16; stride > 0; stride /= 2)
+        for (size_t t = 0; t < stride; ++t)
+            if (val[t + stride] > val[t]) {
+                val[t] = val[t + stride];
+                idx[t] = idx[t + stride];
+            }
+    return idx[0];
 }
 
 /* ------------------------------------------------------------ error norms */
@@ -448,4 +610,40 @@ void oracle_cpu_sgemv_n(size_t rows, size_t n, float alpha, const float *A, cons
         for (size_t j = 0; j < n; ++j) s += A[i * n + j] * x[j];
         y[i] = alpha * s + beta * y[i];
     }
+}
+
+/* DGEMV N rows, the reference's f64 loop (gemv.rs:386-410), one row per
+ * iteration across threads. */
+void oracle_cpu_dgemv_n(size_t rows, size_t n, double alpha, const double *A, const double *x, double beta,
+                        double *y) {
+#pragma omp parallel for schedule(static)
+    for (long ii = 0; ii < (long)rows; ++ii) {
+        size_t i = (size_t)ii;
+        double s = 0.0;
+        for (size_t j = 0; j < n; ++j) s += A[i * n + j] * x[j];
+        y[i] = alpha * s + beta * y[i];
+    }
+}
+
+/* HGEMV N rows with the reference's arithmetic (gemv.rs:553-577): x is
+ * decoded once into xf (n floats), A row by row. */
+void oracle_cpu_hgemv_n(size_t rows, size_t n, float alpha, const uint16_t *A, const uint16_t *x, float beta,
+                        uint16_t *y, float *xf) {
+    for (size_t j = 0; j < n; ++j) xf[j] = oracle_ref_f16_to_f32(x[j]);
+#pragma omp parallel for schedule(static)
+    for (long ii = 0; ii < (long)rows; ++ii) {
+        size_t i = (size_t)ii;
+        float s = 0.0f;
+        for (size_t j = 0; j < n; ++j) s += oracle_ref_f16_to_f32(A[i * n + j]) * xf[j];
+        y[i] = oracle_ref_f32_to_f16(alpha * s + beta * oracle_ref_f16_to_f32(y[i]));
+    }
+}
+
+/* SDOT over all threads: per-thread f32 partial sums (the reference's
+ * per-lane f32 accumulation, dot.rs:27-31), added at the end. */
+float oracle_cpu_sdot(size_t n, const float *x, const float *y) {
+    float acc = 0.0f;
+#pragma omp parallel for schedule(static) reduction(+ : acc)
+    for (long i = 0; i < (long)n; ++i) acc += x[i] * y[i];
+    return acc;
 }

@@ -77,7 +77,16 @@ def lib():
         "oracle_sgemm_strided_batched_f64": (
             None, [_sz, _sz, _sz, _d, _f32p, _sz, _f32p, _sz, _d, ctypes.c_void_p, _sz, _sz, _f64p]),
         "oracle_sgemv_f64": (None, [ctypes.c_int, _sz, _sz, _d, _f32p, _f32p, _d, _f32p, _f64p]),
+        "oracle_dgemv_f64": (None, [ctypes.c_int, _sz, _sz, _d, _f64p, _f64p, _d, _f64p, _f64p]),
+        "oracle_hgemv_f64": (None, [ctypes.c_int, _sz, _sz, _d, _u16p, _u16p, _d, _u16p, _f64p]),
+        "oracle_hgemv_ref": (None, [ctypes.c_int, _sz, _sz, _f, _u16p, _u16p, _f, _u16p]),
         "oracle_saxpy_f64": (None, [_sz, _d, _f32p, _f32p, _f64p]),
+        "oracle_sdot_f64": (_d, [_sz, _f32p, _f32p]),
+        "oracle_snrm2_f64": (_d, [_sz, _f32p]),
+        "oracle_sasum_f64": (_d, [_sz, _f32p]),
+        "oracle_isamax": (_sz, [_sz, _f32p]),
+        "oracle_sreduce_ref": (_f, [ctypes.c_int, _sz, _f32p, ctypes.c_void_p]),
+        "oracle_isamax_ref": (_sz, [_sz, _f32p]),
         "oracle_sgemm_ref_f32": (None, [_sz, _sz, _sz, _f, _f32p, _f32p, _f, _f32p]),
         "oracle_hgemm_ref": (None, [_sz, _sz, _sz, _f, _u16p, _u16p, _f, _u16p]),
         "oracle_rel_fro_err_f32": (_d, [_f32p, _f64p, _sz]),
@@ -89,6 +98,9 @@ def lib():
         "oracle_cpu_dgemm_ikj": (None, [_sz, _sz, _sz, _d, _f64p, _f64p, _d, _f64p, _f64p]),
         "oracle_cpu_hgemm_ikj": (None, [_sz, _sz, _sz, _f, _u16p, _u16p, _f, _u16p, _f32p, _f32p]),
         "oracle_cpu_sgemv_n": (None, [_sz, _sz, _f, _f32p, _f32p, _f, _f32p]),
+        "oracle_cpu_dgemv_n": (None, [_sz, _sz, _d, _f64p, _f64p, _d, _f64p]),
+        "oracle_cpu_hgemv_n": (None, [_sz, _sz, _f, _u16p, _u16p, _f, _u16p, _f32p]),
+        "oracle_cpu_sdot": (_f, [_sz, _f32p, _f32p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -208,11 +220,44 @@ def sgemv_f64(trans: int, m, n, alpha, A, x, beta, y) -> np.ndarray:
     return out
 
 
+def dgemv_f64(trans: int, m, n, alpha, A, x, beta, y) -> np.ndarray:
+    """DGEMV with Dot2-compensated dot products (oracle error ~ eps_f64)."""
+    A, x, y = _c(A, np.float64).ravel(), _c(x, np.float64).ravel(), _c(y, np.float64).ravel()
+    out = np.empty(n if trans else m, np.float64)
+    lib().oracle_dgemv_f64(int(trans), m, n, alpha, A, x, beta, y, out)
+    return out
+
+
+def hgemv_f64(trans: int, m, n, alpha, A, x, beta, y) -> np.ndarray:
+    """HGEMV of f16 bit patterns, evaluated in f64 from the exact inputs."""
+    A, x, y = _c(A, np.uint16).ravel(), _c(x, np.uint16).ravel(), _c(y, np.uint16).ravel()
+    out = np.empty(n if trans else m, np.float64)
+    lib().oracle_hgemv_f64(int(trans), m, n, alpha, A, x, beta, y, out)
+    return out
+
+
 def saxpy_f64(n, alpha, x, y) -> np.ndarray:
     x, y = _c(x, np.float32).ravel(), _c(y, np.float32).ravel()
     out = np.empty(n, np.float64)
     lib().oracle_saxpy_f64(n, alpha, x, y, out)
     return out
+
+
+def sdot_f64(n, x, y) -> float:
+    return lib().oracle_sdot_f64(n, _c(x, np.float32).ravel(), _c(y, np.float32).ravel())
+
+
+def snrm2_f64(n, x) -> float:
+    return lib().oracle_snrm2_f64(n, _c(x, np.float32).ravel())
+
+
+def sasum_f64(n, x) -> float:
+    return lib().oracle_sasum_f64(n, _c(x, np.float32).ravel())
+
+
+def isamax(n, x) -> int:
+    """Smallest index of the largest |x[i]| (NaN skipped; 0 if none)."""
+    return lib().oracle_isamax(n, _c(x, np.float32).ravel())
 
 
 # ------------------------------------------- reference arithmetic (f32/f16)
@@ -227,6 +272,30 @@ def hgemm_ref(m, n, k, alpha, A, B, beta, C) -> np.ndarray:
     C = _c(C, np.uint16).ravel().copy()
     lib().oracle_hgemm_ref(m, n, k, alpha, _c(A, np.uint16).ravel(), _c(B, np.uint16).ravel(), beta, C)
     return C
+
+
+def hgemv_ref(trans: int, m, n, alpha, A, x, beta, y) -> np.ndarray:
+    """The reference's own HGEMV arithmetic (flushing decode, f32 sums,
+    truncating encode); returns the new y as f16 bit patterns."""
+    y = _c(y, np.uint16).ravel().copy()
+    lib().oracle_hgemv_ref(int(trans), m, n, alpha, _c(A, np.uint16).ravel(), _c(x, np.uint16).ravel(), beta, y)
+    return y
+
+
+def sreduce_ref(op: str, n, x, y=None) -> float:
+    """The reference's 32-lane f32 reduction (op 'dot', 'nrm2' or 'asum')."""
+    code = {"dot": 0, "nrm2": 1, "asum": 2}[op]
+    x = _c(x, np.float32).ravel()
+    yp = None
+    if code == 0:
+        y = _c(y, np.float32).ravel()
+        yp = y.ctypes.data
+    return lib().oracle_sreduce_ref(code, n, x, yp)
+
+
+def isamax_ref(n, x) -> int:
+    """The reference's ISAMAX, tie order included."""
+    return lib().oracle_isamax_ref(n, _c(x, np.float32).ravel())
 
 
 # ------------------------------------------------------------------ norms
@@ -278,3 +347,15 @@ def cpu_hgemm_rows(rows, n, k, alpha, A, B, beta, C, bf_scratch, row_scratch) ->
 
 def cpu_sgemv_rows(rows, n, alpha, A, x, beta, y) -> None:
     lib().oracle_cpu_sgemv_n(rows, n, alpha, A, x, beta, y)
+
+
+def cpu_dgemv_rows(rows, n, alpha, A, x, beta, y) -> None:
+    lib().oracle_cpu_dgemv_n(rows, n, alpha, A, x, beta, y)
+
+
+def cpu_hgemv_rows(rows, n, alpha, A, x, beta, y, xf) -> None:
+    lib().oracle_cpu_hgemv_n(rows, n, alpha, A, x, beta, y, xf)
+
+
+def cpu_sdot(n, x, y) -> float:
+    return lib().oracle_cpu_sdot(n, x, y)

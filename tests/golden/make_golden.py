@@ -13,13 +13,16 @@ records them as data, each with the file:line it comes from, together with
 Run:  python tests/golden/make_golden.py   (rewrites the .json files here)
 """
 import json
+import math
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 KNOWN_ANSWERS = {
-    "about": "All-ones known answers from the cublas-rs example binaries: A = B = 1 (x = 1 for gemv), "
-             "so every output equals the inner dimension.",
+    "about": "Known answers from the cublas-rs example binaries.  GEMM/SGEMV cases are all-ones "
+             "(A = B = 1, x = 1), so every output equals the inner dimension; the HGEMV case is the "
+             "example's ramp, checked against an f32 sum of the same f16 values; the reductions use "
+             "x = [0, 1, ..., n-1], whose sums have closed forms.",
     "cases": [
         {"op": "sgemm", "variants": ["naive", "tiled", "vectorized", "double_buf"], "m": 512, "n": 512, "k": 512,
          "alpha": 1.0, "beta": 0.0, "expect": 512.0, "tol_abs": 1e-3,
@@ -46,6 +49,17 @@ KNOWN_ANSWERS = {
          "ref": "examples/saxpy/src/main.rs:88-106"},
         {"op": "sgemv", "trans": "T", "m": 16, "n": 24, "alpha": 1.0, "beta": 0.0, "expect": 16.0, "tol_abs": 1e-3,
          "ref": "examples/saxpy/src/main.rs:108-124"},
+        {"op": "hgemv", "trans": "N", "m": 16, "n": 24, "alpha": 1.0, "beta": 0.0,
+         "a": "f16 round-to-nearest of 0.01*i, i the flat index", "x": "f16 round-to-nearest of 0.1*j",
+         "expect": "f32 sum over j of f32(a[i,j]) * f32(x[j]) in j order", "tol_rel": 5e-3,
+         "ref": "examples/saxpy/src/main.rs:132-172 (tolerance :160)"},
+        {"op": "sdot", "n": 1024, "x": "i", "y": "i", "expect": 357389824.0, "tol_rel": 1e-3,
+         "ref": "examples/saxpy/src/main.rs:12-14,39,44,48-56 (sum of i^2 = (n-1)n(2n-1)/6)"},
+        {"op": "snrm2", "n": 1024, "x": "i", "expect": math.sqrt(357389824.0),
+         "tol_rel": 1e-3, "ref": "examples/saxpy/src/main.rs:40,45,57"},
+        {"op": "sasum", "n": 1024, "x": "i", "expect": 523776.0, "tol_rel": 1e-3,
+         "ref": "examples/saxpy/src/main.rs:41,46,58 (sum of i = n(n-1)/2)"},
+        {"op": "isamax", "n": 1024, "x": "i", "expect": 1023, "ref": "examples/saxpy/src/main.rs:42,59-63"},
     ],
 }
 

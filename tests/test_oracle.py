@@ -57,14 +57,33 @@ def test_rne_f16_matches_numpy(oracle):
     assert np.array_equal(got, want[::7])
 
 
+def hgemv_ramp(m, n):
+    """The saxpy example's HGEMV inputs: a[i] = f16(0.01 i), x[j] = f16(0.1 j)
+    (examples/saxpy/src/main.rs:133-137), as f16 bit patterns."""
+    a16 = (np.arange(m * n, dtype=np.float32) * np.float32(0.01)).astype(np.float16).view(np.uint16)
+    x16 = (np.arange(n, dtype=np.float32) * np.float32(0.1)).astype(np.float16).view(np.uint16)
+    return a16, x16
+
+
+def hgemv_ramp_expect(a16, x16, m, n):
+    """The example's check value: f32 sum in j order of the f16 products
+    (examples/saxpy/src/main.rs:151-157)."""
+    a = a16.view(np.float16).astype(np.float32).reshape(m, n)
+    x = x16.view(np.float16).astype(np.float32)
+    out = np.zeros(m, np.float32)
+    for j in range(n):
+        out += a[:, j] * x[j]
+    return out
+
+
 def _ones(n, dt=np.float32):
     return np.ones(n, dt)
 
 
 @pytest.mark.parametrize("case", [c for c in load_golden("known_answers.json")["cases"]],
-                         ids=lambda c: f"{c['op']}-{c['m']}x{c['n']}")
+                         ids=lambda c: f"{c['op']}-{c.get('m', 1)}x{c['n']}")
 def test_known_answers_through_oracle(oracle, case):
-    op, m, n = case["op"], case["m"], case["n"]
+    op, m, n = case["op"], case.get("m", 1), case["n"]
     if op in ("sgemm", "dgemm"):
         k = case["k"]
         dt = np.float32 if op == "sgemm" else np.float64
@@ -91,6 +110,25 @@ def test_known_answers_through_oracle(oracle, case):
         xl, yl = (n, m) if trans == 0 else (m, n)
         out = oracle.sgemv_f64(trans, m, n, 1.0, _ones(m * n), _ones(xl), 0.0, np.zeros(yl, np.float32))
         assert np.max(np.abs(out - case["expect"])) <= case["tol_abs"]
+    elif op == "hgemv":
+        a16, x16 = hgemv_ramp(m, n)
+        got = oracle.hgemv_ref(0, m, n, 1.0, a16, x16, 0.0, np.zeros(m, np.uint16)).view(np.float16)
+        expect = hgemv_ramp_expect(a16, x16, m, n)
+        err = np.abs(got.astype(np.float32) - expect) / np.maximum(np.abs(expect), 1e-6)
+        assert np.max(err) <= case["tol_rel"]
+        exact = oracle.hgemv_f64(0, m, n, 1.0, a16, x16, 0.0, np.zeros(m, np.uint16))
+        np.testing.assert_allclose(expect, exact, rtol=1e-5)
+    elif op in ("sdot", "snrm2", "sasum"):
+        x = np.arange(n, dtype=np.float32)
+        exact = {"sdot": lambda: oracle.sdot_f64(n, x, x), "snrm2": lambda: oracle.snrm2_f64(n, x),
+                 "sasum": lambda: oracle.sasum_f64(n, x)}[op]()
+        assert exact == pytest.approx(case["expect"], rel=1e-15)
+        ref = oracle.sreduce_ref({"sdot": "dot", "snrm2": "nrm2", "sasum": "asum"}[op], n, x, x)
+        assert abs(ref - case["expect"]) / case["expect"] <= case["tol_rel"]
+    elif op == "isamax":
+        x = np.arange(n, dtype=np.float32)
+        assert oracle.isamax(n, x) == case["expect"]
+        assert oracle.isamax_ref(n, x) == case["expect"]
     else:
         raise AssertionError(op)
 
@@ -143,6 +181,41 @@ def test_strided_batched_offsets(oracle):
         np.testing.assert_allclose(out[b], 2.0 * a @ bb + 0.5 * c, rtol=1e-12, atol=1e-12)
 
 
+def test_dgemv_oracle_formulas_and_compensation(oracle):
+    m, n = 11, 17
+    A = oracle.uniform_f64(m * n, 3, 1)
+    a = A.reshape(m, n)
+    xn, xt = oracle.uniform_f64(n, 3, 2), oracle.uniform_f64(m, 3, 3)
+    yn, yt = oracle.uniform_f64(m, 3, 4), oracle.uniform_f64(n, 3, 5)
+    np.testing.assert_allclose(oracle.dgemv_f64(0, m, n, 1.5, A, xn, 0.25, yn), 1.5 * a @ xn + 0.25 * yn,
+                               rtol=1e-13, atol=1e-14)
+    np.testing.assert_allclose(oracle.dgemv_f64(1, m, n, 1.5, A, xt, 0.25, yt), 1.5 * a.T @ xt + 0.25 * yt,
+                               rtol=1e-13, atol=1e-14)
+    # Dot2 recovers a sum that plain f64 accumulation loses entirely:
+    # 1e16 + 1 - 1e16 (+ 1) = 2, where the naive left-to-right sum gives 1.
+    A2 = np.array([1e16, 1.0, -1e16, 1.0])
+    out = oracle.dgemv_f64(0, 1, 4, 1.0, A2, np.ones(4), 0.0, np.zeros(1))
+    assert out[0] == 2.0
+
+
+def test_hgemv_oracles_agree(oracle):
+    # The exact f64 evaluation and the reference's own arithmetic (flushing
+    # decode, f32 sums, truncating encode) agree within an f16 ulp or two on
+    # normal-range data, for both shapes.
+    m, n = 40, 56
+    A = oracle.uniform_f16(m * n, 9, 1)
+    for trans in (0, 1):
+        xl, yl = (n, m) if trans == 0 else (m, n)
+        x, y = oracle.uniform_f16(xl, 9, 2), oracle.uniform_f16(yl, 9, 3)
+        a = A.view(np.float16).astype(np.float64).reshape(m, n)
+        op = a if trans == 0 else a.T
+        want = 0.75 * op @ x.view(np.float16).astype(np.float64) + 0.5 * y.view(np.float16).astype(np.float64)
+        np.testing.assert_allclose(oracle.hgemv_f64(trans, m, n, 0.75, A, x, 0.5, y), want, rtol=1e-12,
+                                   atol=1e-12)
+        ref = oracle.hgemv_ref(trans, m, n, 0.75, A, x, 0.5, y).view(np.float16).astype(np.float64)
+        assert np.max(np.abs(ref - want) / np.maximum(np.abs(want), 2.0 ** -10)) <= 2.0 ** -9
+
+
 def test_sgemv_index_formulas(oracle):
     m, n = 9, 13
     A = oracle.uniform_f32(m * n, 3, 1)
@@ -154,3 +227,43 @@ def test_sgemv_index_formulas(oracle):
     np.testing.assert_allclose(oracle.sgemv_f64(0, m, n, 1.5, A, xn, 0.25, yn), 1.5 * a @ xn + 0.25 * yn, rtol=1e-12)
     np.testing.assert_allclose(oracle.sgemv_f64(1, m, n, 1.5, A, xt, 0.25, yt), 1.5 * a.T @ xt + 0.25 * yt,
                                rtol=1e-12)
+
+
+def test_reductions_oracle_vs_numpy(oracle):
+    for n in (0, 1, 31, 32, 33, 1000, 4099):
+        x = oracle.uniform_f32(n, 12, 1)
+        y = oracle.uniform_f32(n, 12, 2)
+        xd, yd = x.astype(np.float64), y.astype(np.float64)
+        assert oracle.sdot_f64(n, x, y) == pytest.approx(float(xd @ yd), rel=1e-13, abs=1e-13)
+        assert oracle.snrm2_f64(n, x) == pytest.approx(float(np.sqrt(xd @ xd)), rel=1e-13, abs=1e-13)
+        assert oracle.sasum_f64(n, x) == pytest.approx(float(np.abs(xd).sum()), rel=1e-13, abs=1e-13)
+        if n:
+            assert oracle.isamax(n, x) == int(np.argmax(np.abs(x)))
+            # a unique maximum: the reference's lane tree finds the same index
+            assert oracle.isamax_ref(n, x) == oracle.isamax(n, x)
+        # the reference's f32 arithmetic is within 4*n*eps(f32) * sum|x y|
+        if n:
+            bound = 4 * n * float(np.finfo(np.float32).eps) * float(np.abs(xd * yd).sum())
+            assert abs(oracle.sreduce_ref("dot", n, x, y) - float(xd @ yd)) <= bound
+
+
+def test_isamax_ties_and_nan(oracle):
+    # ties: the BLAS answer is the smallest index
+    x = np.zeros(64, np.float32)
+    x[40] = -5.0
+    x[7] = 5.0
+    assert oracle.isamax(64, x) == 7
+    # NaN never wins; all-NaN gives 0
+    x = np.array([np.nan, 1.0, np.nan, -3.0], np.float32)
+    assert oracle.isamax(4, x) == 3 and oracle.isamax_ref(4, x) == 3
+    assert oracle.isamax(3, np.full(3, np.nan, np.float32)) == 0
+    assert oracle.isamax_ref(3, np.full(3, np.nan, np.float32)) == 0
+    # The reference's lane tree settles ties by lane slot: index 32 (lane 0)
+    # and index 1 (lane 1) meet at stride 1, and slot 0 keeps its own value
+    # unless the other is strictly greater, so it answers 32 where the BLAS
+    # answer is 1.
+    x = np.zeros(64, np.float32)
+    x[32] = 2.0
+    x[1] = -2.0
+    assert oracle.isamax(64, x) == 1
+    assert oracle.isamax_ref(64, x) == 32

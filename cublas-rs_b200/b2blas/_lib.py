@@ -69,6 +69,8 @@ SIGNATURES = {
     "b2b_sreduce_async": (_i, [_vp, _i, _sz, _vp, _vp, _vp]),
     "b2b_saxpy": (_i, [_vp, _sz, _f, _vp, _vp]),
     "b2b_saxpy_simple": (_i, [_vp, _sz, _f, _vp, _sz, _vp, _sz]),
+    "b2b_gpu_timer_start": (_i, [_vp, _vpp]),
+    "b2b_gpu_timer_stop": (_i, [_vp, ctypes.POINTER(ctypes.c_double)]),
     "b2b_panels_to_rowmajor": (_i, [_vp, _sz, _sz, _sz, _szp, _vp, _vp]),
     "b2b_selftest_bounded_wait": (_i, [_vp, ctypes.c_uint64]),
 }

@@ -10,6 +10,8 @@
 // `Handle::create()` (new is a C++ keyword).
 #pragma once
 
+#include <algorithm>
+#include <cmath>
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
@@ -229,6 +231,71 @@ class Handle {
         sgemv_simple(t, m, n, alpha, a, x, beta, y, B2B_ALGO_TILED);
     }
 
+    void dgemv(Transpose t, size_t m, size_t n, double alpha, const DeviceBuffer<double> &a,
+               const DeviceBuffer<double> &x, double beta, DeviceBuffer<double> &y) const {
+        const size_t xl = t == Transpose::NoTrans ? n : m, yl = t == Transpose::NoTrans ? m : n;
+        if (m && n) {
+            need(a, m * n, "A");
+            need(x, xl, "x");
+            need(y, yl, "y");
+        }
+        check(b2b_dgemv(h_, int(t), m, n, alpha, a.ptr(), x.ptr(), beta, y.ptr()));
+    }
+    void dgemv_simple(Transpose t, size_t m, size_t n, double alpha, const std::vector<double> &a,
+                      const std::vector<double> &x, double beta, std::vector<double> &y) const {
+        check(b2b_dgemv_simple(h_, int(t), m, n, alpha, a.data(), a.size(), x.data(), x.size(), beta, y.data(),
+                               y.size()));
+    }
+    // Handle::hgemv (lib.rs:344-366): host slices only, alpha/beta as f16.
+    void hgemv(Transpose t, size_t m, size_t n, f16 alpha, const std::vector<f16> &a, const std::vector<f16> &x,
+               f16 beta, std::vector<f16> &y) const {
+        check(b2b_hgemv_simple(h_, int(t), m, n, alpha.to_f32(), reinterpret_cast<const uint16_t *>(a.data()),
+                               a.size(), reinterpret_cast<const uint16_t *>(x.data()), x.size(), beta.to_f32(),
+                               reinterpret_cast<uint16_t *>(y.data()), y.size()));
+    }
+
+    // ---- Level 1 reductions (lib.rs:157-195); each returns the value
+    float sdot(size_t n, const DeviceBuffer<float> &x, const DeviceBuffer<float> &y) const {
+        if (n) {
+            need(x, n, "x");
+            need(y, n, "y");
+        }
+        float r = 0.0f;
+        check(b2b_sdot(h_, n, x.ptr(), y.ptr(), &r));
+        return r;
+    }
+    float sdot_simple(size_t n, const std::vector<float> &x, const std::vector<float> &y) const {
+        float r = 0.0f;
+        check(b2b_sdot_simple(h_, n, x.data(), x.size(), y.data(), y.size(), &r));
+        return r;
+    }
+#define CUBLAS_RS_REDUCE(NAME)                                                      \
+    float NAME(size_t n, const DeviceBuffer<float> &x) const {                      \
+        if (n) need(x, n, "x");                                                     \
+        float r = 0.0f;                                                             \
+        check(b2b_##NAME(h_, n, x.ptr(), &r));                                      \
+        return r;                                                                   \
+    }                                                                               \
+    float NAME##_simple(size_t n, const std::vector<float> &x) const {              \
+        float r = 0.0f;                                                             \
+        check(b2b_##NAME##_simple(h_, n, x.data(), x.size(), &r));                  \
+        return r;                                                                   \
+    }
+    CUBLAS_RS_REDUCE(snrm2)
+    CUBLAS_RS_REDUCE(sasum)
+#undef CUBLAS_RS_REDUCE
+    size_t isamax(size_t n, const DeviceBuffer<float> &x) const {
+        if (n) need(x, n, "x");
+        size_t r = 0;
+        check(b2b_isamax(h_, n, x.ptr(), &r));
+        return r;
+    }
+    size_t isamax_simple(size_t n, const std::vector<float> &x) const {
+        size_t r = 0;
+        check(b2b_isamax_simple(h_, n, x.data(), x.size(), &r));
+        return r;
+    }
+
     // ---- Level 3: SGEMM (lib.rs:439-524)
 #define CUBLAS_RS_SGEMM_VARIANT(NAME, ALGO)                                                                    \
     void NAME(const GemmConfig<float> &c, const DeviceBuffer<float> &a, const DeviceBuffer<float> &b,        \
@@ -327,5 +394,91 @@ class Handle {
     }
     b2b_handle *h_ = nullptr;
 };
+
+// GpuTimer (benches/src/timer.rs:6-19): start() records a CUDA event on the
+// handle's stream; stop() records the end event, waits for it and returns
+// the elapsed milliseconds.  Move-only; a timer dropped without stop() is
+// released.
+class GpuTimer {
+   public:
+    static GpuTimer start(const Handle &h) {
+        b2b_gpu_timer *t = nullptr;
+        check(b2b_gpu_timer_start(h.raw(), &t));
+        return GpuTimer(t);
+    }
+    double stop() {
+        if (!t_) throw CublasError(B2B_ERR_INVALID_ARG, "GpuTimer::stop called twice");
+        double ms = 0.0;
+        b2b_gpu_timer *t = t_;
+        t_ = nullptr;
+        check(b2b_gpu_timer_stop(t, &ms));
+        return ms;
+    }
+    ~GpuTimer() {
+        if (t_) b2b_gpu_timer_stop(t_, nullptr);
+    }
+    GpuTimer(const GpuTimer &) = delete;
+    GpuTimer &operator=(const GpuTimer &) = delete;
+    GpuTimer(GpuTimer &&o) noexcept : t_(o.t_) { o.t_ = nullptr; }
+
+   private:
+    explicit GpuTimer(b2b_gpu_timer *t) : t_(t) {}
+    b2b_gpu_timer *t_ = nullptr;
+};
+
+// Result of validate_gemm / validate_vector (validator.rs:6-25), where the
+// reference returns Result<(), String>: ok() or the error message.
+struct Validation {
+    std::string error;
+    bool ok() const { return error.empty(); }
+};
+
+// validate_gemm (validator.rs:6-20): recompute alpha*A*B + beta*C on the
+// host in double, C being `expected` (C before the call), and check
+// max |actual - reference| <= tolerance.  Row-major A m x k, B k x n.
+inline Validation validate_gemm(size_t m, size_t n, size_t k, float alpha, const std::vector<float> &a,
+                                const std::vector<float> &b, float beta, const std::vector<float> &expected,
+                                const std::vector<float> &actual, float tolerance) {
+    if (a.size() != m * k || b.size() != k * n || expected.size() != m * n || actual.size() != m * n)
+        return {"slice lengths do not match m, n, k"};
+    std::vector<double> row(n);
+    double worst = 0.0;
+    size_t wi = 0;
+    for (size_t i = 0; i < m; ++i) {
+        std::fill(row.begin(), row.end(), 0.0);
+        for (size_t p = 0; p < k; ++p) {
+            const double av = a[i * k + p];
+            for (size_t j = 0; j < n; ++j) row[j] += av * double(b[p * n + j]);
+        }
+        for (size_t j = 0; j < n; ++j) {
+            double ref = double(alpha) * row[j];
+            if (beta != 0.0f) ref += double(beta) * double(expected[i * n + j]);
+            const double got = actual[i * n + j];
+            const double err = got != got ? HUGE_VAL : (got > ref ? got - ref : ref - got);
+            if (err > worst) {
+                worst = err;
+                wi = i * n + j;
+            }
+        }
+    }
+    if (worst > double(tolerance))
+        return {"max abs error " + std::to_string(worst) + " at C[" + std::to_string(wi / n) + "][" +
+                std::to_string(wi % n) + "] exceeds tolerance " + std::to_string(tolerance)};
+    return {};
+}
+
+// validate_vector (validator.rs:22-25): equal lengths, element-wise
+// max |actual - expected| <= tolerance.
+inline Validation validate_vector(const std::vector<float> &expected, const std::vector<float> &actual,
+                                  float tolerance) {
+    if (expected.size() != actual.size()) return {"length mismatch"};
+    for (size_t i = 0; i < expected.size(); ++i) {
+        const double d = double(actual[i]) - double(expected[i]);
+        if (!(d <= double(tolerance) && -d <= double(tolerance)))
+            return {"element " + std::to_string(i) + " differs by " + std::to_string(d) + " (tolerance " +
+                    std::to_string(tolerance) + ")"};
+    }
+    return {};
+}
 
 }  // namespace cublas_rs

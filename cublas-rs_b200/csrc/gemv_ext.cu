@@ -6,11 +6,12 @@
 // Same streaming structure as SGEMV (gemv.cu), templated on the element type:
 //   * N: one warp per row, 16-byte loads of A (2 doubles / 8 halves) with
 //     ld.global.nc.L1::no_allocate, x through L1, shuffle reduction.
-//   * T: split-row partial sums (about 4 CTAs per SM), each lane owning one
+//   * T: split-row partial sums (as many row slices as fill one resident
+//     wave of CTAs), four rows' loads in flight per lane, each lane owning one
 //     16-byte column group, ordered second-pass reduction; partials in the
 //     handle's workspace in the accumulation type.
 // Accumulation is in double for DGEMV and float for HGEMV; the f16 result is
-// rounded to nearest even (the reference truncates, gemv.rs:155-172).
+// rounded to nearest even (the reference truncates, gemv.rs:534-551).
 // beta == 0 does not read y.  Rows or pointers that break 16-byte alignment
 // take the scalar path of the same kernels.
 #include <cuda_fp16.h>
@@ -24,22 +25,28 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 
+// 16-byte loads, kept raw until every load of an unrolled group is issued
+// (the asm is volatile, so the loads stay in program order; the unpacking
+// that follows is free to wait for them).
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+    uint4 u;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                 : "l"(p));
+    return u;
+}
+
+__device__ __forceinline__ uint4 ld_cached16(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+
 template <typename T>
 struct GV;
 template <>
 struct GV<double> {
     using Acc = double;
     static constexpr int W = 2;  // elements per 16-byte vector
-    __device__ __forceinline__ static void load_stream(const double *p, Acc (&v)[W]) {
-        double2 t;
-        asm volatile("ld.global.nc.L1::no_allocate.v2.f64 {%0, %1}, [%2];" : "=d"(t.x), "=d"(t.y) : "l"(p));
-        v[0] = t.x;
-        v[1] = t.y;
-    }
-    __device__ __forceinline__ static void load_cached(const double *p, Acc (&v)[W]) {
-        const double2 t = __ldg(reinterpret_cast<const double2 *>(p));
-        v[0] = t.x;
-        v[1] = t.y;
+    __device__ __forceinline__ static void unpack(const uint4 &u, Acc (&v)[W]) {
+        v[0] = __hiloint2double((int)u.y, (int)u.x);
+        v[1] = __hiloint2double((int)u.w, (int)u.z);
     }
     __device__ __forceinline__ static Acc get(const double *p) { return *p; }
     __device__ __forceinline__ static Acc get_stream(const double *p) {
@@ -61,16 +68,6 @@ struct GV<uint16_t> {
             v[2 * i] = f.x;
             v[2 * i + 1] = f.y;
         }
-    }
-    __device__ __forceinline__ static void load_stream(const uint16_t *p, Acc (&v)[W]) {
-        uint4 u;
-        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                     : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
-                     : "l"(p));
-        unpack(u, v);
-    }
-    __device__ __forceinline__ static void load_cached(const uint16_t *p, Acc (&v)[W]) {
-        unpack(__ldg(reinterpret_cast<const uint4 *>(p)), v);
     }
     __device__ __forceinline__ static Acc get(const uint16_t *p) { return __half2float(__ushort_as_half(*p)); }
     __device__ __forceinline__ static Acc get_stream(const uint16_t *p) {
@@ -104,20 +101,24 @@ __global__ void __launch_bounds__(kThreads) gemvx_n_kernel(const T *__restrict__
         const int64_t nv = n / W;
         int64_t j = lane;
         for (; j + 32 * (UNROLL - 1) < nv; j += 32 * UNROLL) {
-            Acc av[UNROLL][W], xv[UNROLL][W];
+            uint4 ar[UNROLL], xr[UNROLL];
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) GV<T>::load_stream(a + (j + 32 * u) * W, av[u]);
+            for (int u = 0; u < UNROLL; ++u) ar[u] = ld_stream16(a + (j + 32 * u) * W);
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) GV<T>::load_cached(x + (j + 32 * u) * W, xv[u]);
+            for (int u = 0; u < UNROLL; ++u) xr[u] = ld_cached16(x + (j + 32 * u) * W);
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u)
+            for (int u = 0; u < UNROLL; ++u) {
+                Acc av[W], xv[W];
+                GV<T>::unpack(ar[u], av);
+                GV<T>::unpack(xr[u], xv);
 #pragma unroll
-                for (int e = 0; e < W; ++e) acc = fma(av[u][e], xv[u][e], acc);
+                for (int e = 0; e < W; ++e) acc = fma(av[e], xv[e], acc);
+            }
         }
         for (; j < nv; j += 32) {
             Acc av[W], xv[W];
-            GV<T>::load_stream(a + j * W, av);
-            GV<T>::load_cached(x + j * W, xv);
+            GV<T>::unpack(ld_stream16(a + j * W), av);
+            GV<T>::unpack(ld_cached16(x + j * W), xv);
 #pragma unroll
             for (int e = 0; e < W; ++e) acc = fma(av[e], xv[e], acc);
         }
@@ -154,9 +155,26 @@ __global__ void __launch_bounds__(kThreads) gemvx_t_partial_kernel(const T *__re
     if constexpr (VEC) {
         const int64_t c = c0 + lane * W;
         if (c < n) {  // n % W == 0: the vector is all in range
-            for (int64_t r = r0 + warp; r < r1; r += kWarps) {
+            int64_t r = r0 + warp;
+            // four rows' 16-byte loads in flight per lane
+            for (; r + 3 * kWarps < r1; r += 4 * kWarps) {
+                uint4 raw[4];
+                Acc xs[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) raw[u] = ld_stream16(A + (r + u * kWarps) * n + c);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) xs[u] = GV<T>::get(x + r + u * kWarps);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    Acc v[W];
+                    GV<T>::unpack(raw[u], v);
+#pragma unroll
+                    for (int e = 0; e < W; ++e) acc[e] = fma(v[e], xs[u], acc[e]);
+                }
+            }
+            for (; r < r1; r += kWarps) {
                 Acc v[W];
-                GV<T>::load_stream(A + r * n + c, v);
+                GV<T>::unpack(ld_stream16(A + r * n + c), v);
                 const Acc xs = GV<T>::get(x + r);
 #pragma unroll
                 for (int e = 0; e < W; ++e) acc[e] = fma(v[e], xs, acc[e]);
@@ -227,7 +245,13 @@ int run_gemvx(b2b_handle *h, int trans, int64_t m, int64_t n, typename GV<T>::Ac
     const bool vec = (n % W == 0) && b2b::aligned16(A);
     const int64_t cb = (n + 32 * W - 1) / (32 * W);
     if (cb > 0x7fffffffLL) return b2b::fail(B2B_ERR_INVALID_ARG, "gemv: n too large");
-    int64_t slices = (4LL * h->sm_count + cb - 1) / cb;
+    // Row slices so that every CTA of the grid is resident at once: a grid a
+    // little over one wave would leave a short second wave running alone.
+    const int64_t slots = b2b::resident_ctas(
+        h, vec ? reinterpret_cast<const void *>(gemvx_t_partial_kernel<T, true, false>)
+               : reinterpret_cast<const void *>(gemvx_t_partial_kernel<T, false, false>),
+        kThreads, 0);
+    int64_t slices = cb >= slots ? 1 : slots / cb;
     const int64_t max_slices = (m + 63) / 64;
     if (slices > max_slices) slices = max_slices;
     if (slices > 65535) slices = 65535;

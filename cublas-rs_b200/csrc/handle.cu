@@ -10,8 +10,10 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <mutex>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "internal.h"
 
@@ -72,6 +74,31 @@ int workspace(b2b_handle *h, size_t bytes, void **ptr) {
 
 int staging(b2b_handle *h, size_t bytes, void **ptr) {
     return grow(h, &h->staging, &h->staging_bytes, bytes, ptr, "staging allocation");
+}
+
+int resident_ctas(b2b_handle *h, const void *kernel, int threads, size_t smem) {
+    struct Entry {
+        const void *kernel;
+        int device, threads;
+        size_t smem;
+        int ctas;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const Entry &e : cache)
+            if (e.kernel == kernel && e.device == h->device && e.threads == threads && e.smem == smem) return e.ctas;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        per_sm = 1;
+    }
+    const int ctas = per_sm * h->sm_count;
+    std::lock_guard<std::mutex> lock(mu);
+    cache.push_back(Entry{kernel, h->device, threads, smem, ctas});
+    return ctas;
 }
 
 }  // namespace b2b

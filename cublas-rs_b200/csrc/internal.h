@@ -75,6 +75,11 @@ struct DeviceGuard {
 // stream order on the handle's stream).
 int workspace(b2b_handle *h, size_t bytes, void **ptr);
 int staging(b2b_handle *h, size_t bytes, void **ptr);
+// CTAs of `kernel` (launched with `threads` threads and `smem` dynamic
+// shared bytes) that are resident on the whole GPU at once: the occupancy
+// per SM times the SM count, cached per kernel and device.  Grid-stride
+// kernels launch exactly this many so no partial second wave runs.
+int resident_ctas(b2b_handle *h, const void *kernel, int threads, size_t smem);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -4,8 +4,9 @@
 // (crates/cublas-l1/src/dot.rs:21-53, nrm2.rs:16-48, asum.rs:15-47,
 // iamax.rs:16-61), which reads at a few GB/s.  Here one launch streams the
 // vector over the whole GPU:
-//   * grid = min(ceil(n / 4096), 8 CTAs per SM), 256 threads; each thread
-//     grid-strides over 16-byte vectors (ld.global.nc.L1::no_allocate, four
+//   * grid = min(ceil(n / 4096), the CTAs resident at once), 256 threads
+//     (one wave, no partial second one); each thread
+//     grid-strides over 16-byte vectors (ld.global.nc.L1::no_allocate, eight
 //     in flight per thread) and keeps its sums in f64 -- a product of two f32
 //     values is exact in f64, so the only rounding left that matters is the
 //     final f64 -> f32 one;
@@ -122,17 +123,18 @@ __global__ void __launch_bounds__(kThreads) sreduce_kernel(const float *__restri
     if constexpr (VEC) {
         const int64_t n4 = n >> 2;
         int64_t j = tid;
-        // four 16-byte loads in flight per operand
-        for (; j + 3 * stride < n4; j += 4 * stride) {
-            float4 a[4], b[4];
+        // eight 16-byte loads in flight per thread (four per operand for DOT)
+        constexpr int U = (OP == B2B_REDUCE_DOT) ? 4 : 8;
+        for (; j + (U - 1) * stride < n4; j += U * stride) {
+            float4 a[U], b[U];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) a[u] = ld_stream4(x + 4 * (j + u * stride));
+            for (int u = 0; u < U; ++u) a[u] = ld_stream4(x + 4 * (j + u * stride));
             if constexpr (OP == B2B_REDUCE_DOT) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u) b[u] = ld_stream4(y + 4 * (j + u * stride));
+                for (int u = 0; u < U; ++u) b[u] = ld_stream4(y + 4 * (j + u * stride));
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < U; ++u) {
                 if constexpr (OP == B2B_REDUCE_IAMAX) {
                     const int64_t base = 4 * (j + u * stride);
                     amax_take(bv, bi, fabsf(a[u].x), base);
@@ -237,15 +239,18 @@ __global__ void __launch_bounds__(kThreads) sreduce_kernel(const float *__restri
 
 template <int OP>
 int launch_op(b2b_handle *h, int64_t n, const float *x, const float *y, void *out) {
+    const bool vec = b2b::aligned16(x) && (OP != B2B_REDUCE_DOT || b2b::aligned16(y));
+    // one resident wave: the grid-stride loop covers any n
+    const void *kern = vec ? reinterpret_cast<const void *>(sreduce_kernel<OP, true>)
+                           : reinterpret_cast<const void *>(sreduce_kernel<OP, false>);
     int64_t blocks = (n + 4095) / 4096;
-    const int64_t cap = 8LL * h->sm_count;
+    const int64_t cap = b2b::resident_ctas(h, kern, kThreads, 0);
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     void *ws = nullptr;
     if (int rc = b2b::workspace(h, static_cast<size_t>(blocks) * sizeof(Partial), &ws)) return rc;
     unsigned int *counter = reinterpret_cast<unsigned int *>(reinterpret_cast<char *>(h->d_status) +
                                                              B2B_STATUS_REDUCE_COUNTER);
-    const bool vec = b2b::aligned16(x) && (OP != B2B_REDUCE_DOT || b2b::aligned16(y));
     if (vec)
         sreduce_kernel<OP, true><<<(unsigned)blocks, kThreads, 0, h->stream>>>(x, y, n, static_cast<Partial *>(ws),
                                                                               counter, out);

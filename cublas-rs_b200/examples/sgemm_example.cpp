@@ -5,8 +5,9 @@
 // DGEMM naive/tiled, strided and list-batched 8 x 64^3, HGEMM 128^3), the
 // gemm_bench verification (examples/gemm_bench/src/main.rs:147-153, device
 // buffers, sizes 256/512/1024) and the sgemv smoke check
-// (examples/saxpy/src/main.rs:88-124).  All-ones inputs, so every output
-// equals the inner dimension.  Exits 1 on the first failure, like the
+// (examples/saxpy/src/main.rs:88-124), then the saxpy example's reduction
+// and hgemv checks and the bench crate's timer and validators.  GEMM/GEMV
+// inputs are all ones, so every output equals the inner dimension.  Exits 1 on the first failure, like the
 // reference's examples.
 #include <chrono>
 #include <cmath>
@@ -121,6 +122,58 @@ int main() {
             h.sgemv_tiled_simple(Transpose::Trans, m, n, 1.0f, a, xt, 0.0f, yt);
             if (bad_count(yt, double(m), 1e-3)) fail("sgemv T");
             std::printf("  sgemv N/T OK\n");
+        }
+        {
+            // The saxpy example's reduction and hgemv checks
+            // (examples/saxpy/src/main.rs:38-63, 132-172).
+            const size_t n = 1024;
+            std::vector<float> x(n);
+            for (size_t i = 0; i < n; ++i) x[i] = float(i);
+            const double sumsq = 357389824.0, asum = 523776.0;  // closed forms of sum i^2, sum i
+            const auto rel = [](double got, double want) { return std::fabs(got - want) / want; };
+            if (rel(h.sdot_simple(n, x, x), sumsq) > 1e-3) fail("sdot");
+            if (rel(h.snrm2_simple(n, x), std::sqrt(sumsq)) > 1e-3) fail("snrm2");
+            if (rel(h.sasum_simple(n, x), asum) > 1e-3) fail("sasum");
+            if (h.isamax_simple(n, x) != n - 1) fail("isamax");
+            auto xd = h.upload(x);
+            if (rel(h.sdot(n, xd, xd), sumsq) > 1e-3 || h.isamax(n, xd) != n - 1) fail("device reductions");
+            const size_t m = 16, k = 24;
+            std::vector<f16> a16(m * k), x16(k), y16(m, f16::from_f32(0.0f));
+            for (size_t i = 0; i < m * k; ++i) a16[i] = f16::from_f32(float(i) * 0.01f);
+            for (size_t j = 0; j < k; ++j) x16[j] = f16::from_f32(float(j) * 0.1f);
+            h.hgemv(Transpose::NoTrans, m, k, f16::from_f32(1.0f), a16, x16, f16::from_f32(0.0f), y16);
+            for (size_t i = 0; i < m; ++i) {
+                float want = 0.0f;
+                for (size_t j = 0; j < k; ++j) want += a16[i * k + j].to_f32() * x16[j].to_f32();
+                if (std::fabs(y16[i].to_f32() - want) / std::max(std::fabs(want), 1e-6f) > 5e-3f) fail("hgemv");
+            }
+            std::vector<double> ad(m * k, 1.0), xdv(k, 1.0), ydv(m, 0.0);
+            h.dgemv_simple(Transpose::NoTrans, m, k, 1.0, ad, xdv, 0.0, ydv);
+            if (bad_count(ydv, double(k), 1e-9)) fail("dgemv");
+            std::printf("  reductions, hgemv, dgemv OK\n");
+        }
+        {
+            // GpuTimer and the validators (benches/src/timer.rs, validator.rs)
+            const size_t s = 256;
+            GemmConfig<float> cfg{s, s, s, 1.0f, 0.0f};
+            std::vector<float> a(s * s), b(s * s), c0(s * s, 0.0f);
+            for (size_t i = 0; i < s * s; ++i) {
+                a[i] = float(int(i % 7) - 3);
+                b[i] = float(int(i % 5) - 2) * 0.5f;
+            }
+            auto da = h.upload(a), db = h.upload(b);
+            auto dc = h.zeroed<float>(s * s);
+            GpuTimer t = GpuTimer::start(h);
+            h.sgemm(cfg, da, db, dc);
+            const double ms = t.stop();
+            if (!(ms > 0.0)) fail("GpuTimer");
+            const std::vector<float> c = h.download(dc);
+            if (!validate_gemm(s, s, s, 1.0f, a, b, 0.0f, c0, c, 1e-3f).ok()) fail("validate_gemm on a good C");
+            std::vector<float> bad = c;
+            bad[77] += 1.0f;
+            if (validate_gemm(s, s, s, 1.0f, a, b, 0.0f, c0, bad, 1e-3f).ok()) fail("validate_gemm on a bad C");
+            if (!validate_vector(c, c, 0.0f).ok() || validate_vector(c, bad, 0.5f).ok()) fail("validate_vector");
+            std::printf("  GpuTimer %.4f ms, validate_gemm/validate_vector OK\n", ms);
         }
         {
             // A short A slice is a DimensionMismatch (the reference panics).

@@ -282,6 +282,15 @@ B2B_API int b2b_isamax_simple(b2b_handle *h, size_t n, const float *x, size_t x_
  * different streams through the same handle. */
 B2B_API int b2b_sreduce_async(b2b_handle *h, int op, size_t n, const float *x, const float *y, void *d_result);
 
+/* ------------------------------------------------------------ GpuTimer
+ * benches/src/timer.rs:6-19 (GpuTimer::start / stop, todo! stubs in the
+ * reference): start records a CUDA event on the handle's current stream;
+ * stop records a second one, waits for it, writes the elapsed milliseconds
+ * and frees the timer (stop consumes it, as `stop(self)` does). */
+typedef struct b2b_gpu_timer b2b_gpu_timer;
+B2B_API int b2b_gpu_timer_start(b2b_handle *h, b2b_gpu_timer **timer);
+B2B_API int b2b_gpu_timer_stop(b2b_gpu_timer *timer, double *ms);
+
 /* --------------------------------------------- multi-GPU column sharding
  * No reference counterpart (the reference is single-device,
  * crates/cublas-rs/src/lib.rs:57-68).  A large GEMM is split by column

@@ -465,7 +465,7 @@ class Handle:
     def hgemv(self, trans, m, n, alpha, a, x, beta, y):
         """Handle::hgemv: host slices of f16 (np.float16 or uint16 bit
         patterns).  alpha and beta are f16 values in the reference, so they
-        are rounded to f16 first and passed on as f32 (gemv.rs:648-649)."""
+        are rounded to f16 first and passed on as f32 (gemv.rs:651-652)."""
         a, x, y = _host(a, np.uint16), _host(x, np.uint16), _host(y, np.uint16)
         _check(self._lib.b2b_hgemv_simple(self._h, int(trans), m, n, float(np.float16(alpha)), _hp(a), a.size,
                                           _hp(x), x.size, float(np.float16(beta)), _hp(y), y.size))

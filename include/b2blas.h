@@ -231,7 +231,7 @@ B2B_API int b2b_hgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha,
                       const uint16_t *x, float beta, uint16_t *y);
 /* Handle::hgemv (lib.rs:344-366) -> cublas_l2::hgemv (gemv.rs:619-673):
  * host slices of f16 bit patterns; alpha/beta are the f32 values the
- * reference passes its kernels (alpha.to_f32(), gemv.rs:648-649). */
+ * reference passes its kernels (alpha.to_f32(), gemv.rs:651-652). */
 B2B_API int b2b_hgemv_simple(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const uint16_t *A,
                              size_t a_len, const uint16_t *x, size_t x_len, float beta, uint16_t *y,
                              size_t y_len);

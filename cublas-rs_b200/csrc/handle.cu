@@ -172,6 +172,8 @@ int b2b_create(int device, b2b_handle **out) {
     const char *single = getenv("B2B_HGEMM_SINGLE_CTA");
     h->force_single_cta = single && single[0] == '1';
     if (const char *v = getenv("B2B_SGEMM_VARIANT")) h->sgemm_variant = atoi(v);
+    if (const char *v = getenv("B2B_HGEMM_VARIANT")) h->hgemm_variant = atoi(v);
+    if (const char *v = getenv("B2B_HGEMM_GROUP_M")) h->hgemm_group_m = atoi(v);
     if (const char *v = getenv("B2B_DGEMM_VARIANT")) h->dgemm_variant = atoi(v);
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
     *out = h;

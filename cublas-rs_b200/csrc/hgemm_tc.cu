@@ -70,6 +70,7 @@ struct HgemmArgs {
     float alpha, beta;
     int *status;
     uint64_t wait_ns;
+    int group_m;  // pair kernels' raster group (pair-tile rows); 0 = the kernel's default
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
@@ -357,43 +358,69 @@ __global__ void __launch_bounds__(hg::THREADS, 1)
 //     to both CTAs' "empty" / "tmem full" barriers.
 //   * The leader's "tmem empty" barriers count one arrival per epilogue warp
 //     of both CTAs (8); the partner's warps arrive remotely.
+//   * Epilogue with beta == 0: each warp moves its 32 TMEM lanes x 64 columns
+//     to registers, scales, rounds to f16, writes them to a 4 KiB staging
+//     buffer in the 128-byte-swizzled layout and issues one TMA store of the
+//     32 x 64 box (two buffers per warp, recycled once the bulk group that
+//     used them has read them).  That replaces 32-row-scattered 16-byte
+//     stores; with beta != 0 C is read and written by the threads.
 namespace hg2 {
-constexpr int BM = 128;      // rows per CTA (256 per pair)
-constexpr int BN = 256;      // columns per pair tile
-constexpr int BN_CTA = 128;  // B columns each CTA loads
-constexpr int BK = 64;
-constexpr int STAGES = 6;
-constexpr int A_BYTES = BM * BK * 2;           // 16 KiB
-constexpr int B_BOX_N = 64;
-constexpr int B_BOX_BYTES = B_BOX_N * BK * 2;  // 8 KiB
-constexpr int B_BYTES = BK * BN_CTA * 2;       // 16 KiB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int PAIR_STAGE_BYTES = 2 * STAGE_BYTES;
-constexpr int ACC_COLS = BN;
-constexpr int TMEM_COLS = 2 * ACC_COLS;
+// NSPLIT = number of N=256 MMAs per 16-wide k step.  1: 256 x 256 pair tiles,
+// two 256-column TMEM accumulators (the epilogue overlaps the next tile).
+// 2: 256 x 512 pair tiles (each MMA's A tile feeds two B halves), one
+// 512-column accumulator; per CTA and k-block 48 KiB move for 128x512x64
+// MACs, a quarter fewer operand bytes per flop than NSPLIT = 1, at the cost
+// of an epilogue that the next tile's MMAs wait for.
+template <int NSPLIT>
+struct Cfg {
+    static constexpr int BM = 128;              // rows per CTA (256 per pair)
+    static constexpr int BN = 256 * NSPLIT;     // columns per pair tile
+    static constexpr int BN_HALF = 128;         // B columns each CTA loads per MMA
+    static constexpr int BK = 64;
+    static constexpr int STAGES = NSPLIT == 1 ? 6 : 4;
+    static constexpr int A_BYTES = BM * BK * 2;             // 16 KiB
+    static constexpr int B_BOX_N = 64;
+    static constexpr int B_BOX_BYTES = B_BOX_N * BK * 2;    // 8 KiB
+    static constexpr int B_SPLIT_BYTES = BK * BN_HALF * 2;  // 16 KiB per MMA
+    static constexpr int B_BYTES = NSPLIT * B_SPLIT_BYTES;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int PAIR_STAGE_BYTES = 2 * STAGE_BYTES;
+    static constexpr int ACC_COLS = BN;
+    static constexpr int ACC_BUFS = NSPLIT == 1 ? 2 : 1;
+    static constexpr int TMEM_COLS = ACC_BUFS * ACC_COLS;  // 512 either way
+    static constexpr int EPI_WARPS_PAIR = 8;
+    static constexpr int GROUP_M = 16;  // raster group, in 256-row pair tiles
+    // Epilogue staging for the TMA-store path: two 4 KiB buffers (32 rows x
+    // 64 f16 columns, 128-byte swizzle) per epilogue warp.
+    static constexpr int EPI_BUF_BYTES = 32 * 64 * 2;
+    static constexpr int EPI_BYTES = 4 * 2 * EPI_BUF_BYTES;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+    static constexpr uint32_t IDESC = sm100::idesc_f32acc(0, 0, 1, 256, 256);
+    static_assert(TMEM_COLS == 512, "TMEM holds 512 columns");
+    static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+};
 constexpr int THREADS = 192;
-constexpr int EPI_WARPS_PAIR = 8;
-constexpr int GROUP_M = 16;  // raster group, in 256-row pair tiles
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-constexpr uint32_t IDESC = sm100::idesc_f32acc(0, 0, 1, 256, BN);
 }  // namespace hg2
 
+template <int NSPLIT>
 __global__ void __launch_bounds__(hg2::THREADS, 1)
     hgemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     HgemmArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, HgemmArgs args) {
     using namespace sm100;
+    using Cf = hg2::Cfg<NSPLIT>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
     uint8_t *sA = smem;
-    uint8_t *sB = smem + hg2::STAGES * hg2::A_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + hg2::STAGES * hg2::STAGE_BYTES);
+    uint8_t *sB = smem + Cf::STAGES * Cf::A_BYTES;
+    uint8_t *stg = smem + Cf::STAGES * Cf::STAGE_BYTES;  // epilogue staging, 1024-aligned
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stg + Cf::EPI_BYTES);
     uint64_t *full = bars;
-    uint64_t *empty = bars + hg2::STAGES;
-    uint64_t *tfull = bars + 2 * hg2::STAGES;
-    uint64_t *tempty = bars + 2 * hg2::STAGES + 2;
-    uint64_t *drain = bars + 2 * hg2::STAGES + 4;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * hg2::STAGES + 5);
+    uint64_t *empty = bars + Cf::STAGES;
+    uint64_t *tfull = bars + 2 * Cf::STAGES;
+    uint64_t *tempty = bars + 2 * Cf::STAGES + 2;
+    uint64_t *drain = bars + 2 * Cf::STAGES + 4;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * Cf::STAGES + 5);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -402,19 +429,20 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
     const bool leader = rank == 0;
     const int pair = static_cast<int>(blockIdx.x >> 1);
     const int npairs = static_cast<int>(gridDim.x >> 1);
-    const int tiles_m = (args.M + 2 * hg2::BM - 1) / (2 * hg2::BM);
-    const int tiles_n = (args.N + hg2::BN - 1) / hg2::BN;
+    const int tiles_m = (args.M + 2 * Cf::BM - 1) / (2 * Cf::BM);
+    const int tiles_n = (args.N + Cf::BN - 1) / Cf::BN;
     const int num_tiles = tiles_m * tiles_n;
-    const int kblocks = (args.K + hg2::BK - 1) / hg2::BK;
+    const int kblocks = (args.K + Cf::BK - 1) / Cf::BK;
+    const int group_m = args.group_m > 0 ? args.group_m : Cf::GROUP_M;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < hg2::STAGES; ++s) {
+        for (int s = 0; s < Cf::STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], hg2::EPI_WARPS_PAIR);
+            mbar_init(&tempty[a], Cf::EPI_WARPS_PAIR);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -423,9 +451,10 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
+        prefetch_tensormap(&tmC);
     }
     if (warp == 1) {
-        tmem_alloc_pair(tmem_slot, hg2::TMEM_COLS);
+        tmem_alloc_pair(tmem_slot, Cf::TMEM_COLS);
         tmem_relinquish_pair();
     }
     // Both CTAs' barriers must be initialised before either signals the other.
@@ -443,7 +472,7 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
             bool ok = true;
             for (int t = pair; t < num_tiles && ok; t += npairs) {
                 int tm, tn;
-                tile_coords_g(t, tiles_m, tiles_n, hg2::GROUP_M, tm, tn);
+                tile_coords_g(t, tiles_m, tiles_n, group_m, tm, tn);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x11,
                                    args.wait_ns)) {
@@ -451,18 +480,21 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                         break;
                     }
                     const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
-                    if (leader) mbar_arrive_expect_tx(&full[stage], hg2::PAIR_STAGE_BYTES);
-                    uint8_t *a_dst = sA + stage * hg2::A_BYTES;
-                    uint8_t *b_dst = sB + stage * hg2::B_BYTES;
-                    tma_load_2d_pair(a_dst, &tmA, full_leader, kb * hg2::BK,
-                                     tm * 2 * hg2::BM + static_cast<int>(rank) * hg2::BM);
+                    if (leader) mbar_arrive_expect_tx(&full[stage], Cf::PAIR_STAGE_BYTES);
+                    uint8_t *a_dst = sA + stage * Cf::A_BYTES;
+                    uint8_t *b_dst = sB + stage * Cf::B_BYTES;
+                    tma_load_2d_pair(a_dst, &tmA, full_leader, kb * Cf::BK,
+                                     tm * 2 * Cf::BM + static_cast<int>(rank) * Cf::BM);
 #pragma unroll
-                    for (int j = 0; j < hg2::BN_CTA / hg2::B_BOX_N; ++j)
-                        tma_load_2d_pair(b_dst + j * hg2::B_BOX_BYTES, &tmB, full_leader,
-                                         tn * hg2::BN + static_cast<int>(rank) * hg2::BN_CTA + j * hg2::B_BOX_N,
-                                         kb * hg2::BK);
+                    for (int hs = 0; hs < NSPLIT; ++hs)
+#pragma unroll
+                        for (int j = 0; j < Cf::BN_HALF / Cf::B_BOX_N; ++j)
+                            tma_load_2d_pair(b_dst + hs * Cf::B_SPLIT_BYTES + j * Cf::B_BOX_BYTES, &tmB, full_leader,
+                                             tn * Cf::BN + hs * 256 + static_cast<int>(rank) * Cf::BN_HALF +
+                                                 j * Cf::B_BOX_N,
+                                             kb * Cf::BK);
                     ++issued;
-                    if (++stage == hg2::STAGES) {
+                    if (++stage == Cf::STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -471,12 +503,12 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
             if (!ok && issued) {
                 if (leader) {
                     // Loads in flight complete on this CTA's full barriers.
-                    const uint32_t n = issued < (uint32_t)hg2::STAGES ? issued : (uint32_t)hg2::STAGES;
+                    const uint32_t n = issued < (uint32_t)Cf::STAGES ? issued : (uint32_t)Cf::STAGES;
                     int s = stage;
                     uint32_t ph = phase;
                     for (uint32_t i = 0; i < n; ++i) {
                         if (--s < 0) {
-                            s = hg2::STAGES - 1;
+                            s = Cf::STAGES - 1;
                             ph ^= 1u;
                         }
                         mbar_wait_drain(&full[s], ph, 1000000000ull);
@@ -507,7 +539,7 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * hg2::ACC_COLS);
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cf::ACC_COLS);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x13,
                                    args.wait_ns)) {
@@ -515,24 +547,29 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_base = smem_u32(sA + stage * hg2::A_BYTES);
-                    const uint32_t b_base = smem_u32(sB + stage * hg2::B_BYTES);
+                    const uint32_t a_base = smem_u32(sA + stage * Cf::A_BYTES);
+                    const uint32_t b_base = smem_u32(sB + stage * Cf::B_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < hg2::BK / 16; ++kk) {
+                    for (int kk = 0; kk < Cf::BK / 16; ++kk) {
                         const uint64_t adesc = sdesc_sw128(a_base + kk * 32, 16, 1024);
-                        const uint64_t bdesc = sdesc_sw128(b_base + kk * 2048, hg2::B_BOX_BYTES, 1024);
-                        umma_f16_pair(d_tmem, adesc, bdesc, hg2::IDESC, (kb | kk) != 0 ? 1u : 0u);
+#pragma unroll
+                        for (int hs = 0; hs < NSPLIT; ++hs) {
+                            const uint64_t bdesc =
+                                sdesc_sw128(b_base + hs * Cf::B_SPLIT_BYTES + kk * 2048, Cf::B_BOX_BYTES, 1024);
+                            umma_f16_pair(d_tmem + static_cast<uint32_t>(hs * 256), adesc, bdesc, Cf::IDESC,
+                                          (kb | kk) != 0 ? 1u : 0u);
+                        }
                     }
                     umma_commit_pair(&empty[stage], 0x3);
                     issued_any = true;
-                    if (++stage == hg2::STAGES) {
+                    if (++stage == Cf::STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
                 umma_commit_pair(&tfull[acc], 0x3);
-                if (++acc == 2) {
+                if (++acc == Cf::ACC_BUFS) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
@@ -546,28 +583,85 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
     } else {
         // ------------------------------------------------ epilogue (both CTAs)
         const int q = warp & 3;
-        const int row_in_tile = static_cast<int>(rank) * hg2::BM + q * 32 + lane;
+        const int row_in_tile = static_cast<int>(rank) * Cf::BM + q * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
         const bool read_c = args.beta != 0.0f;
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t nstore = 0;
         for (int t = pair; t < num_tiles; t += npairs) {
             int tm, tn;
-            tile_coords_g(t, tiles_m, tiles_n, hg2::GROUP_M, tm, tn);
+            tile_coords_g(t, tiles_m, tiles_n, group_m, tm, tn);
             bool ok = mbar_wait_sleepy(&tfull[acc], acc_phase, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x14,
                                 args.wait_ns);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            const int row = tm * 2 * hg2::BM + row_in_tile;
+            const int row = tm * 2 * Cf::BM + row_in_tile;
             const bool row_ok = row < args.M;
             uint16_t *crow = args.C + static_cast<int64_t>(row) * args.N;
+            if (!read_c) {
+                // TMEM -> registers -> alpha -> f16 -> swizzled staging -> TMA
+                // store of a 32-row x 64-column box; the store clips rows and
+                // columns outside C.
+                const int row0 = tm * 2 * Cf::BM + static_cast<int>(rank) * Cf::BM + q * 32;
+                uint8_t *wbuf = stg + (warp - 2) * 2 * Cf::EPI_BUF_BYTES;
 #pragma unroll 1
-            for (int c = 0; c < hg2::BN / 32; ++c) {
+                for (int c = 0; c < Cf::BN / 64; ++c) {
+                    uint32_t r0[32], r1[32];
+                    __syncwarp();
+                    const uint32_t taddr = tmem_base + lane_off + static_cast<uint32_t>(acc * Cf::ACC_COLS + c * 64);
+                    tmem_ld_32x32b_x32(taddr, r0);
+                    tmem_ld_32x32b_x32(taddr + 32, r1);
+                    tmem_ld_wait();
+                    if (c == Cf::BN / 64 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            if (leader)
+                                mbar_arrive(&tempty[acc]);
+                            else
+                                mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+                        }
+                    }
+                    const int col0 = tn * Cf::BN + c * 64;
+                    if (col0 >= args.N || row0 >= args.M) continue;  // warp-uniform
+                    uint8_t *buf = wbuf + (nstore & 1) * Cf::EPI_BUF_BYTES;
+                    if (lane == 0) bulk_wait_group_read<1>();  // the store that used buf last has read it
+                    __syncwarp();
+                    uint8_t *rowp = buf + lane * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t *src = j < 4 ? r0 + 8 * j : r1 + 8 * (j - 4);
+                        uint4 o;
+                        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            oh[e] = __floats2half2_rn(args.alpha * __uint_as_float(src[2 * e]),
+                                                      args.alpha * __uint_as_float(src[2 * e + 1]));
+                        // 128-byte swizzle: 16-byte chunk j of row r sits at chunk j ^ (r % 8)
+                        *reinterpret_cast<uint4 *>(rowp + ((j ^ (lane & 7)) << 4)) = o;
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, buf, col0, row0);
+                        bulk_commit_group();
+                    }
+                    ++nstore;
+                }
+                if (++acc == Cf::ACC_BUFS) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+                continue;
+            }
+#pragma unroll 1
+            for (int c = 0; c < Cf::BN / 32; ++c) {
                 uint32_t r[32];
                 __syncwarp();
-                tmem_ld_32x32b_x32(tmem_base + lane_off + static_cast<uint32_t>(acc * hg2::ACC_COLS + c * 32), r);
+                tmem_ld_32x32b_x32(tmem_base + lane_off + static_cast<uint32_t>(acc * Cf::ACC_COLS + c * 32), r);
                 tmem_ld_wait();
-                if (c == hg2::BN / 32 - 1) {
+                if (c == Cf::BN / 32 - 1) {
                     // This warp's share of the accumulator is in registers:
                     // one arrival per warp on the leader's barrier.
                     tc_fence_before();
@@ -579,25 +673,28 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                             mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
                     }
                 }
-                const int col0 = tn * hg2::BN + c * 32;
+                const int col0 = tn * Cf::BN + c * 32;
                 if (!row_ok || col0 >= args.N) continue;
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = args.alpha * __uint_as_float(r[i]);
                 store_c_chunk(crow, col0, args.N, v, read_c, args.beta);
             }
-            if (++acc == 2) {
+            if (++acc == Cf::ACC_BUFS) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
         }
+        // Every TMA store of this warp has completed before the CTA exits.
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
     }
 
     tc_fence_before();
     cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc_pair(tmem_base, hg2::TMEM_COLS);
+        tmem_dealloc_pair(tmem_base, Cf::TMEM_COLS);
     }
 }
 
@@ -670,14 +767,42 @@ bool hgemm_tc_eligible(size_t m, size_t n, size_t k, const void *A, const void *
 namespace {
 
 struct DeviceLaunchState {
-    bool attr1 = false, attr2 = false;
-    int max_pairs = 0;  // co-resident CTA pairs of hgemm_tc2_kernel
+    bool attr1 = false;
+    bool attr2[2] = {false, false};
+    int max_pairs[2] = {0, 0};  // co-resident CTA pairs of hgemm_tc2_kernel<1>, <2>
 };
 DeviceLaunchState g_hgemm_state[64];
 std::mutex g_hgemm_mu;
 
-int launch_pair_kernel(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, const HgemmArgs &args,
-                       size_t m, size_t n) {
+template <int NSPLIT>
+int max_pairs_of(b2b_handle *h, cudaLaunchConfig_t &cfg) {
+    using Cf = hg2::Cfg<NSPLIT>;
+    std::lock_guard<std::mutex> lk(g_hgemm_mu);
+    DeviceLaunchState &st = g_hgemm_state[h->device & 63];
+    if (!st.attr2[NSPLIT - 1]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(hgemm_tc2_kernel<NSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES);
+        if (e != cudaSuccess) {
+            fail_cuda(e, "hgemm pair smem attribute");
+            return -1;
+        }
+        cfg.gridDim = dim3(2 * (h->sm_count / 2));
+        int clusters = 0;
+        e = cudaOccupancyMaxActiveClusters(&clusters, (void *)hgemm_tc2_kernel<NSPLIT>, &cfg);
+        if (e != cudaSuccess) {
+            fail_cuda(e, "cudaOccupancyMaxActiveClusters");
+            return -1;
+        }
+        st.max_pairs[NSPLIT - 1] = clusters > 0 ? clusters : h->sm_count / 2;
+        st.attr2[NSPLIT - 1] = true;
+    }
+    return st.max_pairs[NSPLIT - 1];
+}
+
+template <int NSPLIT>
+int launch_pair_kernel(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmC,
+                       const HgemmArgs &args, size_t m, size_t n, int max_pairs) {
+    using Cf = hg2::Cfg<NSPLIT>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -685,35 +810,50 @@ int launch_pair_kernel(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap 
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(hg2::THREADS);
-    cfg.dynamicSmemBytes = hg2::SMEM_BYTES;
+    cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
     cfg.stream = h->stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int max_pairs;
-    {
-        std::lock_guard<std::mutex> lk(g_hgemm_mu);
-        DeviceLaunchState &st = g_hgemm_state[h->device & 63];
-        if (!st.attr2) {
-            cudaError_t e =
-                cudaFuncSetAttribute(hgemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hg2::SMEM_BYTES);
-            if (e != cudaSuccess) return fail_cuda(e, "hgemm pair smem attribute");
-            cfg.gridDim = dim3(2 * (h->sm_count / 2));
-            int clusters = 0;
-            e = cudaOccupancyMaxActiveClusters(&clusters, (void *)hgemm_tc2_kernel, &cfg);
-            if (e != cudaSuccess) return fail_cuda(e, "cudaOccupancyMaxActiveClusters");
-            st.max_pairs = clusters > 0 ? clusters : h->sm_count / 2;
-            st.attr2 = true;
-        }
-        max_pairs = st.max_pairs;
-    }
-    const size_t tiles = ((m + 255) / 256) * ((n + hg2::BN - 1) / hg2::BN);
+    const size_t tiles = ((m + 255) / 256) * ((n + Cf::BN - 1) / Cf::BN);
     const int pairs = static_cast<int>(tiles < static_cast<size_t>(max_pairs) ? tiles : max_pairs);
     cfg.gridDim = dim3(2 * pairs);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, hgemm_tc2_kernel, tmA, tmB, args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, hgemm_tc2_kernel<NSPLIT>, tmA, tmB, tmC, args);
     if (e != cudaSuccess) return fail_cuda(e, "hgemm tcgen05 pair launch");
     return B2B_OK;
 }
 
+// Pair-kernel choice: 256 x 512 tiles when K is long enough to amortise
+// their unoverlapped epilogue (K >= 2048; measured on 8192 x 8192: 256 x 256
+// wins at K = 1024, 256 x 512 from K = 4096 on) and they still give every
+// co-resident pair at least one tile; else 256 x 256.  hgemm_variant 2 / 3
+// forces one.
+int launch_pairs(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, const HgemmArgs &args, size_t m,
+                 size_t n) {
+    // C as 32-row x 64-column boxes with the 128-byte swizzle (TMA-store epilogue).
+    CUtensorMap tmC;
+    if (int rc = encode_2d_f16(&tmC, args.C, m, n, 64, 32)) return rc;
+    cudaLaunchConfig_t probe = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    probe.blockDim = dim3(hg2::THREADS);
+    probe.stream = h->stream;
+    probe.attrs = attr;
+    probe.numAttrs = 1;
+    probe.dynamicSmemBytes = hg2::Cfg<2>::SMEM_BYTES;
+    const int wide_pairs = max_pairs_of<2>(h, probe);
+    if (wide_pairs < 0) return B2B_ERR_CUDA;
+    const size_t wide_tiles = ((m + 255) / 256) * ((n + 511) / 512);
+    const bool wide = h->hgemm_variant == 3 || (h->hgemm_variant != 2 && n >= 512 && args.K >= 2048 &&
+                                                 wide_tiles >= static_cast<size_t>(wide_pairs));
+    if (wide) return launch_pair_kernel<2>(h, tmA, tmB, tmC, args, m, n, wide_pairs);
+    probe.dynamicSmemBytes = hg2::Cfg<1>::SMEM_BYTES;
+    const int pairs = max_pairs_of<1>(h, probe);
+    if (pairs < 0) return B2B_ERR_CUDA;
+    return launch_pair_kernel<1>(h, tmA, tmB, tmC, args, m, n, pairs);
+}
 }  // namespace
 
 int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A, const uint16_t *B,
@@ -724,9 +864,10 @@ int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const
         if (rc) return rc;
         rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
         if (rc) return rc;
-        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns};
+        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns, h->hgemm_group_m};
         // More than one 128-row tile: CTA pairs with 256 x 256 tiles.
-        if (m > static_cast<size_t>(hg::BM) && !h->force_single_cta) return launch_pair_kernel(h, tmA, tmB, args, m, n);
+        if (m > static_cast<size_t>(hg::BM) && !h->force_single_cta && h->hgemm_variant != 1)
+            return launch_pairs(h, tmA, tmB, args, m, n);
         {
             std::lock_guard<std::mutex> lk(g_hgemm_mu);
             DeviceLaunchState &st = g_hgemm_state[h->device & 63];

@@ -53,6 +53,8 @@ struct b2b_handle {
     bool force_single_cta = false;
     // SGEMM kernel configuration (B2B_SGEMM_VARIANT; 0 = the default).
     int sgemm_variant = 0;
+    int hgemm_variant = 0;              // 0 auto, 1 single CTA, 2 pair 256x256, 3 pair 256x512
+    int hgemm_group_m = 0;              // pair kernels' raster group override (0 = default)
     // DGEMM kernel configuration (B2B_DGEMM_VARIANT; 0 = the default).
     int dgemm_variant = 0;
 };

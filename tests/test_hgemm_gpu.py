@@ -132,3 +132,37 @@ def test_pair_kernel_matches_single_cta_kernel(oracle, monkeypatch):
         assert oracle.rel_err(o, ref) <= 2e-3
     diff = np.abs(outs[0].view(np.float16).astype(np.float64) - outs[1].view(np.float16).astype(np.float64))
     assert np.max(diff) <= 2 * np.max(np.abs(ref)) * 2 ** -10
+
+
+VARIANT_SHAPES = [(1024, 1280, 768), (257, 520, 1000), (300, 264, 72), (256, 512, 64), (129, 1024, 136),
+                  (777, 1536, 200), (2048, 2560, 1024)]
+
+
+@pytest.mark.parametrize("m,n,k", VARIANT_SHAPES)
+@pytest.mark.parametrize("beta", [0.0, -0.5])
+def test_hgemm_kernel_variants_agree(oracle, monkeypatch, m, n, k, beta):
+    # Single-CTA 128x256 (variant 1), pair 256x256 (2) and pair 256x512 (3),
+    # forced through B2B_HGEMM_VARIANT, on shapes with ragged M/N/K edges:
+    # each within the FP64 bound, and all three within an f16 ulp or two.
+    # beta == 0 takes the pair kernels' TMA-store epilogue, beta != 0 the
+    # read-modify-write one.
+    import b2blas
+
+    A = oracle.normal_f16(m * k, 6, 1, 0.0, 0.1)
+    B = oracle.normal_f16(k * n, 6, 2, 0.0, 0.1)
+    C = oracle.normal_f16(m * n, 6, 3, 0.0, 0.1)
+    ref = oracle.hgemm_f64(m, n, k, 0.75, A, B, beta, C)
+    outs = []
+    for v in ("1", "2", "3"):
+        monkeypatch.setenv("B2B_HGEMM_VARIANT", v)
+        h = b2blas.Handle(0)
+        try:
+            outs.append(_run(h, m, n, k, 0.75, beta, A, B, C))
+        finally:
+            h.close()
+    for o in outs:
+        assert oracle.rel_err(o, ref) <= 2e-3
+    scale = 2 * np.max(np.abs(ref)) * 2 ** -10
+    for o in outs[1:]:
+        d = np.abs(o.view(np.float16).astype(np.float64) - outs[0].view(np.float16).astype(np.float64))
+        assert np.max(d) <= scale

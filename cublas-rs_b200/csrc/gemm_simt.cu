@@ -424,13 +424,18 @@ struct AsyncCfg {
     static constexpr int LDB_S = BN;                              // Bs[k][n]
     static constexpr int A_STAGE = BK * LDA_S;
     static constexpr int B_STAGE = BK * LDB_S;
-    static constexpr int A_COPIES = BM * BK / NT;         // element copies per thread
-    static constexpr int A_ROWS_PER_PASS = NT / BK;       // rows covered by one pass of the CTA
+    // A copies: each warp writes 4 rows x 8 consecutive k per instruction
+    // (conflict-free in the transposed As[k][m] layout, whose pitch is 4
+    // banks off a multiple of 32), repeated over row passes and 8-wide k groups.
+    static constexpr int A_ROWS_PER_PASS = NT / 8;        // rows covered by one pass of the CTA
+    static constexpr int A_PASSES = BM / A_ROWS_PER_PASS;
+    static constexpr int A_KGROUPS = BK / 8;
+    static constexpr int A_COPIES = A_PASSES * A_KGROUPS;  // element copies per thread
     static constexpr int B_COPIES = BK * BN / VW / NT;    // 16-byte copies per thread
     static constexpr int B_VECS_PER_ROW = BN / VW;
     static constexpr int B_ROWS_PER_PASS = NT / B_VECS_PER_ROW;
     static constexpr int SMEM = STAGES * (A_STAGE + B_STAGE) * static_cast<int>(sizeof(T));
-    static_assert(NT % BK == 0 && A_COPIES * NT == BM * BK, "A tile divides");
+    static_assert(BK % 8 == 0 && BM % A_ROWS_PER_PASS == 0 && A_COPIES * NT == BM * BK, "A tile divides");
     static_assert(NT % B_VECS_PER_ROW == 0 && B_COPIES * NT * VW == BK * BN, "B tile divides");
 };
 
@@ -468,11 +473,11 @@ __global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
     const int row_base = wm * (TM / 4) * 16 + ty * 4;
     const int col_base = wn * (TN / 4) * 32 + tx * 4;
 
-    // Copy assignment.  A: this thread copies element (r0 + p*A_ROWS_PER_PASS,
-    // ka) of the A tile for p = 0..A_COPIES-1; B: 16-byte vector
-    // (kb0 + p*B_ROWS_PER_PASS, cb) of the B tile.  Only two global base
-    // pointers and a few scalars live across the main loop.
-    const int ka = tid % BK, r0 = tid / BK;
+    // Copy assignment.  A: this thread copies element (r0 + q*A_ROWS_PER_PASS,
+    // ka + 8*g) of the A tile for every row pass q and k group g; B: 16-byte
+    // vector (kb0 + p*B_ROWS_PER_PASS, cb) of the B tile.  Only two global
+    // base pointers and a few scalars live across the main loop.
+    const int ka = tid % 8, r0 = tid / 8;
     const int cb = (tid % Cf::B_VECS_PER_ROW) * VW, kb0 = tid / Cf::B_VECS_PER_ROW;
     const int64_t rows_left = M - m0 - r0;  // copy p is in range iff p*A_ROWS_PER_PASS < rows_left
     const bool col_ok = n0 + cb < N;        // N % VW == 0: a vector is all in or all out
@@ -488,12 +493,16 @@ __global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
         const int64_t k0 = kt * BK;
         const uint32_t a_st = sa0 + static_cast<uint32_t>(stage * Cf::A_STAGE * ES);
         const uint32_t b_st = sb0 + static_cast<uint32_t>(stage * Cf::B_STAGE * ES);
-        const bool ka_ok = k0 + ka < K;
-        const T *pa = ga + k0;
 #pragma unroll
-        for (int p = 0; p < Cf::A_COPIES; ++p) {
-            const bool ok = ka_ok && p * Cf::A_ROWS_PER_PASS < rows_left;
-            cp_async_elem<T>(a_st + p * Cf::A_ROWS_PER_PASS * ES, ok ? pa + p * a_pass : A, ok);
+        for (int g = 0; g < Cf::A_KGROUPS; ++g) {
+            const bool ka_ok = k0 + ka + 8 * g < K;
+            const T *pa = ga + k0 + 8 * g;
+#pragma unroll
+            for (int q = 0; q < Cf::A_PASSES; ++q) {
+                const bool ok = ka_ok && q * Cf::A_ROWS_PER_PASS < rows_left;
+                cp_async_elem<T>(a_st + (8 * g * Cf::LDA_S + q * Cf::A_ROWS_PER_PASS) * ES, ok ? pa + q * a_pass : A,
+                                 ok);
+            }
         }
         const T *pb = gb + k0 * N;
 #pragma unroll
@@ -629,6 +638,7 @@ int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float
         case 10: return run_async<float, 16, 8, 2, 4, 16, 2, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
         case 11: return run_async<float, 16, 8, 2, 4, 8, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
         case 12: return run_async<float, 8, 8, 4, 4, 16, 3, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
+        case 13: return run_async<float, 16, 8, 2, 4, 16, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
         default: return run_async<float, 16, 8, 2, 4, 8, 4, 1>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
     }
 }

@@ -161,13 +161,25 @@ class ClockSampler:
 
 # ------------------------------------------------------------ workloads
 
+# Which page-locked allocator the end-to-end pass uses: the library's
+# (b2b_host_alloc = cudaHostAlloc) or torch's pin_memory.
+E2E_HOST = {"handle": None}
+
+
 def _pinned_numpy(t):
     """Page-locked host copy of a device tensor, as a numpy array."""
+    import numpy as np
     import torch
 
-    h = torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=True)
-    h.copy_(t)
-    return h, h.numpy()
+    h = E2E_HOST["handle"]
+    if h is not None:
+        np_dt = {torch.float16: np.float16, torch.float32: np.float32, torch.float64: np.float64}[t.dtype]
+        arr = h.host_empty(t.numel(), np_dt).reshape(tuple(t.shape))
+        arr[...] = t.cpu().numpy()
+        return arr, arr
+    ht = torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=True)
+    ht.copy_(t)
+    return ht, ht.numpy()
 
 
 class Workload:
@@ -908,7 +920,7 @@ def run_reference(args, rank, world):
     return 0
 
 
-def run_e2e(w, h, stream, steps, world, dist, barrier):
+def run_e2e(w, h, stream, steps, world, dist, barrier, host_alloc="b2b"):
     """The same metric through the host-slice API: page-locked host inputs
     copied in and the result copied out inside every timed step."""
     import torch
@@ -930,7 +942,8 @@ def run_e2e(w, h, stream, steps, world, dist, barrier):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     value = w.scale(w.units_per_step() * world * steps / (float(t.item()) / 1e3))
     return {"value": value, "unit": w.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": steps, "api": "host-slice (_simple) calls on page-locked host buffers"}
+            "steps": steps, "api": "host-slice (_simple) calls on page-locked host buffers",
+            "host_alloc": "b2b_host_alloc (cudaHostAlloc)" if host_alloc == "b2b" else "torch pin_memory"}
 
 
 # ------------------------------------------------------------------ main
@@ -949,6 +962,8 @@ def main():
     ap.add_argument("--tf32x3", action="store_true", help="sgemm/mlp: the opt-in 3xTF32 tensor-core kernel")
     ap.add_argument("--fused", action="store_true", help="mlp: bias (+ReLU) fused into the SGEMM epilogue")
     ap.add_argument("--e2e-steps", type=int, default=None, help="0 skips the end-to-end pass")
+    ap.add_argument("--e2e-host", choices=["b2b", "torch"], default="b2b",
+                    help="page-locked host buffers of the end-to-end pass: b2b_host_alloc or torch pin_memory")
     ap.add_argument("--m", type=int, default=None, help="GEMM size override (profiling small cases)")
     ap.add_argument("--n", type=int, default=None)
     ap.add_argument("--k", type=int, default=None)
@@ -989,6 +1004,8 @@ def main():
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     h.set_stream(stream.cuda_stream)
+    if args.e2e_host == "b2b":
+        E2E_HOST["handle"] = h
     w = make_workload(args.workload, h, rank, world, args)
     torch.cuda.synchronize()
 
@@ -1057,7 +1074,7 @@ def main():
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(3, min(args.steps, 10))
     e2e = None
     if e2e_steps > 0:
-        e2e = run_e2e(w, h, stream, e2e_steps, world, dist, barrier)
+        e2e = run_e2e(w, h, stream, e2e_steps, world, dist, barrier, args.e2e_host)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

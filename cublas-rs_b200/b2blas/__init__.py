@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import ctypes
 import enum
+import weakref
 from dataclasses import dataclass
 from typing import Any, Sequence
 
@@ -248,6 +249,17 @@ class Handle:
         nbytes = int(length) * np.dtype(dtype).itemsize
         _check(self._lib.b2b_malloc(self._h, nbytes, ctypes.byref(p)))
         return DeviceBuffer(self, p.value or 0, length, dtype)
+
+    def host_empty(self, length: int, dtype=np.float32) -> np.ndarray:
+        """A numpy array in page-locked host memory from b2b_host_alloc
+        (cudaHostAlloc), freed when the array is garbage-collected.  Host
+        slices in such memory copy at full PCIe rate in both directions."""
+        nbytes = max(int(length) * np.dtype(dtype).itemsize, 1)
+        p = ctypes.c_void_p()
+        _check(self._lib.b2b_host_alloc(nbytes, ctypes.byref(p)))
+        raw = (ctypes.c_char * nbytes).from_address(p.value)
+        weakref.finalize(raw, _lib.load().b2b_host_free, ctypes.c_void_p(p.value))
+        return np.frombuffer(raw, dtype=dtype, count=int(length))
 
     def upload(self, host: np.ndarray) -> DeviceBuffer:
         host = np.ascontiguousarray(host)

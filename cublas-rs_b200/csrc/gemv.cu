@@ -5,10 +5,12 @@
 //
 // SGEMV reads every element of A once, so it is bound by HBM bandwidth; the
 // kernels are built to keep enough 16-byte loads in flight:
-//   * N: one warp per row; each lane streams 16-byte vectors of the row with
+//   * N: S warps per row (S = 1..8, rows cut into ~16 KiB segments); each
+//     lane streams 16-byte vectors of its segment with
 //     ld.global.nc.L1::no_allocate (A is touched once, keep it out of L1),
 //     UNROLL vectors in flight per lane, while x is read through L1 (it is
-//     shared by every row); warp-shuffle reduction, lane 0 writes y.
+//     shared by every row); warp-shuffle reduction, the S partials added in
+//     segment order through shared memory.
 //   * T: the rows are split into S slices; CTA (column block, slice) walks
 //     its slice with each lane owning 4 consecutive columns (16-byte loads
 //     across the row, coalesced), reduces its 8 warps through shared memory
@@ -50,51 +52,107 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-template <int UNROLL, bool VEC>
+// N: S warps share a row, warp s summing the s-th of S contiguous column
+// segments; the S partials meet in shared memory and are added in segment
+// order (deterministic).  Long rows split this way give the grid more,
+// shorter work units: a warp streaming one 64-128 KiB row alone holds the
+// GPU's last wave open.
+template <int UNROLL, bool VEC, int S>
 __global__ void __launch_bounds__(kThreads) sgemv_n_kernel(const float *__restrict__ A, const float *__restrict__ x,
                                                            float *__restrict__ y, int64_t m, int64_t n, float alpha,
                                                            float beta) {
-    const int lane = threadIdx.x & 31;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
-    if (row >= m) return;
+    static_assert(kWarps % S == 0, "segments per row divide the CTA's warps");
+    __shared__ float part[kWarps];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (kWarps / S) + warp / S;
+    const int seg = warp % S;
     float acc = 0.0f;
-    if constexpr (VEC) {
-        const float4 *a = reinterpret_cast<const float4 *>(A + row * n);
-        const float4 *xv = reinterpret_cast<const float4 *>(x);
-        const int64_t nv = n >> 2;
-        int64_t j = lane;
-        // Full groups: UNROLL independent 16-byte loads per lane in flight.
-        for (; j + 32 * (UNROLL - 1) < nv; j += 32 * UNROLL) {
-            float4 av[UNROLL], xx[UNROLL];
+    if (row < m) {
+        if constexpr (VEC) {
+            const float4 *a = reinterpret_cast<const float4 *>(A + row * n);
+            const float4 *xv = reinterpret_cast<const float4 *>(x);
+            const int64_t nv = n >> 2;
+            const int64_t seg_len = (nv + S - 1) / S;
+            const int64_t v0 = seg * seg_len, v1 = v0 + seg_len < nv ? v0 + seg_len : nv;
+            int64_t j = v0 + lane;
+            // Full groups: UNROLL independent 16-byte loads per lane in flight.
+            for (; j + 32 * (UNROLL - 1) < v1; j += 32 * UNROLL) {
+                float4 av[UNROLL], xx[UNROLL];
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) av[u] = ld_stream(a + j + 32 * u);
+                for (int u = 0; u < UNROLL; ++u) av[u] = ld_stream(a + j + 32 * u);
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) xx[u] = __ldg(xv + j + 32 * u);
+                for (int u = 0; u < UNROLL; ++u) xx[u] = __ldg(xv + j + 32 * u);
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) {
-                acc = fmaf(av[u].x, xx[u].x, acc);
-                acc = fmaf(av[u].y, xx[u].y, acc);
-                acc = fmaf(av[u].z, xx[u].z, acc);
-                acc = fmaf(av[u].w, xx[u].w, acc);
+                for (int u = 0; u < UNROLL; ++u) {
+                    acc = fmaf(av[u].x, xx[u].x, acc);
+                    acc = fmaf(av[u].y, xx[u].y, acc);
+                    acc = fmaf(av[u].z, xx[u].z, acc);
+                    acc = fmaf(av[u].w, xx[u].w, acc);
+                }
             }
+            for (; j < v1; j += 32) {
+                float4 av = ld_stream(a + j), xx = __ldg(xv + j);
+                acc = fmaf(av.x, xx.x, acc);
+                acc = fmaf(av.y, xx.y, acc);
+                acc = fmaf(av.z, xx.z, acc);
+                acc = fmaf(av.w, xx.w, acc);
+            }
+        } else {
+            const float *a = A + row * n;
+            const int64_t seg_len = (n + S - 1) / S;
+            const int64_t c0 = seg * seg_len, c1 = c0 + seg_len < n ? c0 + seg_len : n;
+            for (int64_t j = c0 + lane; j < c1; j += 32) acc = fmaf(ld_stream1(a + j), __ldg(x + j), acc);
         }
-        for (; j < nv; j += 32) {
-            float4 av = ld_stream(a + j), xx = __ldg(xv + j);
-            acc = fmaf(av.x, xx.x, acc);
-            acc = fmaf(av.y, xx.y, acc);
-            acc = fmaf(av.z, xx.z, acc);
-            acc = fmaf(av.w, xx.w, acc);
-        }
-    } else {
-        const float *a = A + row * n;
-        for (int64_t j = lane; j < n; j += 32) acc = fmaf(ld_stream1(a + j), __ldg(x + j), acc);
+        acc = warp_sum(acc);
     }
-    acc = warp_sum(acc);
-    if (lane == 0) {
+    if constexpr (S > 1) {
+        if (lane == 0) part[warp] = acc;
+        __syncthreads();
+        if (seg == 0 && lane == 0 && row < m) {
+            float t = part[warp];
+#pragma unroll
+            for (int q = 1; q < S; ++q) t += part[warp + q];
+            acc = t;
+        }
+    }
+    if (seg == 0 && lane == 0 && row < m) {
         float v = alpha * acc;
         if (beta != 0.0f) v = fmaf(beta, y[row], v);
         y[row] = v;
     }
+}
+
+// Segments per row for the N kernels: rows of `row_bytes` are cut into
+// pieces of about `seg_bytes` (a power of two count, at most 8).
+inline int gemv_segments(int64_t row_bytes, int64_t seg_bytes) {
+    int S = 1;
+    while (S < 8 && row_bytes >= 2 * S * seg_bytes) S *= 2;
+    return S;
+}
+
+template <bool VEC>
+cudaError_t launch_sgemv_n_vec(b2b_handle *h, const float *A, const float *x, float *y, int64_t m, int64_t n,
+                               float alpha, float beta, int S) {
+    const int64_t rows_per_cta = kWarps / S;
+    const unsigned blocks = static_cast<unsigned>((m + rows_per_cta - 1) / rows_per_cta);
+    switch (S) {
+        case 1: sgemv_n_kernel<8, VEC, 1><<<blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta); break;
+        case 2: sgemv_n_kernel<8, VEC, 2><<<blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta); break;
+        case 4: sgemv_n_kernel<8, VEC, 4><<<blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta); break;
+        default: sgemv_n_kernel<8, VEC, 8><<<blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta); break;
+    }
+    return cudaGetLastError();
+}
+
+// The N launch shared by b2b_sgemv and b2b_sgemv_noalloc.
+int launch_sgemv_n(b2b_handle *h, const float *A, const float *x, float *y, int64_t m, int64_t n, float alpha,
+                   float beta) {
+    const bool vec = (n % 4 == 0) && b2b::aligned16(A) && b2b::aligned16(x);
+    const int S = gemv_segments(n * 4, h->gemv_seg_bytes);
+    if ((m + kWarps / S - 1) / (kWarps / S) > 0x7fffffffLL) return b2b::fail(B2B_ERR_INVALID_ARG, "sgemv: m too large");
+    const cudaError_t e = vec ? launch_sgemv_n_vec<true>(h, A, x, y, m, n, alpha, beta, S)
+                              : launch_sgemv_n_vec<false>(h, A, x, y, m, n, alpha, beta, S);
+    return e == cudaSuccess ? B2B_OK : b2b::fail_cuda(e, "sgemv N launch");
 }
 
 // T, pass 1: CTA (blockIdx.x = column block of 128, blockIdx.y = row slice).
@@ -191,19 +249,8 @@ namespace b2b {
 int launch_sgemv(b2b_handle *h, int trans, size_t m_, size_t n_, float alpha, const float *A, const float *x,
                  float beta, float *y) {
     const int64_t m = static_cast<int64_t>(m_), n = static_cast<int64_t>(n_);
-    const bool vec = (n % 4 == 0) && aligned16(A) && aligned16(x);
     cudaError_t e;
-    if (trans == B2B_OP_N) {
-        const int64_t blocks = (m + kWarps - 1) / kWarps;
-        if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemv: m too large");
-        if (vec)
-            sgemv_n_kernel<8, true><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
-        else
-            sgemv_n_kernel<8, false><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return fail_cuda(e, "sgemv N launch");
-        return B2B_OK;
-    }
+    if (trans == B2B_OP_N) return launch_sgemv_n(h, A, x, y, m, n, alpha, beta);
     const bool vec_t = (n % 4 == 0) && aligned16(A);
     const int64_t col_blocks = (n + 127) / 128;
     if (col_blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemv: n too large");
@@ -296,16 +343,7 @@ extern "C" int b2b_sgemv_noalloc(b2b_handle *h, int trans, size_t m_, size_t n_,
     DeviceGuard g(h);
     const int64_t m = static_cast<int64_t>(m_), n = static_cast<int64_t>(n_);
     cudaError_t e;
-    if (trans == B2B_OP_N) {  // the N kernel needs no scratch
-        const int64_t blocks = (m + kWarps - 1) / kWarps;
-        if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: m too large");
-        if ((n % 4 == 0) && aligned16(A) && aligned16(x))
-            sgemv_n_kernel<8, true><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
-        else
-            sgemv_n_kernel<8, false><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
-        e = cudaGetLastError();
-        return e == cudaSuccess ? B2B_OK : fail_cuda(e, "b2b_sgemv_noalloc: N launch");
-    }
+    if (trans == B2B_OP_N) return launch_sgemv_n(h, A, x, y, m, n, alpha, beta);  // needs no scratch
     // T: the same slicing as b2b_sgemv, so both give the same bits.
     const bool vec_t = (n % 4 == 0) && aligned16(A);
     const int64_t col_blocks = (n + 127) / 128;

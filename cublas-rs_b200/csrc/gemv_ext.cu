@@ -4,8 +4,9 @@
 // f16 in/out, f32 accumulate, alpha/beta as f32).
 //
 // Same streaming structure as SGEMV (gemv.cu), templated on the element type:
-//   * N: one warp per row, 16-byte loads of A (2 doubles / 8 halves) with
-//     ld.global.nc.L1::no_allocate, x through L1, shuffle reduction.
+//   * N: S warps per row (rows cut into ~16 KiB segments), 16-byte loads of
+//     A (2 doubles / 8 halves) with ld.global.nc.L1::no_allocate, x through
+//     L1, shuffle reduction, partials added in segment order.
 //   * T: split-row partial sums (as many row slices as fill one resident
 //     wave of CTAs), four rows' loads in flight per lane, each lane owning one
 //     16-byte column group, ordered second-pass reduction; partials in the
@@ -85,52 +86,129 @@ __device__ __forceinline__ Acc warp_sum(Acc v) {
     return v;
 }
 
-template <typename T, bool VEC>
+// N: S warps per row, warp s summing the s-th of S contiguous column
+// segments; partials added in segment order through shared memory.
+template <typename T, bool VEC, int S>
 __global__ void __launch_bounds__(kThreads) gemvx_n_kernel(const T *__restrict__ A, const T *__restrict__ x,
                                                            T *__restrict__ y, int64_t m, int64_t n,
                                                            typename GV<T>::Acc alpha, typename GV<T>::Acc beta) {
     using Acc = typename GV<T>::Acc;
     constexpr int W = GV<T>::W;
     constexpr int UNROLL = 4;
-    const int lane = threadIdx.x & 31;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
-    if (row >= m) return;
-    const T *a = A + row * n;
-    Acc acc = Acc(0);
-    if constexpr (VEC) {
-        const int64_t nv = n / W;
-        int64_t j = lane;
-        for (; j + 32 * (UNROLL - 1) < nv; j += 32 * UNROLL) {
-            uint4 ar[UNROLL], xr[UNROLL];
+    static_assert(kWarps % S == 0, "segments per row divide the CTA's warps");
+    if constexpr (S == 1) {
+        // One warp per row: no shared memory, finished warps leave early.
+        const int lane = threadIdx.x & 31;
+        const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+        if (row >= m) return;
+        const T *a = A + row * n;
+        Acc acc = Acc(0);
+        if constexpr (VEC) {
+            const int64_t nv = n / W;
+            int64_t j = lane;
+            for (; j + 32 * (UNROLL - 1) < nv; j += 32 * UNROLL) {
+                uint4 ar[UNROLL], xr[UNROLL];
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) ar[u] = ld_stream16(a + (j + 32 * u) * W);
+                for (int u = 0; u < UNROLL; ++u) ar[u] = ld_stream16(a + (j + 32 * u) * W);
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) xr[u] = ld_cached16(x + (j + 32 * u) * W);
+                for (int u = 0; u < UNROLL; ++u) xr[u] = ld_cached16(x + (j + 32 * u) * W);
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) {
+                for (int u = 0; u < UNROLL; ++u) {
+                    Acc av[W], xv[W];
+                    GV<T>::unpack(ar[u], av);
+                    GV<T>::unpack(xr[u], xv);
+#pragma unroll
+                    for (int e = 0; e < W; ++e) acc = fma(av[e], xv[e], acc);
+                }
+            }
+            for (; j < nv; j += 32) {
                 Acc av[W], xv[W];
-                GV<T>::unpack(ar[u], av);
-                GV<T>::unpack(xr[u], xv);
+                GV<T>::unpack(ld_stream16(a + j * W), av);
+                GV<T>::unpack(ld_cached16(x + j * W), xv);
 #pragma unroll
                 for (int e = 0; e < W; ++e) acc = fma(av[e], xv[e], acc);
             }
+        } else {
+            for (int64_t j = lane; j < n; j += 32) acc = fma(GV<T>::get_stream(a + j), GV<T>::get(x + j), acc);
         }
-        for (; j < nv; j += 32) {
-            Acc av[W], xv[W];
-            GV<T>::unpack(ld_stream16(a + j * W), av);
-            GV<T>::unpack(ld_cached16(x + j * W), xv);
-#pragma unroll
-            for (int e = 0; e < W; ++e) acc = fma(av[e], xv[e], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            Acc v = alpha * acc;
+            if (beta != Acc(0)) v = fma(beta, GV<T>::get(y + row), v);
+            y[row] = GV<T>::put(v);
         }
-    } else {
-        for (int64_t j = lane; j < n; j += 32) acc = fma(GV<T>::get_stream(a + j), GV<T>::get(x + j), acc);
+        return;
     }
-    acc = warp_sum(acc);
-    if (lane == 0) {
+    __shared__ Acc part[kWarps];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (kWarps / S) + warp / S;
+    const int seg = warp % S;
+    Acc acc = Acc(0);
+    if (row < m) {
+        const T *a = A + row * n;
+        if constexpr (VEC) {
+            const int64_t nv = n / W;
+            const int64_t seg_len = (nv + S - 1) / S;
+            const int64_t v0 = seg * seg_len, v1 = v0 + seg_len < nv ? v0 + seg_len : nv;
+            int64_t j = v0 + lane;
+            for (; j + 32 * (UNROLL - 1) < v1; j += 32 * UNROLL) {
+                uint4 ar[UNROLL], xr[UNROLL];
+#pragma unroll
+                for (int u = 0; u < UNROLL; ++u) ar[u] = ld_stream16(a + (j + 32 * u) * W);
+#pragma unroll
+                for (int u = 0; u < UNROLL; ++u) xr[u] = ld_cached16(x + (j + 32 * u) * W);
+#pragma unroll
+                for (int u = 0; u < UNROLL; ++u) {
+                    Acc av[W], xv[W];
+                    GV<T>::unpack(ar[u], av);
+                    GV<T>::unpack(xr[u], xv);
+#pragma unroll
+                    for (int e = 0; e < W; ++e) acc = fma(av[e], xv[e], acc);
+                }
+            }
+            for (; j < v1; j += 32) {
+                Acc av[W], xv[W];
+                GV<T>::unpack(ld_stream16(a + j * W), av);
+                GV<T>::unpack(ld_cached16(x + j * W), xv);
+#pragma unroll
+                for (int e = 0; e < W; ++e) acc = fma(av[e], xv[e], acc);
+            }
+        } else {
+            const int64_t seg_len = (n + S - 1) / S;
+            const int64_t c0 = seg * seg_len, c1 = c0 + seg_len < n ? c0 + seg_len : n;
+            for (int64_t j = c0 + lane; j < c1; j += 32) acc = fma(GV<T>::get_stream(a + j), GV<T>::get(x + j), acc);
+        }
+        acc = warp_sum(acc);
+    }
+    if constexpr (S > 1) {
+        if (lane == 0) part[warp] = acc;
+        __syncthreads();
+        if (seg == 0 && lane == 0 && row < m) {
+            Acc t = part[warp];
+#pragma unroll
+            for (int q = 1; q < S; ++q) t += part[warp + q];
+            acc = t;
+        }
+    }
+    if (seg == 0 && lane == 0 && row < m) {
         Acc v = alpha * acc;
         if (beta != Acc(0)) v = fma(beta, GV<T>::get(y + row), v);
         y[row] = GV<T>::put(v);
     }
+}
+
+template <typename T, bool VEC>
+cudaError_t launch_gemvx_n(b2b_handle *h, const T *A, const T *x, T *y, int64_t m, int64_t n,
+                           typename GV<T>::Acc alpha, typename GV<T>::Acc beta, int S) {
+    const int64_t rows_per_cta = kWarps / S;
+    const unsigned blocks = static_cast<unsigned>((m + rows_per_cta - 1) / rows_per_cta);
+    switch (S) {
+        case 1: gemvx_n_kernel<T, VEC, 1><<<blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta); break;
+        case 2: gemvx_n_kernel<T, VEC, 2><<<blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta); break;
+        case 4: gemvx_n_kernel<T, VEC, 4><<<blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta); break;
+        default: gemvx_n_kernel<T, VEC, 8><<<blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta); break;
+    }
+    return cudaGetLastError();
 }
 
 // T, pass 1: CTA (column block of 32*W columns, row slice); lane l owns
@@ -233,13 +311,16 @@ int run_gemvx(b2b_handle *h, int trans, int64_t m, int64_t n, typename GV<T>::Ac
     cudaError_t e;
     if (trans == B2B_OP_N) {
         const bool vec = (n % W == 0) && b2b::aligned16(A) && b2b::aligned16(x);
-        const int64_t blocks = (m + kWarps - 1) / kWarps;
-        if (blocks > 0x7fffffffLL) return b2b::fail(B2B_ERR_INVALID_ARG, "gemv: m too large");
-        if (vec)
-            gemvx_n_kernel<T, true><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
-        else
-            gemvx_n_kernel<T, false><<<(unsigned)blocks, kThreads, 0, h->stream>>>(A, x, y, m, n, alpha, beta);
-        e = cudaGetLastError();
+        // Row segments of about gemv_seg_bytes (twice that for f16, whose
+        // unpacking makes short segments slower: HGEMV 16384^2 takes 79 us
+        // with whole 32 KiB rows per warp, 91 us with 16 KiB segments; DGEMV
+        // 16384^2 325 us whole, 301 us in 16 KiB segments).
+        const int64_t seg_bytes = h->gemv_seg_bytes * (sizeof(T) == 2 ? 2 : 1);
+        int S = 1;
+        while (S < 8 && n * static_cast<int64_t>(sizeof(T)) >= 2 * S * seg_bytes) S *= 2;
+        if ((m + kWarps / S - 1) / (kWarps / S) > 0x7fffffffLL) return b2b::fail(B2B_ERR_INVALID_ARG, "gemv: m too large");
+        e = vec ? launch_gemvx_n<T, true>(h, A, x, y, m, n, alpha, beta, S)
+                : launch_gemvx_n<T, false>(h, A, x, y, m, n, alpha, beta, S);
         return e == cudaSuccess ? B2B_OK : b2b::fail_cuda(e, "gemv N launch");
     }
     const bool vec = (n % W == 0) && b2b::aligned16(A);

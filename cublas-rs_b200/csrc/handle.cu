@@ -193,6 +193,7 @@ int b2b_destroy(b2b_handle *h) {
     if (h->down_stream) cudaStreamSynchronize(h->down_stream);
     for (int i = 0; i < h->pipe_event_count; ++i) cudaEventDestroy(h->pipe_events[i]);
     delete[] h->pipe_events;
+    if (h->switch_event) cudaEventDestroy(h->switch_event);
     if (h->down_stream) cudaStreamDestroy(h->down_stream);
     if (h->workspace) cudaFree(h->workspace);
     if (h->staging) cudaFree(h->staging);
@@ -211,7 +212,17 @@ int b2b_get_stream(b2b_handle *h, void **stream) {
 
 int b2b_set_stream(b2b_handle *h, void *stream) {
     if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_set_stream: NULL handle");
-    h->stream = stream ? reinterpret_cast<cudaStream_t>(stream) : h->own_stream;
+    cudaStream_t next = stream ? reinterpret_cast<cudaStream_t>(stream) : h->own_stream;
+    if (next == h->stream) return B2B_OK;
+    // Order the new stream behind the work already queued on the old one:
+    // both use the handle's workspace and reduction counter.
+    DeviceGuard g(h);
+    cudaError_t e = cudaSuccess;
+    if (!h->switch_event) e = cudaEventCreateWithFlags(&h->switch_event, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(h->switch_event, h->stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(next, h->switch_event, 0);
+    if (e != cudaSuccess) return fail_cuda(e, "b2b_set_stream");
+    h->stream = next;
     return B2B_OK;
 }
 

@@ -27,6 +27,7 @@ struct b2b_handle {
     cudaStream_t own_stream = nullptr;  // created by b2b_create
     cudaStream_t stream = nullptr;      // where work is issued (own or caller's)
     int *d_status = nullptr;            // device status block (layout above)
+    cudaEvent_t switch_event = nullptr; // orders a newly set stream behind the previous one
     // Grow-only device scratch for kernels that need it (split reductions).
     void *workspace = nullptr;
     size_t workspace_bytes = 0;

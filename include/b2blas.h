@@ -82,7 +82,11 @@ B2B_API int b2b_get_stream(b2b_handle *h, void **stream);
 /* Run subsequent calls on a caller-owned cudaStream_t.  NULL selects the
  * handle's own stream again; the legacy default stream is selected with
  * cudaStreamLegacy ((void *)0x1).  No reference counterpart; the cuBLAS
- * equivalent is cublasSetStream.  Used to share a stream with torch / NCCL. */
+ * equivalent is cublasSetStream.  Used to share a stream with torch / NCCL.
+ * Switching streams makes the new stream wait (an event) for the work already
+ * queued on the previous one, because every call reuses the handle's
+ * workspace and reduction counter.  Handles are not thread-safe: use one per
+ * thread. */
 B2B_API int b2b_set_stream(b2b_handle *h, void *stream);
 /* Handle::synchronize (lib.rs:79-82): blocks on the stream, then reports a
  * device-side bounded-wait timeout, if one was recorded, as

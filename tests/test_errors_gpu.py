@@ -97,6 +97,41 @@ def test_set_stream_roundtrip(handle):
     handle.set_stream(None)
 
 
+def test_stream_switch_orders_workspace_users(oracle):
+    # SGEMV-T keeps its split-row partials in the handle's workspace.  A call
+    # queued on stream 1 and one queued right after switching to stream 2
+    # (which does not wait for stream 1 on its own) must not share the
+    # partials: the switch orders stream 2 behind stream 1.
+    import torch
+
+    import b2blas
+
+    h = b2blas.Handle(0)
+    try:
+        m, n = 8192, 4096
+        outs, refs = [], []
+        streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+        bufs = []
+        for i in range(2):
+            A = oracle.uniform_f32(m * n, 60 + i, 1)
+            x = oracle.uniform_f32(m, 60 + i, 2)
+            refs.append(oracle.sgemv_f64(1, m, n, 1.0, A, x, 0.0, np.zeros(n, np.float32)))
+            bufs.append((h.upload(A), h.upload(x), h.zeroed(n)))
+        h.synchronize()
+        for i in range(2):
+            h.set_stream(streams[i].cuda_stream)
+            a, x, y = bufs[i]
+            for _ in range(20):
+                h.sgemv(1, m, n, 1.0, a, x, 0.0, y)
+        torch.cuda.synchronize()
+        h.set_stream(None)
+        for i in range(2):
+            got = h.download(bufs[i][2])
+            assert oracle.rel_err(got, refs[i]) <= oracle.tol_normwise(m, "f32")
+    finally:
+        h.close()
+
+
 def test_device_info(handle):
     info = handle.device_info()
     assert info["sm_count"] >= 100 and info["device"] == 0

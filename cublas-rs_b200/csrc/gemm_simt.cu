@@ -648,7 +648,7 @@ int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float
 // variant is forced, for comparisons).
 int run_dgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, double alpha, double beta,
               const double *A, const double *B, double *C) {
-    if (variant == 0 && b2b::dgemm_dmma_eligible(N, K, A, B, C))
+    if ((variant == 0 || variant >= 7) && b2b::dgemm_dmma_eligible(N, K, A, B, C))
         return b2b::launch_dgemm_dmma(h, M, N, K, alpha, beta, A, B, C);
     const bool vec = (K % 4 == 0) && (N % 4 == 0) && b2b::aligned16(A) && b2b::aligned16(B) && b2b::aligned16(C);
     if (!vec || variant == 1)

@@ -273,6 +273,10 @@ class Handle:
         _check(self._lib.b2b_memcpy_d2h(self._h, _hp(out), ctypes.c_void_p(dev.ptr), dev.nbytes))
         return out
 
+    def memset(self, buf: DeviceBuffer, value: int = 0) -> None:
+        """Set every byte of `buf` to `value`, ordered on the handle's stream."""
+        _check(self._lib.b2b_memset(self._h, ctypes.c_void_p(buf.ptr), int(value), buf.nbytes))
+
     def zeroed(self, length: int, dtype=np.float32) -> DeviceBuffer:
         return DeviceBuffer.zeroed(self, length, dtype)
 

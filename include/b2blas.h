@@ -20,6 +20,9 @@
  *     batched.rs:142-152).
  *   - Every function returns a b2b_status; b2b_last_error() gives the message
  *     of the last failure on the calling thread.
+ *   - Device-buffer calls can be captured in a CUDA graph once one eager call
+ *     of the same shapes has sized the handle's workspace; host-slice calls
+ *     and the value-returning reductions synchronise and cannot.
  */
 #ifndef B2BLAS_H
 #define B2BLAS_H

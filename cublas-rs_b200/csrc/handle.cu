@@ -169,6 +169,14 @@ int b2b_create(int device, b2b_handle **out) {
         if (v > 0) h->wait_limit_ns = static_cast<uint64_t>(v) * 1000000ull;
     }
     if (const char *cm = getenv("B2B_COPY_MODE")) h->copy_mode_forced = (cm[0] == '1') ? 1 : (cm[0] == '0' ? 0 : -1);
+    if (const char *v = getenv("B2B_HOST_PANELS")) {
+        const int p = atoi(v);
+        if (p >= 1 && p <= 64) h->host_panels = p;
+    }
+    if (const char *v = getenv("B2B_HOST_COL_PANELS")) {
+        const int p = atoi(v);
+        if (p >= 1 && p <= 16) h->host_col_panels = p;
+    }
     const char *single = getenv("B2B_HGEMM_SINGLE_CTA");
     h->force_single_cta = single && single[0] == '1';
     if (const char *v = getenv("B2B_SGEMM_VARIANT")) h->sgemm_variant = atoi(v);

@@ -27,6 +27,7 @@
 #include <chrono>
 #include <new>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "internal.h"
@@ -102,20 +103,41 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     T *dC = reinterpret_cast<T *>(static_cast<char *>(stage) + oc);
     const bool up_c = beta != S(0);
 
-    // Row panels: ~8 for large problems, multiples of 128 rows so the
-    // tensor-core tiles of a panel start on a tile boundary.
+    // Tiles of C: row panels of A (~8 for large problems, multiples of 128
+    // rows so the tensor-core tiles of a panel start on a tile boundary)
+    // times column panels of B (nb of them, multiples of 256 columns).  Each
+    // piece is contiguous on the device (2-D copies gather and scatter the
+    // host's row-major slices), so tile (i, j) is an ordinary GEMM of A_i and
+    // B_j.  Uploads interleave B_j with A_j so that the first tiles, and with
+    // them the device-to-host copies of C, start after a fraction of B has
+    // arrived instead of all of it.
     const size_t bytes = ea + eb + ec;
-    int panels = bytes >= (size_t(64) << 20) ? 8 : 1;
+    const bool large = bytes >= (size_t(64) << 20);
+    int panels = large ? h->host_panels : 1;
     size_t prow = round_up((m + panels - 1) / panels, 128);
     if (prow > m) prow = m;
     panels = static_cast<int>((m + prow - 1) / prow);
+    int nb = large ? h->host_col_panels : 1;
+    size_t pcol = round_up((n + nb - 1) / nb, 256);
+    if (pcol > n) pcol = n;
+    nb = static_cast<int>((n + pcol - 1) / pcol);
+    auto rows_of = [&](int i) { return (static_cast<size_t>(i) + 1) * prow <= m ? prow : m - i * prow; };
+    auto cols_of = [&](int j) { return (static_cast<size_t>(j) + 1) * pcol <= n ? pcol : n - j * pcol; };
+    // Device layout: A as is (row panels are contiguous), B panel j at
+    // dB + k * j * pcol (k x cols_of(j)), C tile (i, j) at
+    // dC + i * prow * n + rows_of(i) * j * pcol (rows_of(i) x cols_of(j)).
+    auto dB_of = [&](int j) { return dB + k * (static_cast<size_t>(j) * pcol); };
+    auto dC_of = [&](int i, int j) { return dC + static_cast<size_t>(i) * prow * n + rows_of(i) * (j * pcol); };
 
-    if ((rc = pipe_setup(h, 2 * panels + 2))) return rc;
-    cudaEvent_t *ev = h->pipe_events;
+    const int nev = panels + nb + panels * nb + 2;
+    if ((rc = pipe_setup(h, nev))) return rc;
+    cudaEvent_t *ev_a = h->pipe_events;                    // A_i (and C_i) uploaded
+    cudaEvent_t *ev_b = ev_a + panels;                     // B_j uploaded
+    cudaEvent_t *ev_c = ev_b + nb;                         // tile (i, j) computed
+    cudaEvent_t start_ev = ev_c[panels * nb], up_done = ev_c[panels * nb + 1];
     cudaStream_t up = h->copy_stream, down = h->down_stream;
     // Copy schedule (see b2b_handle::copy_mode_*): try each mode once on large
     // calls, then keep the faster.
-    const bool large = bytes >= (size_t(64) << 20);
     int mode = 0;
     if (h->copy_mode_forced >= 0)
         mode = h->copy_mode_forced;
@@ -128,39 +150,57 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     const auto t_start = std::chrono::steady_clock::now();
     cudaError_t e = cudaSuccess;
     cudaStream_t cs = h->stream;
+    const size_t es = sizeof(T);
     // The compute stream's earlier work (e.g. a previous call still using
     // the staging buffer) must finish before the copies overwrite it.
-    cudaEvent_t start_ev = ev[2 * panels];
-    cudaEvent_t up_done = ev[2 * panels + 1];
     e = cudaEventRecord(start_ev, cs);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(up, start_ev, 0);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(dB, B, eb, cudaMemcpyHostToDevice, up);
-    for (int i = 0; i < panels && e == cudaSuccess; ++i) {
-        const size_t r0 = static_cast<size_t>(i) * prow;
-        const size_t rows = (r0 + prow <= m) ? prow : m - r0;
-        e = cudaMemcpyAsync(dA + r0 * k, A + r0 * k, rows * k * sizeof(T), cudaMemcpyHostToDevice, up);
-        if (e == cudaSuccess && up_c)
-            e = cudaMemcpyAsync(dC + r0 * n, C + r0 * n, rows * n * sizeof(T), cudaMemcpyHostToDevice, up);
-        if (e == cudaSuccess) e = cudaEventRecord(ev[2 * i], up);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ev[2 * i], 0);
+    // Upload order: B_0 A_0 B_1 A_1 ... then the remaining A_i (or B_j).
+    int na = 0, nbu = 0;  // pieces uploaded so far
+    std::vector<std::pair<int, int>> order;  // tiles in the order they become computable
+    order.reserve(static_cast<size_t>(panels) * nb);
+    while ((na < panels || nbu < nb) && e == cudaSuccess) {
+        if (nbu < nb && (nbu <= na || na == panels)) {
+            const int j = nbu++;
+            const size_t cj = cols_of(j);
+            e = cudaMemcpy2DAsync(dB_of(j), cj * es, B + j * pcol, n * es, cj * es, k, cudaMemcpyHostToDevice, up);
+            if (e == cudaSuccess) e = cudaEventRecord(ev_b[j], up);
+            for (int i = 0; i < na; ++i) order.emplace_back(i, j);
+        } else {
+            const int i = na++;
+            const size_t ri = rows_of(i);
+            e = cudaMemcpyAsync(dA + static_cast<size_t>(i) * prow * k, A + static_cast<size_t>(i) * prow * k,
+                                ri * k * es, cudaMemcpyHostToDevice, up);
+            for (int j = 0; j < nb && e == cudaSuccess && up_c; ++j)
+                e = cudaMemcpy2DAsync(dC_of(i, j), cols_of(j) * es, C + static_cast<size_t>(i) * prow * n + j * pcol,
+                                      n * es, cols_of(j) * es, ri, cudaMemcpyHostToDevice, up);
+            if (e == cudaSuccess) e = cudaEventRecord(ev_a[i], up);
+            for (int j = 0; j < nbu; ++j) order.emplace_back(i, j);
+        }
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(up_done, up);
+    for (size_t t = 0; t < order.size() && e == cudaSuccess; ++t) {
+        const int i = order[t].first, j = order[t].second;
+        e = cudaStreamWaitEvent(cs, ev_a[i], 0);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ev_b[j], 0);
         if (e != cudaSuccess) break;
-        rc = launch(h, rows, n, k, alpha, dA + r0 * k, dB, beta, dC + r0 * n);
+        rc = launch(h, rows_of(i), cols_of(j), k, alpha, dA + static_cast<size_t>(i) * prow * k, dB_of(j), beta,
+                    dC_of(i, j));
         if (rc) {
             cudaStreamSynchronize(up);
             cudaStreamSynchronize(cs);
             return rc;
         }
-        e = cudaEventRecord(ev[2 * i + 1], cs);
+        e = cudaEventRecord(ev_c[i * nb + j], cs);
     }
     // Phased mode: the device-to-host copies wait for the last upload.
-    if (e == cudaSuccess) e = cudaEventRecord(up_done, up);
     if (e == cudaSuccess && mode == 0) e = cudaStreamWaitEvent(down, up_done, 0);
-    for (int i = 0; i < panels && e == cudaSuccess; ++i) {
-        const size_t r0 = static_cast<size_t>(i) * prow;
-        const size_t rows = (r0 + prow <= m) ? prow : m - r0;
-        e = cudaStreamWaitEvent(down, ev[2 * i + 1], 0);
+    for (size_t t = 0; t < order.size() && e == cudaSuccess; ++t) {
+        const int i = order[t].first, j = order[t].second;
+        e = cudaStreamWaitEvent(down, ev_c[i * nb + j], 0);
         if (e == cudaSuccess)
-            e = cudaMemcpyAsync(C + r0 * n, dC + r0 * n, rows * n * sizeof(T), cudaMemcpyDeviceToHost, down);
+            e = cudaMemcpy2DAsync(C + static_cast<size_t>(i) * prow * n + j * pcol, n * es, dC_of(i, j),
+                                  cols_of(j) * es, cols_of(j) * es, rows_of(i), cudaMemcpyDeviceToHost, down);
     }
     cudaError_t e2 = cudaStreamSynchronize(up);
     cudaError_t e3 = cudaStreamSynchronize(down);

@@ -46,6 +46,8 @@ struct b2b_handle {
     // path, so the first two large calls try one each and later calls use the
     // faster (B2B_COPY_MODE=0/1 forces one).
     int copy_mode_forced = -1;
+    int host_panels = 8;                // row panels of a large host-slice GEMM (B2B_HOST_PANELS)
+    int host_col_panels = 4;            // column panels of B in a large host-slice GEMM (B2B_HOST_COL_PANELS)
     double copy_mode_ms_per_gb[2] = {0.0, 0.0};
     // Upper bound on any single bounded device wait, in nanoseconds.
     uint64_t wait_limit_ns = 2000000000ull;

@@ -141,6 +141,54 @@ def test_simple_equals_device_flavour_bitwise(handle, oracle):
     assert np.array_equal(dev, host)
 
 
+@pytest.mark.parametrize("col_panels", ["1", "2", "3"])
+@pytest.mark.parametrize("prec", ["s", "d", "h"])
+def test_large_simple_tiled_pipeline(oracle, monkeypatch, col_panels, prec):
+    # Host slices above 64 MiB take the pipelined path: row panels of A times
+    # column panels of B, gathered and scattered with 2-D copies.  Ragged
+    # sizes leave short last panels in both directions; beta != 0 uploads C
+    # tiles too.  The result equals the device-buffer flavour bit for bit
+    # (same kernel per output element), and is checked against FP64 rows.
+    import b2blas
+
+    monkeypatch.setenv("B2B_HOST_COL_PANELS", col_panels)
+    m, n, k = 3000, 2600, 3000  # f32: 98 MB of operands
+    if prec == "d":
+        m, n, k = 2100, 1800, 2100
+    if prec == "h":
+        m, n, k = 4100, 4104, 4096
+    h = b2blas.Handle(0)
+    try:
+        if prec == "h":
+            A = oracle.normal_f16(m * k, 11, 1, 0.0, 0.1)
+            B = oracle.normal_f16(k * n, 11, 2, 0.0, 0.1)
+            C = oracle.normal_f16(m * n, 11, 3, 0.0, 0.1)
+        else:
+            f = oracle.uniform_f32 if prec == "s" else oracle.uniform_f64
+            A, B, C = f(m * k, 11, 1), f(k * n, 11, 2), f(m * n, 11, 3)
+        cfg = b2blas.GemmConfig(m, n, k, 1.25, -0.5)
+        host = C.copy()
+        getattr(h, f"{prec}gemm_simple")(cfg, A, B, host)
+        a, b, c = h.upload(A), h.upload(B), h.upload(C)
+        getattr(h, f"{prec}gemm")(cfg, a, b, c)
+        h.synchronize()
+        dev = h.download(c)
+        ref_fn = {"s": oracle.sgemm_f64, "d": oracle.dgemm_f64, "h": oracle.hgemm_f64}[prec]
+        rows = [0, 383, 384, m - 1]
+        for r in rows:
+            ref = ref_fn(m, n, k, 1.25, A, B, -0.5, C, row0=r, nrows=1)
+            got = np.ascontiguousarray(host.reshape(m, n)[r])
+            tol = 2e-2 if prec == "h" else oracle.tol_normwise(k, "f32" if prec == "s" else "f64")
+            assert oracle.rel_err(got, ref) <= tol, r
+        if prec != "h":
+            assert np.array_equal(dev, host)
+        else:  # tile shapes may pick another tcgen05 variant: within an f16 ulp
+            d = np.abs(dev.view(np.float16).astype(np.float64) - host.view(np.float16).astype(np.float64))
+            assert np.max(d) <= 2 * np.max(np.abs(host.view(np.float16).astype(np.float64))) * 2 ** -10
+    finally:
+        h.close()
+
+
 def test_sgemm_8192_full_size_sampled(handle, oracle):
     # The 8192^3 configuration (alpha 1.5, beta 0.5): sampled rows against the
     # FP64 oracle, plus a column check C[:, j] against A @ B[:, j].

@@ -251,20 +251,48 @@ class GemmWorkload(Workload):
         self.bound = {"hgemm": "tensor", "sgemm": "fma", "dgemm": "fp64"}[kind]
         if kind == "sgemm" and args.tf32x3:
             self.kernel, self.bound = "sgemm_3xtf32_kernel", "tf32x3"
-        self.gather = bool(args.gather) and world > 1
-        if self.gather:
+        # --gather: every rank ends each step with the full C.  "fused": the
+        # GEMM writes its panel into every rank's C itself (b2b_*gemm_gather
+        # through IPC-mapped peer buffers), then a 1-element all-reduce orders
+        # the next step behind all ranks' writes.  "nccl": GEMM into the
+        # panel, NCCL all-gather of the panels, re-layout kernel.
+        self.gather = ("nccl" if args.gather_nccl else "fused") if (args.gather or args.gather_nccl) and world > 1 \
+            else None
+        if self.gather == "nccl":
             self.panels = torch.empty(sum(self.widths) * m, device=dev, dtype=tdt)
             self.full = torch.empty(m, sum(self.widths), device=dev, dtype=tdt)
             self.launches_per_step = 2
+        elif self.gather == "fused":
+            if args.tf32x3:
+                raise SystemExit("--gather with --tf32x3 is not supported")
+            self.col_off = sum(self.widths[:rank])
+            self.peers = shard.PeerBuffers(h, m * self.global_n, bdt)
+            if beta:
+                host = np.zeros((m, self.global_n), bdt)
+                host[:, self.col_off:self.col_off + self.n] = self.C.cpu().numpy().view(bdt)
+                h.upload_into(self.peers.buf, host.ravel())
+            self.gfn = {"hgemm": h.hgemm_gather, "sgemm": h.sgemm_gather, "dgemm": h.dgemm_gather}[kind]
+            self.bar = torch.zeros(1, device=dev)
+            self.launches_per_step = 1
 
     def step(self):
+        if self.gather == "fused":
+            import torch.distributed as dist
+
+            self.gfn(self.cfg, self.a, self.b, self.global_n, self.col_off, self.peers.ptrs, self.rank)
+            dist.all_reduce(self.bar)
+            return
         self.fn(self.cfg, self.a, self.b, self.c)
-        if self.gather:
+        if self.gather == "nccl":
             import torch.distributed as dist
 
             dist.all_gather_into_tensor(self.panels, self.C.view(-1))
             esz = self.C.element_size()
             self.h.panels_to_rowmajor(esz, self.m, self.widths, self.panels.data_ptr(), self.full.data_ptr())
+
+    def close(self):
+        if self.gather == "fused":
+            self.peers.close()
 
     def units_per_step(self):
         return 2.0 * self.m * self.n * self.k
@@ -288,7 +316,7 @@ class GemmWorkload(Workload):
                          + (f", column-sharded over {self.world} GPUs ({self.n} columns per GPU), A replicated"
                             if self.world > 1 else ""),
              "m": self.m, "n": self.global_n, "k": self.k, "n_per_gpu": self.n, "alpha": self.alpha,
-             "beta": self.beta, "gather": self.gather, "parallelism": f"column-shard x{self.world}",
+             "beta": self.beta, "gather": self.gather or False, "parallelism": f"column-shard x{self.world}",
              "l2": "inputs larger than L2 (126 MB): no flush needed"}
         return d
 
@@ -958,7 +986,10 @@ def main():
                                            "mlp"], default="hgemm")
     ap.add_argument("--op", choices=["dot", "nrm2", "asum", "iamax"], default="dot", help="reduce: which reduction")
     ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
-    ap.add_argument("--gather", action="store_true", help="column-sharded GEMMs: all-gather C every step")
+    ap.add_argument("--gather", action="store_true",
+                    help="column-sharded GEMMs: every rank ends each step with the full C (GEMM with the gather fused)")
+    ap.add_argument("--gather-nccl", action="store_true",
+                    help="as --gather, but GEMM into the panel + NCCL all-gather + re-layout kernel")
     ap.add_argument("--tf32x3", action="store_true", help="sgemm/mlp: the opt-in 3xTF32 tensor-core kernel")
     ap.add_argument("--fused", action="store_true", help="mlp: bias (+ReLU) fused into the SGEMM epilogue")
     ap.add_argument("--e2e-steps", type=int, default=None, help="0 skips the end-to-end pass")
@@ -1059,7 +1090,7 @@ def main():
         torch.cuda.synchronize()
         per_launch_ms = e0.elapsed_time(e1) / args.steps
         achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
-    elif isinstance(w, GemvWorkload) or (isinstance(w, GemmWorkload) and w.gather):
+    elif isinstance(w, GemvWorkload) or (isinstance(w, GemmWorkload) and w.gather == "nccl"):
         achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
     else:
         achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
@@ -1069,6 +1100,17 @@ def main():
             "peak_source": psrc, "traffic": traffic,
             "algorithmic_units_per_launch": w.units_per_step(),
             "launch_ms": per_launch_ms}
+    if isinstance(w, GemmWorkload) and w.gather == "fused":
+        # Fused GEMM + all-gather: the step cannot beat the slower of its
+        # math (flops / peak) and its NVLink traffic (this rank's panel to
+        # each of the world - 1 peers, at the measured 770 GB/s per direction).
+        esz = {"hgemm": 2, "sgemm": 4, "dgemm": 8}[w.kind]
+        nvl_bytes = (world - 1) * w.m * w.n * esz
+        t_math = w.units_per_step() / (peak * 1e12) * 1e3 if punit == "TFLOP/s" else 0.0
+        t_link = nvl_bytes / 770e9 * 1e3
+        roof["fused_collective"] = {"nvlink_bytes_per_step": nvl_bytes, "link_gbs": 770.0,
+                                    "math_ms": t_math, "link_ms": t_link, "target_ms": max(t_math, t_link),
+                                    "frac_of_target": max(t_math, t_link) / per_launch_ms}
 
     # end to end through the host-slice API
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(3, min(args.steps, 10))
@@ -1095,6 +1137,8 @@ def main():
                 "config": w.config(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": w.launches_per_step * args.steps, "clocks": sampler.summary()}
         print(json.dumps(line), flush=True)
+    if hasattr(w, "close"):
+        w.close()
     h.set_stream(None)
     h.close()
     if dist is not None:

@@ -268,6 +268,13 @@ class Handle:
         _check(self._lib.b2b_memcpy_h2d(self._h, ctypes.c_void_p(buf.ptr), _hp(host), host.nbytes))
         return buf
 
+    def upload_into(self, dev: DeviceBuffer, host: np.ndarray) -> None:
+        """Copy a host array into an existing device buffer (its first bytes)."""
+        host = np.ascontiguousarray(host)
+        if host.nbytes > dev.nbytes:
+            raise CublasError(2, f"{host.nbytes} bytes do not fit a {dev.nbytes}-byte buffer")
+        _check(self._lib.b2b_memcpy_h2d(self._h, ctypes.c_void_p(dev.ptr), _hp(host), host.nbytes))
+
     def download(self, dev: DeviceBuffer) -> np.ndarray:
         out = np.empty(len(dev), dev.dtype)
         _check(self._lib.b2b_memcpy_d2h(self._h, _hp(out), ctypes.c_void_p(dev.ptr), dev.nbytes))
@@ -583,6 +590,44 @@ class Handle:
         """Queues a kernel whose wait can never complete; it gives up after
         limit_ns.  The following synchronize() raises CublasError(status=4)."""
         _check(self._lib.b2b_selftest_bounded_wait(self._h, int(limit_ns)))
+
+    # ---- multi-GPU: GEMM with the all-gather folded in
+    def _gather(self, fn, dtype, config, a, b, ldc, col_off, dst_ptrs, self_index):
+        m, n, k = config.m, config.n, config.k
+        if m and n and k:
+            self._need(a, m * k, "A", dtype)
+            self._need(b, k * n, "B", dtype)
+        arr = (ctypes.c_void_p * len(dst_ptrs))(*[int(p) for p in dst_ptrs])
+        _check(fn(self._h, m, n, k, config.alpha, ctypes.c_void_p(a.ptr), ctypes.c_void_p(b.ptr), config.beta,
+                  int(ldc), int(col_off), ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)), len(dst_ptrs),
+                  int(self_index)))
+
+    def hgemm_gather(self, config, a, b, ldc, col_off, dst_ptrs, self_index):
+        """This rank's column panel of C = alpha*A*B (+ beta*C) written into
+        every rank's full m x ldc C (dst_ptrs, b2b_hgemm_gather)."""
+        self._gather(self._lib.b2b_hgemm_gather, np.uint16, config, a, b, ldc, col_off, dst_ptrs, self_index)
+
+    def sgemm_gather(self, config, a, b, ldc, col_off, dst_ptrs, self_index):
+        self._gather(self._lib.b2b_sgemm_gather, np.float32, config, a, b, ldc, col_off, dst_ptrs, self_index)
+
+    def dgemm_gather(self, config, a, b, ldc, col_off, dst_ptrs, self_index):
+        self._gather(self._lib.b2b_dgemm_gather, np.float64, config, a, b, ldc, col_off, dst_ptrs, self_index)
+
+    def ipc_get_handle(self, buf: DeviceBuffer) -> bytes:
+        """64-byte CUDA IPC handle of a library allocation (its base pointer)."""
+        out = ctypes.create_string_buffer(64)
+        _check(self._lib.b2b_ipc_get_handle(self._h, ctypes.c_void_p(buf.ptr), out))
+        return out.raw
+
+    def ipc_open_handle(self, handle: bytes) -> int:
+        """Device pointer (in this process) to the allocation behind `handle`."""
+        p = ctypes.c_void_p()
+        _check(self._lib.b2b_ipc_open_handle(self._h, ctypes.create_string_buffer(bytes(handle), 64),
+                                             ctypes.byref(p)))
+        return p.value
+
+    def ipc_close_handle(self, ptr: int) -> None:
+        _check(self._lib.b2b_ipc_close_handle(self._h, ctypes.c_void_p(int(ptr))))
 
     # ---- multi-GPU helper
     def panels_to_rowmajor(self, elem_bytes: int, m: int, widths: Sequence[int], panels_ptr: int, c_ptr: int):

@@ -71,6 +71,12 @@ SIGNATURES = {
     "b2b_saxpy_simple": (_i, [_vp, _sz, _f, _vp, _sz, _vp, _sz]),
     "b2b_gpu_timer_start": (_i, [_vp, _vpp]),
     "b2b_gpu_timer_stop": (_i, [_vp, ctypes.POINTER(ctypes.c_double)]),
+    "b2b_hgemm_gather": (_i, [_vp, _sz, _sz, _sz, _f, _vp, _vp, _f, _sz, _sz, _vpp, _i, _i]),
+    "b2b_sgemm_gather": (_i, [_vp, _sz, _sz, _sz, _f, _vp, _vp, _f, _sz, _sz, _vpp, _i, _i]),
+    "b2b_dgemm_gather": (_i, [_vp, _sz, _sz, _sz, _d, _vp, _vp, _d, _sz, _sz, _vpp, _i, _i]),
+    "b2b_ipc_get_handle": (_i, [_vp, _vp, _vp]),
+    "b2b_ipc_open_handle": (_i, [_vp, _vp, _vpp]),
+    "b2b_ipc_close_handle": (_i, [_vp, _vp]),
     "b2b_panels_to_rowmajor": (_i, [_vp, _sz, _sz, _sz, _szp, _vp, _vp]),
     "b2b_selftest_bounded_wait": (_i, [_vp, ctypes.c_uint64]),
 }

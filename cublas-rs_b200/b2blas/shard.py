@@ -10,7 +10,9 @@ crates/cublas-rs/src/lib.rs:57-68):
   column panel B[:, c0:c1] (k x w) and C[:, c0:c1] (m x w), stored as its own
   contiguous row-major panel.  Only when the caller asks for the full C do
   the ranks all-gather their panels (panel-major), after which
-  b2b_panels_to_rowmajor lays the result out row-major.
+  b2b_panels_to_rowmajor lays the result out row-major -- or, fused,
+  b2b_*gemm_gather writes each rank's panel straight into every rank's
+  full C through the peer pointers PeerBuffers sets up.
 """
 from __future__ import annotations
 
@@ -59,3 +61,42 @@ def panels_to_rowmajor_host(panels: np.ndarray, m: int, widths: List[int]) -> np
         off += m * w
         c += w
     return out.ravel()
+
+
+class PeerBuffers:
+    """One library allocation per rank, mapped into every rank: after
+    construction (collective over `group`), `ptrs[r]` is rank r's buffer as a
+    device pointer valid in this process (CUDA IPC for the peers).  Used as
+    the destinations of b2b_*gemm_gather.  Call close() (collectively) before
+    the handle goes away."""
+
+    def __init__(self, handle, length: int, dtype, group=None):
+        import torch.distributed as dist
+
+        self.handle = handle
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.buf = handle.alloc(length, dtype)
+        mine = handle.ipc_get_handle(self.buf)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine, group=group)
+        self.ptrs = []
+        for r, hd in enumerate(handles):
+            self.ptrs.append(self.buf.ptr if r == self.rank else handle.ipc_open_handle(hd))
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if not self.ptrs:
+            return
+        # Nobody may still be writing into a peer's buffer when it is unmapped
+        # and freed.
+        self.handle.synchronize()
+        dist.barrier(group=self.group)
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self.handle.ipc_close_handle(p)
+        dist.barrier(group=self.group)
+        self.buf.free()
+        self.ptrs = []

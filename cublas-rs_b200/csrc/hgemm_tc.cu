@@ -71,6 +71,12 @@ struct HgemmArgs {
     int *status;
     uint64_t wait_ns;
     int group_m;  // pair kernels' raster group (pair-tile rows); 0 = the kernel's default
+    // Fused all-gather (pair kernels, beta == 0): when ndst > 0 the epilogue
+    // writes element (r, c) of this rank's panel to dst[d][r * ldc + col_off + c]
+    // for every d -- each rank's full row-major C, peers' mapped through CUDA IPC.
+    int ndst;
+    int64_t ldc, col_off;
+    uint16_t *dst[8];
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
@@ -641,6 +647,33 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                         // 128-byte swizzle: 16-byte chunk j of row r sits at chunk j ^ (r % 8)
                         *reinterpret_cast<uint4 *>(rowp + ((j ^ (lane & 7)) << 4)) = o;
                     }
+                    if (args.ndst > 0) {
+                        // Fused all-gather: 16-byte chunk q = lane + 32t of the box
+                        // (row q / 8, columns 8 (q % 8) ..) is read back from its
+                        // swizzled slot and stored to every rank's C; each store
+                        // instruction covers four whole 128-byte row segments.
+                        __syncwarp();
+                        uint4 v[8];
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            const int qq = lane + 32 * t, rr = qq >> 3, jj = qq & 7;
+                            v[t] = *reinterpret_cast<const uint4 *>(buf + rr * 128 + ((jj ^ (rr & 7)) << 4));
+                        }
+#pragma unroll 1
+                        for (int d = 0; d < args.ndst; ++d) {
+                            uint16_t *base = args.dst[d] + args.col_off;
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) {
+                                const int qq = lane + 32 * t;
+                                const int grow = row0 + (qq >> 3), gcol = col0 + (qq & 7) * 8;
+                                if (grow < args.M && gcol < args.N)
+                                    *reinterpret_cast<uint4 *>(base + static_cast<int64_t>(grow) * args.ldc + gcol) =
+                                        v[t];
+                            }
+                        }
+                        ++nstore;
+                        continue;
+                    }
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
@@ -856,6 +889,33 @@ int launch_pairs(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, 
 }
 }  // namespace
 
+// HGEMM whose epilogue scatters the panel into every rank's C (see
+// HgemmArgs::ndst).  Sets *done when the CTA-pair kernel took the call
+// (beta == 0, pair-kernel shapes, 16-byte aligned destinations); otherwise
+// the caller falls back to compute-then-copy.
+int launch_hgemm_gather_fused(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A,
+                              const uint16_t *B, uint16_t *const *dst, int ndst, int self, size_t ldc, size_t col_off,
+                              bool *done) {
+    *done = false;
+    uint16_t *cself = dst[self] + col_off;
+    if (!hgemm_tc_eligible(m, n, k, A, B, cself) || m <= static_cast<size_t>(hg::BM) || h->force_single_cta ||
+        h->hgemm_variant == 1 || ldc % 8 != 0 || col_off % 8 != 0 || ndst > 8)
+        return B2B_OK;
+    for (int d = 0; d < ndst; ++d)
+        if (!aligned16(dst[d])) return B2B_OK;
+    CUtensorMap tmA, tmB;
+    int rc = encode_2d_f16(&tmA, A, m, k, hg::BK, hg::BM);
+    if (rc) return rc;
+    rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
+    if (rc) return rc;
+    HgemmArgs args{cself, (int)m, (int)n, (int)k, alpha, 0.0f, h->d_status, h->wait_limit_ns, h->hgemm_group_m,
+                   ndst, static_cast<int64_t>(ldc), static_cast<int64_t>(col_off), {}};
+    for (int d = 0; d < ndst; ++d) args.dst[d] = dst[d];
+    rc = launch_pairs(h, tmA, tmB, args, m, n);
+    if (rc == B2B_OK) *done = true;
+    return rc;
+}
+
 int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A, const uint16_t *B,
                  float beta, uint16_t *C) {
     if (hgemm_tc_eligible(m, n, k, A, B, C)) {
@@ -864,7 +924,7 @@ int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const
         if (rc) return rc;
         rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
         if (rc) return rc;
-        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns, h->hgemm_group_m};
+        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns, h->hgemm_group_m, 0, 0, 0, {}};
         // More than one 128-row tile: CTA pairs with 256 x 256 tiles.
         if (m > static_cast<size_t>(hg::BM) && !h->force_single_cta && h->hgemm_variant != 1)
             return launch_pairs(h, tmA, tmB, args, m, n);

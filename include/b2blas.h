@@ -310,6 +310,37 @@ B2B_API int b2b_gpu_timer_stop(b2b_gpu_timer *timer, double *ms);
 B2B_API int b2b_panels_to_rowmajor(b2b_handle *h, size_t elem_bytes, size_t m, size_t g, const size_t *widths,
                                    const void *panels, void *C);
 
+/* ------------------------------------- multi-GPU: GEMM + all-gather, fused
+ * No reference counterpart.  Rank g of a column-sharded GEMM computes its
+ * m x n panel alpha*A*B_g + beta*C_g and writes it into every rank's full
+ * row-major C (m x ldc, columns [col_off, col_off + n)): dst[d] is rank d's
+ * C as a device pointer valid in this process (its own allocation, or a
+ * peer's opened with b2b_ipc_open_handle); dst[self_index] is this rank's and
+ * also holds the input panel when beta != 0.  1 <= ndst <= 8.  HGEMM with
+ * beta == 0 on CTA-pair shapes stores each output box to every destination
+ * from the kernel's epilogue (the transfer overlaps the MMAs, no separate
+ * all-gather or re-layout); the other cases compute the panel, then copy it
+ * to each destination.  Asynchronous on the handle's stream; C is complete
+ * on every rank only after all ranks' calls have finished, so order readers
+ * behind a barrier or collective, as for an all-gather. */
+B2B_API int b2b_hgemm_gather(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A,
+                             const uint16_t *B, float beta, size_t ldc, size_t col_off, uint16_t *const *dst,
+                             int ndst, int self_index);
+B2B_API int b2b_sgemm_gather(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
+                             const float *B, float beta, size_t ldc, size_t col_off, float *const *dst, int ndst,
+                             int self_index);
+B2B_API int b2b_dgemm_gather(b2b_handle *h, size_t m, size_t n, size_t k, double alpha, const double *A,
+                             const double *B, double beta, size_t ldc, size_t col_off, double *const *dst, int ndst,
+                             int self_index);
+
+/* CUDA IPC for the destinations above: a 64-byte handle for a b2b_malloc
+ * allocation (pass its base pointer), opened in another process on the same
+ * node to get a device pointer to it; close it before the owner frees it. */
+#define B2B_IPC_HANDLE_BYTES 64
+B2B_API int b2b_ipc_get_handle(b2b_handle *h, void *dptr, void *handle);
+B2B_API int b2b_ipc_open_handle(b2b_handle *h, const void *handle, void **dptr);
+B2B_API int b2b_ipc_close_handle(b2b_handle *h, void *dptr);
+
 /* ------------------------------------------------------------ self-test
  * No reference counterpart.  Launches one CTA whose mbarrier wait can never
  * complete; the bounded wait gives up after limit_ns (0 < limit <= 5 s),

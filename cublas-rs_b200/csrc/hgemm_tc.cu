@@ -879,8 +879,11 @@ int launch_pairs(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, 
     const int wide_pairs = max_pairs_of<2>(h, probe);
     if (wide_pairs < 0) return B2B_ERR_CUDA;
     const size_t wide_tiles = ((m + 255) / 256) * ((n + 511) / 512);
-    const bool wide = h->hgemm_variant == 3 || (h->hgemm_variant != 2 && n >= 512 && args.K >= 2048 &&
-                                                 wide_tiles >= static_cast<size_t>(wide_pairs));
+    // A fused all-gather makes the epilogue long (its stores cross NVLink to
+    // every rank): keep the double-buffered accumulators of the 256 x 256
+    // tiles so the next tile's MMAs run meanwhile.
+    const bool wide = h->hgemm_variant == 3 || (h->hgemm_variant != 2 && args.ndst <= 1 && n >= 512 &&
+                                                 args.K >= 2048 && wide_tiles >= static_cast<size_t>(wide_pairs));
     if (wide) return launch_pair_kernel<2>(h, tmA, tmB, tmC, args, m, n, wide_pairs);
     probe.dynamicSmemBytes = hg2::Cfg<1>::SMEM_BYTES;
     const int pairs = max_pairs_of<1>(h, probe);

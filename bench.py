@@ -256,8 +256,9 @@ class GemmWorkload(Workload):
         # through IPC-mapped peer buffers), then a 1-element all-reduce orders
         # the next step behind all ranks' writes.  "nccl": GEMM into the
         # panel, NCCL all-gather of the panels, re-layout kernel.
-        self.gather = ("nccl" if args.gather_nccl else "fused") if (args.gather or args.gather_nccl) and world > 1 \
-            else None
+        self.gather = ("nccl" if args.gather_nccl else "fused") \
+            if (args.gather or args.gather_nccl or args.gather_p2p) and world > 1 else None
+        self.mc = 0
         if self.gather == "nccl":
             self.panels = torch.empty(sum(self.widths) * m, device=dev, dtype=tdt)
             self.full = torch.empty(m, sum(self.widths), device=dev, dtype=tdt)
@@ -266,6 +267,27 @@ class GemmWorkload(Workload):
             if args.tf32x3:
                 raise SystemExit("--gather with --tf32x3 is not supported")
             self.col_off = sum(self.widths[:rank])
+            if kind == "hgemm" and not beta and not args.gather_p2p:
+                # NVLink multicast (torch symmetric memory binds one buffer per
+                # rank): each output store crosses NVLink once.
+                import torch.distributed as dist
+
+                try:
+                    import torch.distributed._symmetric_memory as symm
+
+                    self.symm_buf = symm.empty(m * self.global_n, dtype=tdt, device=dev)
+                    self.symm_hd = symm.rendezvous(self.symm_buf, dist.group.WORLD.group_name)
+                    mc = int(getattr(self.symm_hd, "multicast_ptr", 0) or 0)
+                except Exception:  # noqa: BLE001 -- no symmetric memory: peer stores
+                    mc = 0
+                ok = torch.tensor([1 if mc else 0], device=dev)
+                dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+                self.mc = mc if ok.item() else 0
+            if self.mc:
+                self.gather = "fused-multicast"
+                self.bar = torch.zeros(1, device=dev)
+                self.launches_per_step = 1
+                return
             self.peers = shard.PeerBuffers(h, m * self.global_n, bdt)
             if beta:
                 host = np.zeros((m, self.global_n), bdt)
@@ -276,6 +298,13 @@ class GemmWorkload(Workload):
             self.launches_per_step = 1
 
     def step(self):
+        if self.gather == "fused-multicast":
+            import torch.distributed as dist
+
+            self.h.hgemm_gather_multicast(self.cfg, self.a, self.b, self.global_n, self.col_off, self.mc,
+                                          self.symm_buf.data_ptr())
+            dist.all_reduce(self.bar)
+            return
         if self.gather == "fused":
             import torch.distributed as dist
 
@@ -293,6 +322,14 @@ class GemmWorkload(Workload):
     def close(self):
         if self.gather == "fused":
             self.peers.close()
+        if self.mc:
+            # every rank's stores into the multicast object have landed
+            # before any rank releases its buffer
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.synchronize()
+            dist.barrier()
 
     def units_per_step(self):
         return 2.0 * self.m * self.n * self.k
@@ -988,6 +1025,8 @@ def main():
     ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
     ap.add_argument("--gather", action="store_true",
                     help="column-sharded GEMMs: every rank ends each step with the full C (GEMM with the gather fused)")
+    ap.add_argument("--gather-p2p", action="store_true",
+                    help="as --gather, with peer stores even where an NVLink multicast address is available")
     ap.add_argument("--gather-nccl", action="store_true",
                     help="as --gather, but GEMM into the panel + NCCL all-gather + re-layout kernel")
     ap.add_argument("--tf32x3", action="store_true", help="sgemm/mlp: the opt-in 3xTF32 tensor-core kernel")
@@ -1100,12 +1139,14 @@ def main():
             "peak_source": psrc, "traffic": traffic,
             "algorithmic_units_per_launch": w.units_per_step(),
             "launch_ms": per_launch_ms}
-    if isinstance(w, GemmWorkload) and w.gather == "fused":
+    if isinstance(w, GemmWorkload) and w.gather in ("fused", "fused-multicast"):
         # Fused GEMM + all-gather: the step cannot beat the slower of its
         # math (flops / peak) and its NVLink traffic (this rank's panel to
-        # each of the world - 1 peers, at the measured 770 GB/s per direction).
+        # each of the world - 1 peers, or once through the switch with
+        # multicast, at the measured 770 GB/s per direction).
         esz = {"hgemm": 2, "sgemm": 4, "dgemm": 8}[w.kind]
-        nvl_bytes = (world - 1) * w.m * w.n * esz
+        # multicast: the panel leaves the GPU once and NVSwitch replicates it
+        nvl_bytes = (1 if w.gather == "fused-multicast" else world - 1) * w.m * w.n * esz
         t_math = w.units_per_step() / (peak * 1e12) * 1e3 if punit == "TFLOP/s" else 0.0
         t_link = nvl_bytes / 770e9 * 1e3
         roof["fused_collective"] = {"nvlink_bytes_per_step": nvl_bytes, "link_gbs": 770.0,

@@ -607,6 +607,19 @@ class Handle:
         every rank's full m x ldc C (dst_ptrs, b2b_hgemm_gather)."""
         self._gather(self._lib.b2b_hgemm_gather, np.uint16, config, a, b, ldc, col_off, dst_ptrs, self_index)
 
+    def hgemm_gather_multicast(self, config, a, b, ldc, col_off, mc_ptr, own_ptr):
+        """b2b_hgemm_gather_multicast: the gather through an NVLink multicast
+        address bound to every rank's C (beta must be 0)."""
+        m, n, k = config.m, config.n, config.k
+        if config.beta != 0.0:
+            raise CublasError(3, "hgemm_gather_multicast needs beta == 0")
+        if m and n and k:
+            self._need(a, m * k, "A", np.uint16)
+            self._need(b, k * n, "B", np.uint16)
+        _check(self._lib.b2b_hgemm_gather_multicast(self._h, m, n, k, config.alpha, ctypes.c_void_p(a.ptr),
+                                                    ctypes.c_void_p(b.ptr), int(ldc), int(col_off),
+                                                    ctypes.c_void_p(int(mc_ptr)), ctypes.c_void_p(int(own_ptr))))
+
     def sgemm_gather(self, config, a, b, ldc, col_off, dst_ptrs, self_index):
         self._gather(self._lib.b2b_sgemm_gather, np.float32, config, a, b, ldc, col_off, dst_ptrs, self_index)
 

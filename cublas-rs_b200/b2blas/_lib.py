@@ -74,6 +74,7 @@ SIGNATURES = {
     "b2b_hgemm_gather": (_i, [_vp, _sz, _sz, _sz, _f, _vp, _vp, _f, _sz, _sz, _vpp, _i, _i]),
     "b2b_sgemm_gather": (_i, [_vp, _sz, _sz, _sz, _f, _vp, _vp, _f, _sz, _sz, _vpp, _i, _i]),
     "b2b_dgemm_gather": (_i, [_vp, _sz, _sz, _sz, _d, _vp, _vp, _d, _sz, _sz, _vpp, _i, _i]),
+    "b2b_hgemm_gather_multicast": (_i, [_vp, _sz, _sz, _sz, _f, _vp, _vp, _sz, _sz, _vp, _vp]),
     "b2b_ipc_get_handle": (_i, [_vp, _vp, _vp]),
     "b2b_ipc_open_handle": (_i, [_vp, _vp, _vpp]),
     "b2b_ipc_close_handle": (_i, [_vp, _vp]),

@@ -28,6 +28,9 @@ namespace b2b {
 int launch_hgemm_gather_fused(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A,
                               const uint16_t *B, uint16_t *const *dst, int ndst, int self, size_t ldc, size_t col_off,
                               bool *done);
+int launch_hgemm_gather_multicast(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A,
+                                  const uint16_t *B, uint16_t *mc, uint16_t *own, size_t ldc, size_t col_off,
+                                  bool *done);
 }
 
 namespace {
@@ -85,6 +88,25 @@ int b2b_hgemm_gather(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, c
         if (done) return B2B_OK;
     }
     return gather_generic(h, m, n, k, alpha, A, B, beta, ldc, col_off, dst, ndst, self_index, launch_hgemm);
+}
+
+int b2b_hgemm_gather_multicast(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A,
+                               const uint16_t *B, size_t ldc, size_t col_off, uint16_t *mc, uint16_t *own) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_hgemm_gather_multicast: NULL handle");
+    if (!mc || !own) return fail(B2B_ERR_INVALID_ARG, "b2b_hgemm_gather_multicast: NULL buffer");
+    if (col_off > ldc || n > ldc - col_off)
+        return fail(B2B_ERR_DIMENSION, "b2b_hgemm_gather_multicast: panel [col_off, col_off + n) exceeds ldc");
+    if (m == 0 || n == 0 || k == 0) return B2B_OK;
+    if (!A || !B) return fail(B2B_ERR_INVALID_ARG, "b2b_hgemm_gather_multicast: NULL operand");
+    if (ldc > SIZE_MAX / m / 2) return fail(B2B_ERR_INVALID_ARG, "b2b_hgemm_gather_multicast: sizes overflow");
+    DeviceGuard g(h);
+    bool done = false;
+    if (int rc = launch_hgemm_gather_multicast(h, m, n, k, alpha, A, B, mc, own, ldc, col_off, &done)) return rc;
+    if (!done)
+        return fail(B2B_ERR_NOT_SUPPORTED,
+                    "b2b_hgemm_gather_multicast: needs the CTA-pair kernel (m > 128, k and n multiples of 8, "
+                    "16-byte aligned operands, ldc and col_off multiples of 8)");
+    return B2B_OK;
 }
 
 int b2b_sgemm_gather(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,

@@ -77,6 +77,9 @@ struct HgemmArgs {
     int ndst;
     int64_t ldc, col_off;
     uint16_t *dst[8];
+    // With mc set, the gather goes through that NVLink multicast address
+    // instead (one store reaches every rank's C); dst/ndst are then unused.
+    uint16_t *mc;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
@@ -647,7 +650,7 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                         // 128-byte swizzle: 16-byte chunk j of row r sits at chunk j ^ (r % 8)
                         *reinterpret_cast<uint4 *>(rowp + ((j ^ (lane & 7)) << 4)) = o;
                     }
-                    if (args.ndst > 0) {
+                    if (args.ndst > 0 || args.mc != nullptr) {
                         // Fused all-gather: 16-byte chunk q = lane + 32t of the box
                         // (row q / 8, columns 8 (q % 8) ..) is read back from its
                         // swizzled slot and stored to every rank's C; each store
@@ -658,6 +661,16 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                         for (int t = 0; t < 8; ++t) {
                             const int qq = lane + 32 * t, rr = qq >> 3, jj = qq & 7;
                             v[t] = *reinterpret_cast<const uint4 *>(buf + rr * 128 + ((jj ^ (rr & 7)) << 4));
+                        }
+                        if (args.mc != nullptr) {
+                            uint16_t *base = args.mc + args.col_off;
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) {
+                                const int qq = lane + 32 * t;
+                                const int grow = row0 + (qq >> 3), gcol = col0 + (qq & 7) * 8;
+                                if (grow < args.M && gcol < args.N)
+                                    multimem_st_v4(base + static_cast<int64_t>(grow) * args.ldc + gcol, v[t]);
+                            }
                         }
 #pragma unroll 1
                         for (int d = 0; d < args.ndst; ++d) {
@@ -912,8 +925,30 @@ int launch_hgemm_gather_fused(b2b_handle *h, size_t m, size_t n, size_t k, float
     rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
     if (rc) return rc;
     HgemmArgs args{cself, (int)m, (int)n, (int)k, alpha, 0.0f, h->d_status, h->wait_limit_ns, h->hgemm_group_m,
-                   ndst, static_cast<int64_t>(ldc), static_cast<int64_t>(col_off), {}};
+                   ndst, static_cast<int64_t>(ldc), static_cast<int64_t>(col_off), {}, nullptr};
     for (int d = 0; d < ndst; ++d) args.dst[d] = dst[d];
+    rc = launch_pairs(h, tmA, tmB, args, m, n);
+    if (rc == B2B_OK) *done = true;
+    return rc;
+}
+
+// Same as launch_hgemm_gather_fused, the destinations being every member
+// of an NVLink multicast object mapped at `mc` (own buffer at `own`).
+int launch_hgemm_gather_multicast(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A,
+                                  const uint16_t *B, uint16_t *mc, uint16_t *own, size_t ldc, size_t col_off,
+                                  bool *done) {
+    *done = false;
+    uint16_t *cself = own + col_off;
+    if (!hgemm_tc_eligible(m, n, k, A, B, cself) || m <= static_cast<size_t>(hg::BM) || h->force_single_cta ||
+        h->hgemm_variant == 1 || ldc % 8 != 0 || col_off % 8 != 0 || !aligned16(mc))
+        return B2B_OK;
+    CUtensorMap tmA, tmB;
+    int rc = encode_2d_f16(&tmA, A, m, k, hg::BK, hg::BM);
+    if (rc) return rc;
+    rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
+    if (rc) return rc;
+    HgemmArgs args{cself, (int)m, (int)n, (int)k, alpha, 0.0f, h->d_status, h->wait_limit_ns, h->hgemm_group_m,
+                   0, static_cast<int64_t>(ldc), static_cast<int64_t>(col_off), {}, mc};
     rc = launch_pairs(h, tmA, tmB, args, m, n);
     if (rc == B2B_OK) *done = true;
     return rc;
@@ -927,7 +962,7 @@ int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const
         if (rc) return rc;
         rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
         if (rc) return rc;
-        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns, h->hgemm_group_m, 0, 0, 0, {}};
+        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns, h->hgemm_group_m, 0, 0, 0, {}, nullptr};
         // More than one 128-row tile: CTA pairs with 256 x 256 tiles.
         if (m > static_cast<size_t>(hg::BM) && !h->force_single_cta && h->hgemm_variant != 1)
             return launch_pairs(h, tmA, tmB, args, m, n);

@@ -153,6 +153,16 @@ __device__ __forceinline__ void bulk_wait_group() {
     asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// 16-byte store through an NVLink multicast address (a multicast object
+// bound to one buffer per GPU): NVSwitch writes it to every member's buffer
+// at the same offset.  Weak store; the caller orders readers with a
+// cross-GPU barrier after the kernel.
+__device__ __forceinline__ void multimem_st_v4(void *addr, const uint4 &v) {
+    asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(__uint_as_float(v.x)),
+                 "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)), "f"(__uint_as_float(v.w))
+                 : "memory");
+}
+
 // --------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),

@@ -333,6 +333,16 @@ B2B_API int b2b_dgemm_gather(b2b_handle *h, size_t m, size_t n, size_t k, double
                              const double *B, double beta, size_t ldc, size_t col_off, double *const *dst, int ndst,
                              int self_index);
 
+/* The HGEMM gather through an NVLink multicast object instead of per-peer
+ * pointers: mc is the multicast address bound to every rank's full C (same
+ * size and layout on each), own this rank's buffer.  Each output store goes
+ * once through NVSwitch, which writes it to every member, so a panel crosses
+ * NVLink once instead of once per peer.  beta is 0; shapes the CTA-pair
+ * kernel cannot take return B2B_ERR_NOT_SUPPORTED (use b2b_hgemm_gather).
+ * Same ordering rule as above. */
+B2B_API int b2b_hgemm_gather_multicast(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A,
+                                       const uint16_t *B, size_t ldc, size_t col_off, uint16_t *mc, uint16_t *own);
+
 /* CUDA IPC for the destinations above: a 64-byte handle for a b2b_malloc
  * allocation (pass its base pointer), opened in another process on the same
  * node to get a device pointer to it; close it before the owner frees it. */

@@ -77,7 +77,49 @@ def main() -> int:
         peers.close()
         a.free()
         b.free()
+    # The HGEMM gather through an NVLink multicast object (torch symmetric
+    # memory binds one buffer per rank and maps the multicast address).
+    try:
+        import torch.distributed._symmetric_memory as symm
+        have_symm = True
+    except Exception:  # noqa: BLE001 -- older torch: nothing to test
+        have_symm = False
+    if have_symm:
+        for m, n_total, k, alpha in ((640, 1000, 384, 1.0), (1024, 3072, 512, 0.5)):
+            widths = shard.column_panels(n_total, world, 8)
+            c0, w = sum(widths[:rank]), widths[rank]
+            A = oracle.normal_f16(m * k, 7, 1, 0.0, 0.1)
+            B = oracle.normal_f16(k * n_total, 7, 2, 0.0, 0.1)
+            ref = oracle.hgemm_f64(m, n_total, k, alpha, A, B)
+            t = symm.empty(m * n_total, dtype=torch.float16, device=f"cuda:{local}")
+            hd = symm.rendezvous(t, dist.group.WORLD.group_name)
+            mc = int(getattr(hd, "multicast_ptr", 0) or 0)
+            ok_mc = torch.tensor([1 if mc else 0], device="cuda")
+            dist.all_reduce(ok_mc, op=dist.ReduceOp.MIN)
+            if ok_mc.item():
+                t.view(torch.int16).fill_(0x7E00)  # NaN: every element must be written
+                torch.cuda.synchronize()
+                dist.barrier()
+                a, b = h.upload(A), h.upload(shard.panel_of(B, k, n_total, c0, c0 + w))
+                try:
+                    h.hgemm_gather_multicast(b2blas.GemmConfig(m, w, k, alpha, 0.0), a, b, n_total, c0, mc,
+                                             t.data_ptr())
+                except b2blas.CublasError as e:
+                    failures.append(f"multicast {m}x{n_total}x{k}: {e}")
+                h.synchronize()
+                dist.barrier()
+                got = t.cpu().numpy().view(np.uint16)
+                err = oracle.rel_err(got, ref)
+                if not err <= 2e-2:
+                    failures.append(f"multicast {m}x{n_total}x{k}: rel err {err:.3e}")
+                a.free()
+                b.free()
+            else:
+                print(f"rank {rank}: no multicast address, multicast case skipped", flush=True)
+            dist.barrier()
+            del t, hd
     h.close()
+    dist.barrier()
     dist.destroy_process_group()
     for f in failures:
         print(f"rank {rank}: FAIL {f}", flush=True)

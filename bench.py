@@ -257,7 +257,7 @@ class GemmWorkload(Workload):
         # the next step behind all ranks' writes.  "nccl": GEMM into the
         # panel, NCCL all-gather of the panels, re-layout kernel.
         self.gather = ("nccl" if args.gather_nccl else "fused") \
-            if (args.gather or args.gather_nccl or args.gather_p2p) and world > 1 else None
+            if (args.gather or args.gather_nccl or args.gather_multicast) and world > 1 else None
         self.mc = 0
         if self.gather == "nccl":
             self.panels = torch.empty(sum(self.widths) * m, device=dev, dtype=tdt)
@@ -267,9 +267,12 @@ class GemmWorkload(Workload):
             if args.tf32x3:
                 raise SystemExit("--gather with --tf32x3 is not supported")
             self.col_off = sum(self.widths[:rank])
-            if kind == "hgemm" and not beta and not args.gather_p2p:
+            if kind == "hgemm" and not beta and args.gather_multicast:
                 # NVLink multicast (torch symmetric memory binds one buffer per
-                # rank): each output store crosses NVLink once.
+                # rank): each output store leaves the GPU once.  Every GPU
+                # still receives the (world - 1) other panels, so the step's
+                # link bound is the same as with peer stores (measured on 8
+                # B200s: 1.67 ms multicast, 1.58 ms peer stores).
                 import torch.distributed as dist
 
                 try:
@@ -1025,8 +1028,8 @@ def main():
     ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
     ap.add_argument("--gather", action="store_true",
                     help="column-sharded GEMMs: every rank ends each step with the full C (GEMM with the gather fused)")
-    ap.add_argument("--gather-p2p", action="store_true",
-                    help="as --gather, with peer stores even where an NVLink multicast address is available")
+    ap.add_argument("--gather-multicast", action="store_true",
+                    help="as --gather, HGEMM stores through an NVLink multicast object (torch symmetric memory)")
     ap.add_argument("--gather-nccl", action="store_true",
                     help="as --gather, but GEMM into the panel + NCCL all-gather + re-layout kernel")
     ap.add_argument("--tf32x3", action="store_true", help="sgemm/mlp: the opt-in 3xTF32 tensor-core kernel")
@@ -1141,12 +1144,12 @@ def main():
             "launch_ms": per_launch_ms}
     if isinstance(w, GemmWorkload) and w.gather in ("fused", "fused-multicast"):
         # Fused GEMM + all-gather: the step cannot beat the slower of its
-        # math (flops / peak) and its NVLink traffic (this rank's panel to
-        # each of the world - 1 peers, or once through the switch with
-        # multicast, at the measured 770 GB/s per direction).
+        # math (flops / peak) and its NVLink traffic (the world - 1 panels
+        # every GPU receives, at the measured 770 GB/s per direction).
         esz = {"hgemm": 2, "sgemm": 4, "dgemm": 8}[w.kind]
-        # multicast: the panel leaves the GPU once and NVSwitch replicates it
-        nvl_bytes = (1 if w.gather == "fused-multicast" else world - 1) * w.m * w.n * esz
+        # Each GPU receives the (world - 1) other panels whatever the sender
+        # does (peer stores, or one multicast store replicated by NVSwitch).
+        nvl_bytes = (world - 1) * w.m * w.n * esz
         t_math = w.units_per_step() / (peak * 1e12) * 1e3 if punit == "TFLOP/s" else 0.0
         t_link = nvl_bytes / 770e9 * 1e3
         roof["fused_collective"] = {"nvlink_bytes_per_step": nvl_bytes, "link_gbs": 770.0,

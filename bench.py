@@ -247,7 +247,7 @@ class GemmWorkload(Workload):
         self.simple = {"hgemm": h.hgemm_simple, "dgemm": h.dgemm_simple,
                        "sgemm": h.sgemm_3xtf32_simple if args.tf32x3 else h.sgemm_simple}[kind]
         self.kernel = {"hgemm": "hgemm_tc2_kernel" if m > 128 else "hgemm_tc_kernel",
-                       "sgemm": "gemm_async_kernel<float>", "dgemm": "dgemm_dmma_kernel"}[kind]
+                       "sgemm": "sgemm_tma_kernel", "dgemm": "dgemm_dmma_kernel<32,3>"}[kind]
         self.bound = {"hgemm": "tensor", "sgemm": "fma", "dgemm": "fp64"}[kind]
         if kind == "sgemm" and args.tf32x3:
             self.kernel, self.bound = "sgemm_3xtf32_kernel", "tf32x3"
@@ -695,7 +695,7 @@ class MlpWorkload(Workload):
         self.fused = bool(args.fused)
         self.algo = b2blas.Algo.Tf32x3 if args.tf32x3 else b2blas.Algo.Default
         self.launches_per_step = 4 if self.fused else 8
-        self.kernel = "gemm_async_kernel<float>"
+        self.kernel = "sgemm_tma_kernel"
         self.bound = "fma"
 
     def forward(self, xb):

@@ -117,7 +117,10 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     size_t prow = round_up((m + panels - 1) / panels, 128);
     if (prow > m) prow = m;
     panels = static_cast<int>((m + prow - 1) / prow);
-    int nb = large ? h->host_col_panels : 1;
+    // Column panels pay off where the copies bound the call (f16: 4); a
+    // compute-bound FP32/FP64 call keeps whole row panels, whose GEMMs fill
+    // the GPU (a 1024 x 2048 tile is 64 CTAs of 128 x 256).
+    int nb = large ? (h->host_col_panels > 0 ? h->host_col_panels : (sizeof(T) == 2 ? 4 : 1)) : 1;
     size_t pcol = round_up((n + nb - 1) / nb, 256);
     if (pcol > n) pcol = n;
     nb = static_cast<int>((n + pcol - 1) / pcol);

@@ -47,7 +47,7 @@ struct b2b_handle {
     // faster (B2B_COPY_MODE=0/1 forces one).
     int copy_mode_forced = -1;
     int host_panels = 8;                // row panels of a large host-slice GEMM (B2B_HOST_PANELS)
-    int host_col_panels = 4;            // column panels of B in a large host-slice GEMM (B2B_HOST_COL_PANELS)
+    int host_col_panels = 0;            // column panels of B in a large host-slice GEMM; 0 = auto (B2B_HOST_COL_PANELS)
     double copy_mode_ms_per_gb[2] = {0.0, 0.0};
     // Upper bound on any single bounded device wait, in nanoseconds.
     uint64_t wait_limit_ns = 2000000000ull;
@@ -113,6 +113,9 @@ int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const
 int launch_sgemm_3xtf32(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
                         const float *B, float beta, float *C);
 bool dgemm_dmma_eligible(int64_t N, int64_t K, const void *A, const void *B, const void *C);
+bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C);
+int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
+                     const float *B, float *C, const float *bias, int relu);
 int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
                       const double *B, double *C);
 int launch_sgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A, const float *x,

@@ -1,0 +1,294 @@
+// sgemm_tma.cu -- FP32 SGEMM on the CUDA cores with TMA-fed operands.
+//
+// The operation of cublas-rs's sgemm_* kernels (crates/cublas-l3/src/
+// sgemm.rs:31-360): C <- alpha*A*B + beta*C (+ bias[j], ReLU for the fused
+// epilogue), row-major, FP32 FFMA arithmetic, each output summed over k in
+// order by one thread -- the same per-element arithmetic as the cp.async
+// kernel in gemm_simt.cu, so results are bit-identical to it.
+//
+// The FFMA loop wants A as As[k][m] (four consecutive rows of one k in a
+// 16-byte shared load).  Instead of transposing A tile by tile with 4-byte
+// copies in the FFMA warps, A is transposed once into workspace (At, K x M;
+// an HBM-bound pass of 8 bytes per element of A, ~0.4% of an 8192^3 GEMM),
+// after which both operands are plain row-major tiles that TMA copies into
+// shared memory exactly as the FFMA warps read them:
+//   * CTA tile 128 x 256, k-block 32, 4-stage ring of 48 KiB (At box 128 x 32,
+//     B box 256 x 32, no swizzle: fragment loads are conflict-free as laid out).
+//   * 8 FFMA warps (2 x 4, 16 x 8 outputs per thread, the gemm_simt.cu
+//     fragment layout) wait on a stage's "full" mbarrier (TMA completion)
+//     and release it on its "empty" mbarrier -- no CTA-wide barrier and no
+//     copy instructions in the loop.  Lane 0 of warp 0 issues the TMA loads:
+//     all stages up front, then, after each k-block, a refill of the stage
+//     every warp released one k-block earlier (S - 1 blocks ahead), so it
+//     rarely waits for a slower warp.  (A separate producer warp would make
+//     the CTA 288 threads, which registers are allocated for as 384, too few
+//     registers per thread for the 128 accumulators.)
+//   * Every wait is bounded; a wait that gives up records a status code,
+//     raises the abort flag, and warp 0 drains its in-flight loads before the
+//     CTA exits.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "internal.h"
+#include "sm100.cuh"
+
+namespace {
+
+constexpr int kTM = 16, kTN = 8, kWM = 2, kWN = 4;
+constexpr int kBM = kWM * (kTM / 4) * 16;  // 128
+constexpr int kBN = kWN * (kTN / 4) * 32;  // 256
+constexpr int kBK = 32;
+constexpr int kStages = 4;
+constexpr int kComputeWarps = kWM * kWN;
+constexpr int kThreads = kComputeWarps * 32;
+constexpr int kAStageF = kBK * kBM;                // floats per stage
+constexpr int kBStageF = kBK * kBN;
+constexpr uint32_t kStageBytes = (kAStageF + kBStageF) * 4;  // 48 KiB
+constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+constexpr int kGroupM = 8;  // raster group (M tiles sweeping the N tiles together)
+
+struct SArgs {
+    float *C;
+    int64_t M, N, K;
+    float alpha, beta;
+    const float *bias;
+    int relu;
+    int *status;
+    uint64_t wait_ns;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    sgemm_tma_kernel(const __grid_constant__ CUtensorMap tmAt, const __grid_constant__ CUtensorMap tmB, SArgs args) {
+    using namespace sm100;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    float *As = reinterpret_cast<float *>(smem);
+    float *Bs = As + kStages * kAStageF;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + kStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * kStages);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t tiles_m = (args.M + kBM - 1) / kBM, tiles_n = (args.N + kBN - 1) / kBN;
+    // grouped raster
+    const int64_t t = blockIdx.x;
+    const int64_t span = kGroupM * tiles_n;
+    const int64_t g = t / span;
+    const int64_t first = g * kGroupM;
+    const int64_t gm = tiles_m - first < kGroupM ? tiles_m - first : kGroupM;
+    const int64_t r = t - g * span;
+    const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * kBN;
+    const int64_t ktiles = (args.K + kBK - 1) / kBK;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kComputeWarps);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmAt);
+        prefetch_tensormap(&tmB);
+    }
+    __syncthreads();
+
+    const bool loader = tid == 0;
+    int64_t issued = 0;  // k-blocks whose loads warp 0's lane 0 has issued
+    auto issue = [&](int64_t kt) {
+        const int s = static_cast<int>(kt % kStages);
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        tma_load_2d(As + s * kAStageF, &tmAt, &full[s], static_cast<int32_t>(m0), static_cast<int32_t>(kt * kBK));
+        tma_load_2d(Bs + s * kBStageF, &tmB, &full[s], static_cast<int32_t>(n0), static_cast<int32_t>(kt * kBK));
+        ++issued;
+    };
+    if (loader)
+        for (int64_t kt = 0; kt < kStages && kt < ktiles; ++kt) issue(kt);
+
+    const int wm = warp / kWN, wn = warp % kWN;
+    const int ty = lane >> 3, tx = lane & 7;
+    const int row_base = wm * (kTM / 4) * 16 + ty * 4;
+    const int col_base = wn * (kTN / 4) * 32 + tx * 4;
+
+    float acc[kTM][kTN];
+#pragma unroll
+    for (int i = 0; i < kTM; ++i)
+#pragma unroll
+        for (int j = 0; j < kTN; ++j) acc[i][j] = 0.0f;
+
+    auto load_frags = [&](const float *as, const float *bs, int kk, float (&af)[kTM], float (&bf)[kTN]) {
+#pragma unroll
+        for (int q = 0; q < kTM / 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4 *>(as + kk * kBM + row_base + q * 16);
+            af[q * 4 + 0] = v.x;
+            af[q * 4 + 1] = v.y;
+            af[q * 4 + 2] = v.z;
+            af[q * 4 + 3] = v.w;
+        }
+#pragma unroll
+        for (int q = 0; q < kTN / 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4 *>(bs + kk * kBN + col_base + q * 32);
+            bf[q * 4 + 0] = v.x;
+            bf[q * 4 + 1] = v.y;
+            bf[q * 4 + 2] = v.z;
+            bf[q * 4 + 3] = v.w;
+        }
+    };
+
+    bool ok = true;
+    for (int64_t kt = 0; kt < ktiles; ++kt) {
+        const int s = static_cast<int>(kt % kStages);
+        const uint32_t ph = static_cast<uint32_t>((kt / kStages) & 1);
+        const bool w = mbar_wait(&full[s], ph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x32, args.wait_ns);
+        if (!__all_sync(0xffffffffu, w)) {
+            ok = false;
+            break;
+        }
+        const float *as = As + s * kAStageF;
+        const float *bs = Bs + s * kBStageF;
+        float af[2][kTM], bf[2][kTN];
+        load_frags(as, bs, 0, af[0], bf[0]);
+#pragma unroll
+        for (int kk = 0; kk < kBK; ++kk) {
+            if (kk + 1 < kBK) load_frags(as, bs, kk + 1, af[(kk + 1) & 1], bf[(kk + 1) & 1]);
+#pragma unroll
+            for (int i = 0; i < kTM; ++i)
+#pragma unroll
+                for (int j = 0; j < kTN; ++j) acc[i][j] = fmaf(af[kk & 1][i], bf[kk & 1][j], acc[i][j]);
+        }
+        // every lane's reads of this stage are done: release it
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        // Refill the stage released one k-block ago with the block S ahead of it.
+        if (loader && kt >= 1) {
+            const int64_t done = kt - 1, next = done + kStages;
+            if (next < ktiles) {
+                const int ds = static_cast<int>(done % kStages);
+                const uint32_t dph = static_cast<uint32_t>((done / kStages) & 1);
+                if (!mbar_wait(&empty[ds], dph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x31, args.wait_ns)) {
+                    ok = false;
+                } else {
+                    issue(next);
+                }
+            }
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+        }
+    }
+    if (!ok) {
+        if (loader && issued) {
+            // Loads in flight complete on their full barriers: wait for them
+            // (bounded) before the CTA's shared memory goes away.
+            const int64_t first_pending = issued > kStages ? issued - kStages : 0;
+            for (int64_t kt = first_pending; kt < issued; ++kt)
+                mbar_wait_drain(&full[kt % kStages], static_cast<uint32_t>((kt / kStages) & 1), 1000000000ull);
+        }
+        return;
+    }
+
+    const bool read_c = args.beta != 0.0f;
+#pragma unroll
+    for (int gi = 0; gi < kTM / 4; ++gi) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t row = m0 + row_base + gi * 16 + i;
+            if (row >= args.M) continue;
+            float *crow = args.C + row * args.N;
+#pragma unroll
+            for (int gj = 0; gj < kTN / 4; ++gj) {
+                const int64_t col = n0 + col_base + gj * 32;
+                if (col >= args.N) continue;  // N % 4 == 0: the 4-vector is all in or all out
+                float o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[e] = args.alpha * acc[gi * 4 + i][gj * 4 + e];
+                if (read_c) {
+                    const float4 old = *reinterpret_cast<const float4 *>(crow + col);
+                    o[0] = fmaf(args.beta, old.x, o[0]);
+                    o[1] = fmaf(args.beta, old.y, o[1]);
+                    o[2] = fmaf(args.beta, old.z, o[2]);
+                    o[3] = fmaf(args.beta, old.w, o[3]);
+                }
+                if (args.bias || args.relu) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (args.bias) o[e] += args.bias[col + e];
+                        if (args.relu) o[e] = o[e] > 0.0f ? o[e] : 0.0f;
+                    }
+                }
+                *reinterpret_cast<float4 *>(crow + col) = make_float4(o[0], o[1], o[2], o[3]);
+            }
+        }
+    }
+}
+
+// At[k][m] = A[m][k]: 32 x 32 tiles through shared memory (padded row).
+__global__ void __launch_bounds__(256) transpose_f32_kernel(const float *__restrict__ A, float *__restrict__ At,
+                                                            int64_t M, int64_t K) {
+    __shared__ float tile[32][33];
+    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 32, k0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+#pragma unroll
+    for (int j = ty; j < 32; j += 8) {
+        const int64_t m = m0 + j, k = k0 + tx;
+        if (m < M && k < K) tile[j][tx] = A[m * K + k];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = ty; j < 32; j += 8) {
+        const int64_t k = k0 + j, m = m0 + tx;
+        if (k < K && m < M) At[k * M + m] = tile[tx][j];
+    }
+}
+
+}  // namespace
+
+namespace b2b {
+
+bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C) {
+    // N >= 1024 keeps the transpose below ~3.5% of the GEMM's time.
+    return M % 4 == 0 && N % 4 == 0 && aligned16(A) && aligned16(B) && aligned16(C) && M >= kBM && N >= 1024 &&
+           K >= kBK && (K + kBK - 1) / kBK < (int64_t(1) << 30) && M < (int64_t(1) << 31) &&
+           N < (int64_t(1) << 31) && K < (int64_t(1) << 31) && K <= 65535LL * 32;
+}
+
+int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
+                     const float *B, float *C, const float *bias, int relu) {
+    void *ws = nullptr;
+    if (int rc = workspace(h, static_cast<size_t>(M) * static_cast<size_t>(K) * 4, &ws)) return rc;
+    float *At = static_cast<float *>(ws);
+    const dim3 tgrid(static_cast<unsigned>((M + 31) / 32), static_cast<unsigned>((K + 31) / 32));
+    transpose_f32_kernel<<<tgrid, 256, 0, h->stream>>>(A, At, M, K);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "sgemm transpose launch");
+    CUtensorMap tmAt, tmB;
+    int rc = encode_tma_2d(&tmAt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, At, static_cast<uint64_t>(K),
+                           static_cast<uint64_t>(M), kBM, kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = encode_tma_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, B, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                       kBN, kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    {
+        static std::mutex mu;
+        static bool attr_set[64] = {};
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set[h->device & 63]) {
+            e = cudaFuncSetAttribute(sgemm_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+            if (e != cudaSuccess) return fail_cuda(e, "sgemm smem attribute");
+            attr_set[h->device & 63] = true;
+        }
+    }
+    const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    if (tiles > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
+    SArgs args{C, M, N, K, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns};
+    sgemm_tma_kernel<<<static_cast<unsigned>(tiles), kThreads, kSmem, h->stream>>>(tmAt, tmB, args);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm TMA launch");
+}
+
+}  // namespace b2b

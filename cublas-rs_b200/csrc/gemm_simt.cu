@@ -440,6 +440,21 @@ struct AsyncCfg {
 };
 
 template <typename T>
+struct PairOf;
+template <>
+struct PairOf<float> {
+    using type = float2;
+};
+template <>
+struct PairOf<double> {
+    using type = double2;
+};
+__device__ __forceinline__ float2 pair_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ double2 pair_fma(double2 a, double2 b, double2 c) {
+    return make_double2(fma(a.x, b.x, c.x), fma(a.y, b.y, c.y));
+}
+
+template <typename T>
 __device__ __forceinline__ void cp_async_elem(uint32_t dst, const T *src, bool ok) {
     if constexpr (sizeof(T) == 4)
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(ok ? 4 : 0) : "memory");
@@ -512,11 +527,17 @@ __global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
         }
     };
 
-    T acc[TM][TN];
+    // Outputs as row pairs: acc2[p][j] = (acc[2p][j], acc[2p+1][j]).  For
+    // FP32 one packed FFMA2 (__ffma2_rn, sm_100) updates a pair, halving the
+    // issue slots of the FMA loop; each lane is the same single-rounding fma,
+    // so the result is that of the scalar loop, bit for bit.
+    using P2 = typename PairOf<T>::type;
+    P2 acc2[TM / 2][TN];
 #pragma unroll
-    for (int i = 0; i < TM; ++i)
+    for (int i = 0; i < TM / 2; ++i)
 #pragma unroll
-        for (int j = 0; j < TN; ++j) acc[i][j] = T(0);
+        for (int j = 0; j < TN; ++j) acc2[i][j] = P2{T(0), T(0)};
+    auto acc_at = [&](int i, int j) -> T & { return (i & 1) ? acc2[i >> 1][j].y : acc2[i >> 1][j].x; };
 
 #pragma unroll
     for (int s = 0; s < STAGES - 1; ++s) {
@@ -557,10 +578,13 @@ __global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
 #pragma unroll
         for (int kk = 0; kk < BK; ++kk) {
             if (kk + 1 < BK) load_frags(as, bs, kk + 1, af[(kk + 1) & 1], bf[(kk + 1) & 1]);
+            const T *a = af[kk & 1], *b = bf[kk & 1];
 #pragma unroll
-            for (int i = 0; i < TM; ++i)
+            for (int j = 0; j < TN; ++j) {
+                const P2 bb{b[j], b[j]};
 #pragma unroll
-                for (int j = 0; j < TN; ++j) acc[i][j] = fma(af[kk & 1][i], bf[kk & 1][j], acc[i][j]);
+                for (int p = 0; p < TM / 2; ++p) acc2[p][j] = pair_fma(P2{a[2 * p], a[2 * p + 1]}, bb, acc2[p][j]);
+            }
         }
     }
     cp_async_wait<0>();
@@ -579,7 +603,7 @@ __global__ void __launch_bounds__(WARPS_M *WARPS_N * 32, MINB)
                 if (c >= N) continue;  // N % 4 == 0: the 4-vector is all in or all out
                 T out[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) out[e] = alpha * acc[gi * 4 + i][gj * 4 + e];
+                for (int e = 0; e < 4; ++e) out[e] = alpha * acc_at(gi * 4 + i, gj * 4 + e);
                 if (read_c) {
                     T old[4];
                     Vec4<T>::load(crow + c, old);
@@ -628,10 +652,12 @@ int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float
               int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch,
               EpiArgs<float> epi = EpiArgs<float>{nullptr, 0}) {
     // Single large GEMMs: the TMA-fed kernel (sgemm_tma.cu; same per-element
-    // arithmetic, 5-6% faster at 4096^3-8192^3).  Variant 11 forces the
-    // cp.async kernel below.
-    if ((variant == 0 || variant == 20) && batch == 1 && b2b::sgemm_tma_eligible(M, N, K, A, B, C))
-        return b2b::launch_sgemm_tma(h, M, N, K, alpha, beta, A, B, C, epi.bias, epi.relu);
+    // arithmetic, 10% faster at 8192^3), packed FFMA2 on row pairs by default;
+    // variants 20/21/22 force its scalar / row-pair / column-pair forms and
+    // variant 11 the cp.async kernel below.
+    if ((variant == 0 || (variant >= 20 && variant <= 22)) && batch == 1 && b2b::sgemm_tma_eligible(M, N, K, A, B, C))
+        return b2b::launch_sgemm_tma(h, M, N, K, alpha, beta, A, B, C, epi.bias, epi.relu,
+                                     variant == 0 ? 1 : variant - 20);
     if (!vec_ok(K, N, sA, sB, sC, A, B, C) || variant == 1)
         return run_simt<float, 8, 8, 4, 2, 8, 2>(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi);
     switch (variant) {

@@ -115,7 +115,7 @@ int launch_sgemm_3xtf32(b2b_handle *h, size_t m, size_t n, size_t k, float alpha
 bool dgemm_dmma_eligible(int64_t N, int64_t K, const void *A, const void *B, const void *C);
 bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C);
 int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
-                     const float *B, float *C, const float *bias, int relu);
+                     const float *B, float *C, const float *bias, int relu, int pack);
 int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
                       const double *B, double *C);
 int launch_sgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A, const float *x,

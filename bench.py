@@ -23,6 +23,13 @@ hgemv (16384^2, N, or T with --trans), reduce (sdot by default, --op
 nrm2|asum|iamax; 2^28-element f32 vectors), mlp (4 layers
 1024-4096-4096-4096-1024, batch 4096, sgemm + saxpy bias).
 
+On one GPU the line also carries `reference_kernels`: the reference's own GPU
+kernels for the same operation (naive / tiled / vectorized / double_buf
+GEMMs, hgemm_half, the strided-batched and GEMV kernels, the 32-thread
+reductions, the mlp example's sgemm_tiled + saxpy), restated in CUDA C
+because the reference's Rust / cuda-oxide build cannot run here, timed on the
+same resident buffers (--no-ref-kernels skips them).
+
 --impl reference times the CPU restatement of the reference's algorithm
 (the oracle's host triple loop) on this machine's cores, rank 0 only, with a
 bounded sample of the same workload per step.
@@ -164,6 +171,12 @@ class ClockSampler:
 # Which page-locked allocator the end-to-end pass uses: the library's
 # (b2b_host_alloc = cudaHostAlloc) or torch's pin_memory.
 E2E_HOST = {"handle": None}
+
+
+def _cur_stream():
+    import torch
+
+    return torch.cuda.current_stream().cuda_stream
 
 
 def _pinned_numpy(t):
@@ -322,6 +335,22 @@ class GemmWorkload(Workload):
             esz = self.C.element_size()
             self.h.panels_to_rowmajor(esz, self.m, self.widths, self.panels.data_ptr(), self.full.data_ptr())
 
+    def ref_kernels(self):
+        """The reference's kernels for this GEMM (restated in CUDA C), writing
+        a scratch copy of C: [(name, launch)]."""
+        if self.gather is not None:
+            return []
+        from baseline import refkernels as R
+
+        self._ref_c = self.C.clone()
+        m, n, k, al, be = self.m, self.n, self.k, self.alpha, self.beta
+        pa, pb, pc, st = self.A.data_ptr(), self.B.data_ptr(), self._ref_c.data_ptr(), _cur_stream()
+        if self.kind == "hgemm":
+            return [("hgemm_half", lambda: R.hgemm_half(m, n, k, al, pa, pb, be, pc, st))]
+        fn = R.sgemm if self.kind == "sgemm" else R.dgemm
+        return [(f"{self.kind}_{name}", (lambda v=v: fn(v, m, n, k, al, pa, pb, be, pc, st)))
+                for v, name in R.GEMM_VARIANTS.items()]
+
     def close(self):
         if self.gather == "fused":
             self.peers.close()
@@ -450,6 +479,15 @@ class BatchedWorkload(Workload):
         mk = self.m * self.m
         self.h.strided_batched_sgemm_simple(self.cfg, self.batch, self.hA, mk, self.hB, mk, self.hC, mk)
 
+    def ref_kernels(self):
+        from baseline import refkernels as R
+
+        self._ref_c = self.C.clone()
+        m, mk, nb = self.m, self.m * self.m, self.batch
+        pa, pb, pc, st = self.A.data_ptr(), self.B.data_ptr(), self._ref_c.data_ptr(), _cur_stream()
+        return [("strided_batched_sgemm", lambda: R.sgemm_strided_batched(m, m, m, 1.0, pa, mk, pb, mk, 0.0, pc, mk,
+                                                                          nb, st))]
+
     def config(self):
         return {"workload": f"strided-batched sgemm {self.total_batch} x {self.m}^3"
                             + (f", {self.batch} batches per GPU" if self.world > 1 else ""),
@@ -539,6 +577,19 @@ class GemvWorkload(Workload):
     def e2e_step(self):
         fn = {"s": self.h.sgemv_simple, "d": self.h.dgemv_simple, "h": self.h.hgemv}[self.prec]
         fn(self.trans, self.m, self.n, 1.0, self.hA, self.hx, 0.0, self.hy)
+
+    def ref_kernels(self):
+        from baseline import refkernels as R
+
+        self._ref_y = self.y.clone()
+        t, m, n = self.trans, self.m, self.n
+        pa, px, py, st = self.A.data_ptr(), self.x.data_ptr(), self._ref_y.data_ptr(), _cur_stream()
+        if self.prec == "s":
+            return [(f"sgemv_{name}", (lambda v=v: R.sgemv(v, t, m, n, 1.0, pa, px, 0.0, py, st)))
+                    for v, name in ((0, "naive"), (1, "tiled"))]
+        if self.prec == "d":
+            return [("dgemv", lambda: R.dgemv(t, m, n, 1.0, pa, px, 0.0, py, st))]
+        return [("hgemv", lambda: R.hgemv(t, m, n, 1.0, pa, px, 0.0, py, st))]
 
     def config(self):
         gib = self.m * self.n * self.esize / 2 ** 30
@@ -635,6 +686,16 @@ class ReduceWorkload(Workload):
         else:
             getattr(h, {"nrm2": "snrm2_simple", "asum": "sasum_simple", "iamax": "isamax_simple"}[self.op])(
                 self.n, self.hx)
+
+    def ref_kernels(self):
+        import torch
+
+        from baseline import refkernels as R
+
+        self._ref_out = torch.zeros(1, device=self.x.device, dtype=torch.float32)
+        n, px, st = self.n, self.x.data_ptr(), _cur_stream()
+        py, po, op = (self.y.data_ptr() if self.y is not None else 0), self._ref_out.data_ptr(), self.op
+        return [("s" + op if op != "iamax" else "isamax", lambda: R.sreduce(op, n, px, py, po, st))]
 
     def config(self):
         return {"workload": f"s{self.op} n={self.n}" + (f", one replica per GPU" if self.world > 1 else ""),
@@ -734,6 +795,22 @@ class MlpWorkload(Workload):
         self.forward(self.xb)
         self._hY.copy_(self.Z[-1], non_blocking=True)
         torch.cuda.current_stream().synchronize()
+
+    def ref_kernels(self):
+        """The example's forward on the reference's kernels: sgemm_tiled + saxpy
+        of the pre-broadcast bias per layer, into scratch activations."""
+        from baseline import refkernels as R
+
+        self._ref_z = [z.clone() for z in self.Z]
+        st, b, d = _cur_stream(), self.batch, self.dims
+        ptrs = [self.X.data_ptr()] + [z.data_ptr() for z in self._ref_z]
+
+        def forward():
+            for i in range(4):
+                R.sgemm(1, b, d[i + 1], d[i], 1.0, ptrs[i], self.W[i].data_ptr(), 0.0, ptrs[i + 1], st)
+                R.saxpy(b * d[i + 1], 1.0, self.bias[i].data_ptr(), ptrs[i + 1], st)
+
+        return [("sgemm_tiled + saxpy (mlp forward)", forward)]
 
     def config(self):
         how = ("fused sgemm+bias+ReLU epilogue" if self.fused else "sgemm + saxpy bias") + \
@@ -1016,6 +1093,43 @@ def run_e2e(w, h, stream, steps, world, dist, barrier, host_alloc="b2b"):
 
 # ------------------------------------------------------------------ main
 
+def time_ref_kernels(w, stream, budget_ms=2500.0, max_launches=10):
+    """Times the reference's kernels (restated in CUDA C, baseline/) on this
+    workload's resident buffers: one untimed launch, then as many launches as
+    fit in about budget_ms (at least one), CUDA events on `stream`."""
+    import torch
+
+    try:
+        launchers = w.ref_kernels() if hasattr(w, "ref_kernels") else []
+    except (OSError, RuntimeError, ImportError) as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    if not launchers:
+        return None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    results = []
+    for name, fn in launchers:
+        fn()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        first = e0.elapsed_time(e1)
+        reps = max(1, min(max_launches, int(budget_ms / max(first, 1e-3))))
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        results.append({"kernel": name, "value": w.scale(w.units_per_step() / (ms / 1e3)), "ms_per_launch": ms,
+                        "launches": reps})
+    best = max(results, key=lambda r: r["value"])
+    return {"impl": "the reference's GPU kernels restated in CUDA C (baseline/refkernels.cu), "
+                    "same resident device buffers, same B200", "unit": w.unit, "results": results,
+            "best_kernel": best["kernel"], "best_value": best["value"]}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1041,6 +1155,8 @@ def main():
     ap.add_argument("--n", type=int, default=None)
     ap.add_argument("--k", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-kernels", action="store_true",
+                    help="skip timing the reference's GPU kernels (restated in CUDA C) beside the library")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -1162,6 +1278,10 @@ def main():
     if e2e_steps > 0:
         e2e = run_e2e(w, h, stream, e2e_steps, world, dist, barrier, args.e2e_host)
 
+    refk = None
+    if rank == 0 and world == 1 and not args.no_ref_kernels:
+        refk = time_ref_kernels(w, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle
@@ -1178,7 +1298,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
                 "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype,
                 "data": "synthetic (seeded torch generators; normal(0,0.1)->f16 for HGEMM, uniform[-1,1) else)",
-                "config": w.config(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "config": w.config(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "reference_kernels": refk,
                 "gpu_launches": w.launches_per_step * args.steps, "clocks": sampler.summary()}
         print(json.dumps(line), flush=True)
     if hasattr(w, "close"):

@@ -173,6 +173,18 @@ class ClockSampler:
 E2E_HOST = {"handle": None}
 
 
+def sgemm_kernels_per_call(m, n, k, tf32x3=False):
+    """Kernels one single SGEMM call launches: 2 on the TMA-fed FFMA path (the
+    transpose of A, then the GEMM), else 1.  Mirrors the library's dispatch
+    (run_sgemm in gemm_simt.cu, sgemm_tma_eligible in sgemm_tma.cu) for
+    16-byte aligned operands."""
+    variant = int(os.environ.get("B2B_SGEMM_VARIANT", "0") or 0)
+    if tf32x3 or variant not in (0, 20, 21, 22):
+        return 1
+    ok = m % 4 == 0 and n % 4 == 0 and m >= 128 and n >= 1024 and 32 <= k <= 65535 * 32
+    return 2 if ok else 1
+
+
 def _cur_stream():
     import torch
 
@@ -272,10 +284,12 @@ class GemmWorkload(Workload):
         self.gather = ("nccl" if args.gather_nccl else "fused") \
             if (args.gather or args.gather_nccl or args.gather_multicast) and world > 1 else None
         self.mc = 0
+        gemm_kernels = sgemm_kernels_per_call(m, self.n, k, args.tf32x3) if kind == "sgemm" else 1
+        self.launches_per_step = gemm_kernels
         if self.gather == "nccl":
             self.panels = torch.empty(sum(self.widths) * m, device=dev, dtype=tdt)
             self.full = torch.empty(m, sum(self.widths), device=dev, dtype=tdt)
-            self.launches_per_step = 2
+            self.launches_per_step = gemm_kernels + 1  # + the re-layout kernel
         elif self.gather == "fused":
             if args.tf32x3:
                 raise SystemExit("--gather with --tf32x3 is not supported")
@@ -311,7 +325,8 @@ class GemmWorkload(Workload):
                 h.upload_into(self.peers.buf, host.ravel())
             self.gfn = {"hgemm": h.hgemm_gather, "sgemm": h.sgemm_gather, "dgemm": h.dgemm_gather}[kind]
             self.bar = torch.zeros(1, device=dev)
-            self.launches_per_step = 1
+            # the GEMM's kernels (peer copies of the panel run on copy engines)
+            self.launches_per_step = gemm_kernels
 
     def step(self):
         if self.gather == "fused-multicast":
@@ -755,7 +770,9 @@ class MlpWorkload(Workload):
         self.bvec = [wrap(t) for t in self.bias_vec]
         self.fused = bool(args.fused)
         self.algo = b2blas.Algo.Tf32x3 if args.tf32x3 else b2blas.Algo.Default
-        self.launches_per_step = 4 if self.fused else 8
+        per_gemm = [sgemm_kernels_per_call(self.batch, self.dims[i + 1], self.dims[i], bool(args.tf32x3))
+                    for i in range(4)]
+        self.launches_per_step = sum(per_gemm) + (0 if self.fused else 4)  # + a saxpy per layer
         self.kernel = "sgemm_tma_kernel"
         self.bound = "fma"
 

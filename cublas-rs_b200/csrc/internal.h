@@ -95,6 +95,11 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 int encode_tma_2d(CUtensorMap *map, CUtensorMapDataType dtype, size_t elem_bytes, const void *base, uint64_t rows,
                   uint64_t cols, uint32_t box_cols, uint32_t box_rows,
                   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
+// 3-D map: dim0 innermost (contiguous), dim1 with pitch stride1_bytes, dim2
+// with pitch stride2_bytes; box box0 x box1 x 1.
+int encode_tma_3d(CUtensorMap *map, CUtensorMapDataType dtype, size_t elem_bytes, const void *base, uint64_t dim0,
+                  uint64_t dim1, uint64_t dim2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                  uint32_t box1, CUtensorMapSwizzle swizzle);
 
 // ---- kernel launchers (each returns a b2b_status) --------------------------
 int launch_sgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A, const float *B,
@@ -116,6 +121,13 @@ bool dgemm_dmma_eligible(int64_t N, int64_t K, const void *A, const void *B, con
 bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C);
 int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
                      const float *B, float *C, const float *bias, int relu, int pack);
+// The TMA-fed FFMA kernel reading row-major A directly (no transpose pass),
+// batched over 3-D tensor maps; batch 1 for a single GEMM.
+bool sgemm_tma_rowa_eligible(int64_t M, int64_t N, int64_t K, int64_t sA, int64_t sB, int64_t sC, int64_t batch,
+                             const void *A, const void *B, const void *C);
+int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
+                          int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch,
+                          const float *bias, int relu);
 int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
                       const double *B, double *C);
 int launch_sgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A, const float *x,

@@ -128,6 +128,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *m, uin
         : "memory");
 }
 
+// 3-D tiled load (x innermost), completing on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *m, uint64_t *bar, int32_t x, int32_t y,
+                                            int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 // 2-D tiled store of one box from shared memory to global memory, tracked
 // by this thread's bulk async-group.  Elements outside the tensor are not
 // written.  The writes to `src` must be made visible to the async proxy

@@ -45,4 +45,19 @@ int encode_tma_2d(CUtensorMap *map, CUtensorMapDataType dtype, size_t elem_bytes
     return B2B_OK;
 }
 
+int encode_tma_3d(CUtensorMap *map, CUtensorMapDataType dtype, size_t elem_bytes, const void *base, uint64_t dim0,
+                  uint64_t dim1, uint64_t dim2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                  uint32_t box1, CUtensorMapSwizzle swizzle) {
+    auto enc = encode_fn();
+    if (!enc) return fail(B2B_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[3] = {dim0, dim1, dim2};
+    cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    cuuint32_t box[3] = {box0, box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(B2B_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (" + std::to_string(r) + ")");
+    return B2B_OK;
+}
+
 }  // namespace b2b

@@ -364,3 +364,63 @@ def test_sgemm_bias_equals_sgemm_plus_saxpy(handle, oracle):
     handle.sgemm_bias(cfg, a, b, c2, bd)
     handle.synchronize()
     np.testing.assert_allclose(handle.download(c2), handle.download(c1), rtol=0, atol=1e-5)
+
+
+# ------------------------------------------- FFMA kernel forms, same bits
+
+@pytest.mark.parametrize("m,n,k,alpha,beta", [(1000, 1028, 1000, 1.5, 0.5), (300, 1024, 96, 1.0, 0.0),
+                                              (256, 2048, 64, 0.75, 0.25)])
+def test_sgemm_ffma_kernels_bit_identical(monkeypatch, oracle, m, n, k, alpha, beta):
+    # Every FP32 FFMA kernel sums each output over k in order with one fma per
+    # step, so the forms must agree bit for bit: the cp.async kernel (variant
+    # 11), the TMA-fed kernel on a transposed A with scalar FFMA (20), FFMA2
+    # on row pairs (21, the default), FFMA2 on column pairs (22), and the
+    # TMA-fed kernel on row-major A (23).
+    import b2blas
+
+    A = oracle.uniform_f32(m * k, 21, 1)
+    B = oracle.uniform_f32(k * n, 21, 2)
+    C = oracle.uniform_f32(m * n, 21, 3)
+    cfg = b2blas.GemmConfig(m, n, k, alpha, beta)
+    outs = {}
+    for v in ("11", "20", "21", "22", "23"):
+        monkeypatch.setenv("B2B_SGEMM_VARIANT", v)
+        h = b2blas.Handle(0)
+        try:
+            outs[v] = _gemm_dev(h, "sgemm", None, cfg, A, B, C)
+        finally:
+            h.close()
+    ref = oracle.sgemm_f64(m, n, k, alpha, A, B, beta, C)
+    assert oracle.rel_err(outs["11"], ref) <= oracle.tol_normwise(k, "f32")
+    for v in ("20", "21", "22", "23"):
+        assert np.array_equal(outs[v], outs["11"]), v
+
+
+def test_strided_batched_tma_kernel_bit_identical(monkeypatch, oracle):
+    # The batched default (TMA-fed on row-major A, 3-D tensor maps) against
+    # the cp.async kernel, with gaps between batches and ragged M/N edges.
+    import b2blas
+
+    batch, m, n, k = 12, 200, 136, 100
+    sa, sb, sc = m * k + 4, k * n + 8, m * n + 12
+    A = oracle.uniform_f32(batch * sa, 22, 1)
+    B = oracle.uniform_f32(batch * sb, 22, 2)
+    C = oracle.uniform_f32(batch * sc, 22, 3)
+    cfg = b2blas.GemmConfig(m, n, k, 1.5, 0.5)
+    outs = {}
+    for v in ("0", "11"):
+        monkeypatch.setenv("B2B_SGEMM_VARIANT", v)
+        h = b2blas.Handle(0)
+        try:
+            a, b, c = h.upload(A), h.upload(B), h.upload(C)
+            h.strided_batched_sgemm(cfg, batch, a, sa, b, sb, c, sc)
+            h.synchronize()
+            outs[v] = h.download(c)
+        finally:
+            h.close()
+    assert np.array_equal(outs["0"], outs["11"])
+    ref = oracle.sgemm_strided_batched_f64(m, n, k, 1.5, A, sa, B, sb, 0.5, C, sc, batch)
+    got = np.concatenate([outs["0"][i * sc:i * sc + m * n] for i in range(batch)])
+    assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f32")
+    for i in range(batch):
+        assert np.array_equal(outs["0"][i * sc + m * n:(i + 1) * sc], C[i * sc + m * n:(i + 1) * sc])

@@ -81,6 +81,25 @@ int finish(b2b_handle *h) {
 
 // Pipelined host-slice GEMM for element type T, with `launch` the device
 // launcher for one row panel.
+// Copy schedule for a pipelined call (see b2b_handle::copy_mode_*): 0 phased
+// (downloads wait for the last upload), 1 full duplex.  Large calls try each
+// once, then keep the faster; small ones stay phased.
+int copy_mode(const b2b_handle *h, bool large) {
+    if (h->copy_mode_forced >= 0) return h->copy_mode_forced;
+    if (!large || h->copy_mode_ms_per_gb[0] == 0.0) return 0;
+    if (h->copy_mode_ms_per_gb[1] == 0.0) return 1;
+    return h->copy_mode_ms_per_gb[1] < h->copy_mode_ms_per_gb[0] ? 1 : 0;
+}
+
+void record_copy_mode(b2b_handle *h, bool large, int mode, std::chrono::steady_clock::time_point t_start,
+                      size_t bytes) {
+    if (!large || h->copy_mode_forced >= 0) return;
+    const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_start).count();
+    const double per_gb = ms / (static_cast<double>(bytes) / 1e9);
+    double &slot = h->copy_mode_ms_per_gb[mode];
+    slot = slot == 0.0 ? per_gb : (slot < per_gb ? slot : per_gb);
+}
+
 template <typename T, typename S, typename Launch>
 int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S alpha, const T *A, size_t a_len,
                 const T *B, size_t b_len, S beta, T *C, size_t c_len, Launch launch) {
@@ -139,17 +158,7 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     cudaEvent_t *ev_c = ev_b + nb;                         // tile (i, j) computed
     cudaEvent_t start_ev = ev_c[panels * nb], up_done = ev_c[panels * nb + 1];
     cudaStream_t up = h->copy_stream, down = h->down_stream;
-    // Copy schedule (see b2b_handle::copy_mode_*): try each mode once on large
-    // calls, then keep the faster.
-    int mode = 0;
-    if (h->copy_mode_forced >= 0)
-        mode = h->copy_mode_forced;
-    else if (large && h->copy_mode_ms_per_gb[0] == 0.0)
-        mode = 0;
-    else if (large && h->copy_mode_ms_per_gb[1] == 0.0)
-        mode = 1;
-    else if (large)
-        mode = h->copy_mode_ms_per_gb[1] < h->copy_mode_ms_per_gb[0] ? 1 : 0;
+    const int mode = copy_mode(h, large);
     const auto t_start = std::chrono::steady_clock::now();
     cudaError_t e = cudaSuccess;
     cudaStream_t cs = h->stream;
@@ -213,13 +222,7 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
         cudaStreamSynchronize(cs);
         return fail_cuda(e, fn);
     }
-    if (large && h->copy_mode_forced < 0) {
-        const double ms =
-            std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_start).count();
-        const double per_gb = ms / (static_cast<double>(bytes) / 1e9);
-        double &slot = h->copy_mode_ms_per_gb[mode];
-        slot = slot == 0.0 ? per_gb : (slot < per_gb ? slot : per_gb);
-    }
+    record_copy_mode(h, large, mode, t_start, bytes);
     return finish(h);
 }
 
@@ -293,14 +296,75 @@ int b2b_sgemm_strided_batched_simple(b2b_handle *h, size_t m, size_t n, size_t k
     float *dB = reinterpret_cast<float *>(static_cast<char *>(stage) + ob);
     float *dC = reinterpret_cast<float *>(static_cast<char *>(stage) + oc);
     // Packed outputs with beta == 0: C is write-only.  Otherwise upload it
-    // whole so elements between batches come back unchanged.
+    // so that elements between batches come back unchanged.
     const bool packed = stride_c == m * n;
     const bool up_c = beta != 0.0f || !packed;
-    if ((rc = h2d(h, dA, A, ea)) || (rc = h2d(h, dB, B, eb))) return rc;
-    if (up_c && (rc = h2d(h, dC, C, ec))) return rc;
-    rc = launch_sgemm_strided_batched(h, m, n, k, alpha, dA, stride_a, dB, stride_b, beta, dC, stride_c, batch);
-    if (rc) return rc;
-    if ((rc = d2h(h, C, dC, packed ? batch * m * n * 4 : ec))) return rc;
+    // Chunks of consecutive batches (h->host_panels of them on large calls),
+    // pipelined like the GEMMs: chunk c's A, B (and C) ranges go up on the
+    // copy stream, its GEMM waits for them on the compute stream, and its C
+    // range comes back on the download stream while later chunks still
+    // upload (full duplex) or after the last upload (phased).  The device
+    // copy mirrors the host layout, gaps included.
+    const size_t bytes = ea + eb + (up_c ? ec : 0) + (packed ? batch * m * n * 4 : ec);
+    const bool large = bytes >= (size_t(64) << 20);
+    size_t chunks = large ? static_cast<size_t>(h->host_panels > 0 ? h->host_panels : 1) : 1;
+    if (chunks > batch) chunks = batch;
+    const size_t per = (batch + chunks - 1) / chunks;
+    chunks = (batch + per - 1) / per;
+    if ((rc = pipe_setup(h, static_cast<int>(2 * chunks + 2)))) return rc;
+    cudaEvent_t *ev_up = h->pipe_events, *ev_done = ev_up + chunks;
+    cudaEvent_t start_ev = ev_done[chunks], up_done = ev_done[chunks + 1];
+    cudaStream_t cs = h->stream, up = h->copy_stream, down = h->down_stream;
+    const int mode = copy_mode(h, large);
+    const auto t_start = std::chrono::steady_clock::now();
+    // [first element, end) of chunk c's batches in a strided operand
+    auto span = [&](size_t c, size_t stride, size_t mat) {
+        const size_t b0 = c * per, b1 = b0 + per < batch ? b0 + per : batch;
+        return std::make_pair(b0 * stride, (b1 - 1) * stride + mat);
+    };
+    cudaError_t e = cudaEventRecord(start_ev, cs);  // earlier users of the staging buffer first
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(up, start_ev, 0);
+    for (size_t c = 0; c < chunks && e == cudaSuccess; ++c) {
+        const auto ra = span(c, stride_a, m * k), rb = span(c, stride_b, k * n), rcn = span(c, stride_c, m * n);
+        e = cudaMemcpyAsync(dA + ra.first, A + ra.first, (ra.second - ra.first) * 4, cudaMemcpyHostToDevice, up);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(dB + rb.first, B + rb.first, (rb.second - rb.first) * 4, cudaMemcpyHostToDevice, up);
+        if (e == cudaSuccess && up_c)
+            e = cudaMemcpyAsync(dC + rcn.first, C + rcn.first, (rcn.second - rcn.first) * 4, cudaMemcpyHostToDevice,
+                                up);
+        if (e == cudaSuccess) e = cudaEventRecord(ev_up[c], up);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(up_done, up);
+    for (size_t c = 0; c < chunks && e == cudaSuccess; ++c) {
+        const size_t b0 = c * per, nbat = b0 + per < batch ? per : batch - b0;
+        e = cudaStreamWaitEvent(cs, ev_up[c], 0);
+        if (e != cudaSuccess) break;
+        rc = launch_sgemm_strided_batched(h, m, n, k, alpha, dA + b0 * stride_a, stride_a, dB + b0 * stride_b,
+                                          stride_b, beta, dC + b0 * stride_c, stride_c, nbat);
+        if (rc) {
+            cudaStreamSynchronize(up);
+            cudaStreamSynchronize(cs);
+            return rc;
+        }
+        e = cudaEventRecord(ev_done[c], cs);
+    }
+    if (e == cudaSuccess && mode == 0) e = cudaStreamWaitEvent(down, up_done, 0);
+    for (size_t c = 0; c < chunks && e == cudaSuccess; ++c) {
+        const auto rcn = span(c, stride_c, m * n);
+        e = cudaStreamWaitEvent(down, ev_done[c], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(C + rcn.first, dC + rcn.first, (rcn.second - rcn.first) * 4, cudaMemcpyDeviceToHost,
+                                down);
+    }
+    cudaError_t e2 = cudaStreamSynchronize(up);
+    cudaError_t e3 = cudaStreamSynchronize(down);
+    if (e == cudaSuccess) e = e2;
+    if (e == cudaSuccess) e = e3;
+    if (e != cudaSuccess) {
+        cudaStreamSynchronize(cs);
+        return fail_cuda(e, fn);
+    }
+    record_copy_mode(h, large, mode, t_start, bytes);
     return finish(h);
 }
 

@@ -424,3 +424,40 @@ def test_strided_batched_tma_kernel_bit_identical(monkeypatch, oracle):
     assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f32")
     for i in range(batch):
         assert np.array_equal(outs["0"][i * sc + m * n:(i + 1) * sc], C[i * sc + m * n:(i + 1) * sc])
+
+
+@pytest.mark.parametrize("gap,beta", [(0, 0.0), (0, 0.5), (3, 0.0), (3, 0.5)])
+def test_strided_batched_simple_pipelined(monkeypatch, oracle, gap, beta):
+    # Large host-slice calls run in chunks of batches over three streams
+    # (upload / compute / download); both copy schedules must give the bits
+    # of the device-buffer call, leave the gaps between batches untouched
+    # and not write past the last batch.
+    import b2blas
+
+    batch, m, n, k = 1000, 128, 128, 128  # 197 MB of operands: pipelined
+    sa, sb, sc = m * k + 4 * gap, k * n + 8 * gap, m * n + 4 * gap
+    A = oracle.uniform_f32(batch * sa, 23, 1)
+    B = oracle.uniform_f32(batch * sb, 23, 2)
+    C = oracle.uniform_f32(batch * sc + 5, 23, 3)  # 5 elements past the last batch's stride
+    cfg = b2blas.GemmConfig(m, n, k, 1.25, beta)
+    h = b2blas.Handle(0)
+    try:
+        a, b, c = h.upload(A), h.upload(B), h.upload(C)
+        h.strided_batched_sgemm(cfg, batch, a, sa, b, sb, c, sc)
+        h.synchronize()
+        want = h.download(c)
+    finally:
+        h.close()
+    for mode in ("0", "1"):
+        monkeypatch.setenv("B2B_COPY_MODE", mode)
+        h = b2blas.Handle(0)
+        try:
+            host = C.copy()
+            h.strided_batched_sgemm_simple(cfg, batch, A, sa, B, sb, host, sc)
+        finally:
+            h.close()
+        assert np.array_equal(host, want), mode
+        assert np.array_equal(host[batch * sc:], C[batch * sc:])
+    ref = oracle.sgemm_strided_batched_f64(m, n, k, 1.25, A[:3 * sa], sa, B[:3 * sb], sb, beta, C[:3 * sc], sc, 3)
+    got = np.concatenate([want[i * sc:i * sc + m * n] for i in range(3)])
+    assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f32")

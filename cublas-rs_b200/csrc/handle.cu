@@ -177,6 +177,10 @@ int b2b_create(int device, b2b_handle **out) {
         const int p = atoi(v);
         if (p >= 1 && p <= 16) h->host_col_panels = p;
     }
+    if (const char *v = getenv("B2B_HOST_LANES")) {
+        const int p = atoi(v);
+        if (p == 1 || p == 2) h->host_lanes = p;
+    }
     const char *single = getenv("B2B_HGEMM_SINGLE_CTA");
     h->force_single_cta = single && single[0] == '1';
     if (const char *v = getenv("B2B_SGEMM_VARIANT")) h->sgemm_variant = atoi(v);
@@ -199,11 +203,14 @@ int b2b_destroy(b2b_handle *h) {
     if (h->stream && h->stream != h->own_stream) cudaStreamSynchronize(h->stream);
     if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);
     if (h->down_stream) cudaStreamSynchronize(h->down_stream);
+    if (h->compute2) cudaStreamSynchronize(h->compute2);
     for (int i = 0; i < h->pipe_event_count; ++i) cudaEventDestroy(h->pipe_events[i]);
     delete[] h->pipe_events;
     if (h->switch_event) cudaEventDestroy(h->switch_event);
     if (h->down_stream) cudaStreamDestroy(h->down_stream);
     if (h->workspace) cudaFree(h->workspace);
+    if (h->workspace2) cudaFree(h->workspace2);
+    if (h->compute2) cudaStreamDestroy(h->compute2);
     if (h->staging) cudaFree(h->staging);
     if (h->d_status) cudaFree(h->d_status);
     if (h->copy_stream) cudaStreamDestroy(h->copy_stream);

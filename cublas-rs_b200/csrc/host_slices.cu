@@ -47,6 +47,7 @@ int dim_err(const char *fn, const char *what, size_t expected, size_t got) {
 int pipe_setup(b2b_handle *h, int nev) {
     cudaError_t e = cudaSuccess;
     if (!h->down_stream) e = cudaStreamCreateWithFlags(&h->down_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess && !h->compute2) e = cudaStreamCreateWithFlags(&h->compute2, cudaStreamNonBlocking);
     if (e == cudaSuccess && h->pipe_event_count < nev) {
         cudaEvent_t *ev = new (std::nothrow) cudaEvent_t[nev];
         if (!ev) return fail(B2B_ERR_ALLOC, "pipeline events: out of host memory");
@@ -81,6 +82,22 @@ int finish(b2b_handle *h) {
 
 // Pipelined host-slice GEMM for element type T, with `launch` the device
 // launcher for one row panel.
+// While alive, the handle issues work on its second compute lane: stream
+// and workspace swap with compute2 / workspace2 (a launch's scratch, such as
+// the SGEMM's transposed A, must not be shared by two lanes in flight).
+struct SecondLane {
+    b2b_handle *h;
+    explicit SecondLane(b2b_handle *hh) : h(hh) { swap_lane(); }
+    ~SecondLane() { swap_lane(); }
+    void swap_lane() {
+        std::swap(h->stream, h->compute2);
+        std::swap(h->workspace, h->workspace2);
+        std::swap(h->workspace_bytes, h->workspace2_bytes);
+    }
+    SecondLane(const SecondLane &) = delete;
+    SecondLane &operator=(const SecondLane &) = delete;
+};
+
 // Copy schedule for a pipelined call (see b2b_handle::copy_mode_*): 0 phased
 // (downloads wait for the last upload), 1 full duplex.  Large calls try each
 // once, then keep the faster; small ones stay phased.
@@ -136,10 +153,11 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     size_t prow = round_up((m + panels - 1) / panels, 128);
     if (prow > m) prow = m;
     panels = static_cast<int>((m + prow - 1) / prow);
-    // Column panels pay off where the copies bound the call (f16: 4); a
-    // compute-bound FP32/FP64 call keeps whole row panels, whose GEMMs fill
-    // the GPU (a 1024 x 2048 tile is 64 CTAs of 128 x 256).
-    int nb = large ? (h->host_col_panels > 0 ? h->host_col_panels : (sizeof(T) == 2 ? 4 : 1)) : 1;
+    // Column panels shorten the wait for the first tile (it needs only B_0):
+    // 4 for f16, whose call the copies bound; 2 for FP32/FP64, whose tiles
+    // must stay large (a 1024 x 4096 FP32 tile is 128 CTAs of 128 x 256; the
+    // two compute lanes below keep the GPU full across tile boundaries).
+    int nb = large ? (h->host_col_panels > 0 ? h->host_col_panels : (sizeof(T) == 2 ? 4 : 2)) : 1;
     size_t pcol = round_up((n + nb - 1) / nb, 256);
     if (pcol > n) pcol = n;
     nb = static_cast<int>((n + pcol - 1) / pcol);
@@ -151,12 +169,13 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     auto dB_of = [&](int j) { return dB + k * (static_cast<size_t>(j) * pcol); };
     auto dC_of = [&](int i, int j) { return dC + static_cast<size_t>(i) * prow * n + rows_of(i) * (j * pcol); };
 
-    const int nev = panels + nb + panels * nb + 2;
+    const int nev = panels + nb + panels * nb + 3;
     if ((rc = pipe_setup(h, nev))) return rc;
     cudaEvent_t *ev_a = h->pipe_events;                    // A_i (and C_i) uploaded
     cudaEvent_t *ev_b = ev_a + panels;                     // B_j uploaded
     cudaEvent_t *ev_c = ev_b + nb;                         // tile (i, j) computed
     cudaEvent_t start_ev = ev_c[panels * nb], up_done = ev_c[panels * nb + 1];
+    cudaEvent_t lane2_done = ev_c[panels * nb + 2];
     cudaStream_t up = h->copy_stream, down = h->down_stream;
     const int mode = copy_mode(h, large);
     const auto t_start = std::chrono::steady_clock::now();
@@ -167,6 +186,7 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     // the staging buffer) must finish before the copies overwrite it.
     e = cudaEventRecord(start_ev, cs);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(up, start_ev, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(h->compute2, start_ev, 0);
     // Upload order: B_0 A_0 B_1 A_1 ... then the remaining A_i (or B_j).
     int na = 0, nbu = 0;  // pieces uploaded so far
     std::vector<std::pair<int, int>> order;  // tiles in the order they become computable
@@ -191,20 +211,34 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
         }
     }
     if (e == cudaSuccess) e = cudaEventRecord(up_done, up);
+    // Tiles alternate between the two compute lanes (odd ones on compute2).
     for (size_t t = 0; t < order.size() && e == cudaSuccess; ++t) {
         const int i = order[t].first, j = order[t].second;
-        e = cudaStreamWaitEvent(cs, ev_a[i], 0);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ev_b[j], 0);
+        const bool second = h->host_lanes == 2 && (t & 1) != 0;
+        cudaStream_t ts = second ? h->compute2 : cs;
+        e = cudaStreamWaitEvent(ts, ev_a[i], 0);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ts, ev_b[j], 0);
         if (e != cudaSuccess) break;
-        rc = launch(h, rows_of(i), cols_of(j), k, alpha, dA + static_cast<size_t>(i) * prow * k, dB_of(j), beta,
-                    dC_of(i, j));
+        if (second) {
+            SecondLane lane(h);
+            rc = launch(h, rows_of(i), cols_of(j), k, alpha, dA + static_cast<size_t>(i) * prow * k, dB_of(j), beta,
+                        dC_of(i, j));
+        } else {
+            rc = launch(h, rows_of(i), cols_of(j), k, alpha, dA + static_cast<size_t>(i) * prow * k, dB_of(j), beta,
+                        dC_of(i, j));
+        }
         if (rc) {
             cudaStreamSynchronize(up);
+            cudaStreamSynchronize(h->compute2);
             cudaStreamSynchronize(cs);
             return rc;
         }
-        e = cudaEventRecord(ev_c[i * nb + j], cs);
+        e = cudaEventRecord(ev_c[i * nb + j], ts);
     }
+    // The compute stream ends behind the second lane, so finishing the call
+    // (and the next call's start) covers both.
+    if (e == cudaSuccess) e = cudaEventRecord(lane2_done, h->compute2);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, lane2_done, 0);
     // Phased mode: the device-to-host copies wait for the last upload.
     if (e == cudaSuccess && mode == 0) e = cudaStreamWaitEvent(down, up_done, 0);
     for (size_t t = 0; t < order.size() && e == cudaSuccess; ++t) {
@@ -219,6 +253,7 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     if (e == cudaSuccess) e = e2;
     if (e == cudaSuccess) e = e3;
     if (e != cudaSuccess) {
+        cudaStreamSynchronize(h->compute2);
         cudaStreamSynchronize(cs);
         return fail_cuda(e, fn);
     }

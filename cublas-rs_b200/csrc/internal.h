@@ -38,6 +38,12 @@ struct b2b_handle {
     // first use): `up` carries host-to-device copies, `down` device-to-host.
     cudaStream_t copy_stream = nullptr;  // up
     cudaStream_t down_stream = nullptr;
+    // Second compute lane of the host-slice GEMM pipeline: consecutive tiles
+    // alternate between `stream` and this one (each with its own workspace),
+    // so one tile's last wave overlaps the next tile's first.
+    cudaStream_t compute2 = nullptr;
+    void *workspace2 = nullptr;
+    size_t workspace2_bytes = 0;
     cudaEvent_t *pipe_events = nullptr;
     int pipe_event_count = 0;
     // Copy scheduling of large host-slice GEMMs: 0 = phased (device-to-host
@@ -48,6 +54,7 @@ struct b2b_handle {
     int copy_mode_forced = -1;
     int host_panels = 8;                // row panels of a large host-slice GEMM (B2B_HOST_PANELS)
     int host_col_panels = 0;            // column panels of B in a large host-slice GEMM; 0 = auto (B2B_HOST_COL_PANELS)
+    int host_lanes = 2;                 // compute lanes of the host-slice GEMM pipeline, 1 or 2 (B2B_HOST_LANES)
     double copy_mode_ms_per_gb[2] = {0.0, 0.0};
     // Upper bound on any single bounded device wait, in nanoseconds.
     uint64_t wait_limit_ns = 2000000000ull;

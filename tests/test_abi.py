@@ -31,6 +31,13 @@ def test_library_exports_every_declared_symbol():
     assert sorted(_lib.SIGNATURES) == names
 
 
+def test_integration_binding_covers_the_header():
+    # INTEGRATION.md's Rust FFI block declares every entry point, once.
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    declared = re.findall(r"pub fn (b2b_\w+)\(", doc)
+    assert sorted(declared) == _header_functions()
+
+
 def test_library_exports_nothing_else():
     # Only b2b_* symbols are visible (the .so is built with hidden visibility).
     import subprocess

@@ -770,27 +770,56 @@ class MlpWorkload(Workload):
         self.bvec = [wrap(t) for t in self.bias_vec]
         self.fused = bool(args.fused)
         self.algo = b2blas.Algo.Tf32x3 if args.tf32x3 else b2blas.Algo.Default
-        per_gemm = [sgemm_kernels_per_call(self.batch, self.dims[i + 1], self.dims[i], bool(args.tf32x3))
-                    for i in range(4)]
-        self.launches_per_step = sum(per_gemm) + (0 if self.fused else 4)  # + a saxpy per layer
+        # --mlp-streams 2: the batch as two halves, each on its own stream and
+        # handle (rows of a GEMM are independent, so the results are the same
+        # bits); one half's GEMM tail overlaps the other half's kernels.
+        self.streams = 2 if getattr(args, "mlp_streams", 2) == 2 else 1
+        self.lanes = [(h, 0, self.batch)]
+        if self.streams == 2:
+            half = self.batch // 2
+            self.s2 = torch.cuda.Stream()
+            self.h2 = b2blas.Handle(torch.cuda.current_device())
+            self.h2.set_stream(self.s2.cuda_stream)
+            self.lanes = [(h, 0, half), (self.h2, half, self.batch - half)]
+            self.ev_start, self.ev_done = torch.cuda.Event(), torch.cuda.Event()
+        # per lane: (handle, rows) -> buffers over that lane's rows
+        self.lane_bufs = []
+        for lh, r0, rows in self.lanes:
+            lw = lambda t, lh=lh: b2blas.DeviceBuffer.from_ptr(lh, t.data_ptr(), t.numel(), "float32", owner=t)  # noqa
+            self.lane_bufs.append({"x": lw(self.X[r0:r0 + rows]), "w": [lw(t) for t in self.W],
+                                   "b": [lw(t[r0:r0 + rows]) for t in self.bias], "bv": [lw(t) for t in self.bias_vec],
+                                   "z": [lw(t[r0:r0 + rows]) for t in self.Z]})
+        per_gemm = [sgemm_kernels_per_call(rows, self.dims[i + 1], self.dims[i], bool(args.tf32x3))
+                    for _, _, rows in self.lanes for i in range(4)]
+        self.launches_per_step = sum(per_gemm) + (0 if self.fused else 4 * self.streams)  # + a saxpy per layer
         self.kernel = "sgemm_tma_kernel"
         self.bound = "fma"
 
     def forward(self, xb):
+        import torch
+
         import b2blas
 
-        inp = xb
-        for i in range(4):
-            fi, fo = self.dims[i], self.dims[i + 1]
-            cfg = b2blas.GemmConfig(self.batch, fo, fi, 1.0, 0.0)
-            if self.fused:
-                # bias (and, for hidden layers, ReLU) in the GEMM epilogue
-                self.h.sgemm_bias(cfg, inp, self.wb[i], self.zb[i], self.bvec[i], relu=i < 3, algo=self.algo)
-            else:
-                # the example's pattern: sgemm + saxpy of the pre-broadcast bias
-                self.h.sgemm_tiled(cfg, inp, self.wb[i], self.zb[i])
-                self.h.saxpy(self.batch * fo, 1.0, self.bb[i], self.zb[i])
-            inp = self.zb[i]
+        if self.streams == 2:  # the second lane starts behind the step's earlier work
+            self.ev_start.record(torch.cuda.current_stream())
+            self.s2.wait_event(self.ev_start)
+        for li, (lh, r0, rows) in enumerate(self.lanes):
+            bufs = self.lane_bufs[li]
+            inp = xb if self.streams == 1 else bufs["x"]
+            for i in range(4):
+                fi, fo = self.dims[i], self.dims[i + 1]
+                cfg = b2blas.GemmConfig(rows, fo, fi, 1.0, 0.0)
+                if self.fused:
+                    # bias (and, for hidden layers, ReLU) in the GEMM epilogue
+                    lh.sgemm_bias(cfg, inp, bufs["w"][i], bufs["z"][i], bufs["bv"][i], relu=i < 3, algo=self.algo)
+                else:
+                    # the example's pattern: sgemm + saxpy of the pre-broadcast bias
+                    lh.sgemm_tiled(cfg, inp, bufs["w"][i], bufs["z"][i])
+                    lh.saxpy(rows * fo, 1.0, bufs["b"][i], bufs["z"][i])
+                inp = bufs["z"][i]
+        if self.streams == 2:  # and the step ends behind it
+            self.ev_done.record(self.s2)
+            torch.cuda.current_stream().wait_event(self.ev_done)
 
     def step(self):
         self.forward(self.xb)
@@ -833,9 +862,19 @@ class MlpWorkload(Workload):
         how = ("fused sgemm+bias+ReLU epilogue" if self.fused else "sgemm + saxpy bias") + \
             (", 3xTF32" if self.algo == __import__("b2blas").Algo.Tf32x3 else "")
         return {"workload": f"mlp forward 1024-4096-4096-4096-1024, batch 4096, {how}"
+                            + (", two half-batch streams" if self.streams == 2 else "")
                             + (", one replica per GPU" if self.world > 1 else ""),
-                "layers": self.dims, "batch": self.batch, "parallelism": f"replicas x{self.world}",
+                "layers": self.dims, "batch": self.batch, "streams": self.streams,
+                "parallelism": f"replicas x{self.world}",
                 "l2": "weights + activations larger than L2: no flush needed"}
+
+    def close(self):
+        if self.streams == 2:
+            import torch
+
+            torch.cuda.synchronize()
+            self.h2.set_stream(None)
+            self.h2.close()
 
     def cpu_sample(self, oracle, target_s):
         import numpy as np
@@ -1165,6 +1204,8 @@ def main():
                     help="as --gather, but GEMM into the panel + NCCL all-gather + re-layout kernel")
     ap.add_argument("--tf32x3", action="store_true", help="sgemm/mlp: the opt-in 3xTF32 tensor-core kernel")
     ap.add_argument("--fused", action="store_true", help="mlp: bias (+ReLU) fused into the SGEMM epilogue")
+    ap.add_argument("--mlp-streams", type=int, choices=[1, 2], default=2,
+                    help="mlp: the batch as two halves on two streams (default; same results) or one stream")
     ap.add_argument("--e2e-steps", type=int, default=None, help="0 skips the end-to-end pass")
     ap.add_argument("--e2e-host", choices=["b2b", "torch"], default="b2b",
                     help="page-locked host buffers of the end-to-end pass: b2b_host_alloc or torch pin_memory")

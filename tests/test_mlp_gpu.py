@@ -1,7 +1,7 @@
 """The mlp example's forward as bench.py runs it: 4 layers 1024-4096-4096-4096-1024,
 batch 4096, bias (+ReLU on hidden layers) fused into the SGEMM epilogue.  Two
 half-batch streams must give the bits of one stream, and both must match a
-plain PyTorch fp32 forward (TF32 off) within the FP32 GEMM bound."""
+PyTorch fp64 forward of the same weights within the FP32 GEMM bound."""
 import pytest
 
 pytestmark = pytest.mark.gpu
@@ -41,15 +41,10 @@ def test_mlp_two_streams_same_bits_and_fp32_reference():
             h.close()
     torch.cuda.set_stream(torch.cuda.default_stream())
     assert torch.equal(outs[0], outs[1])
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False
-    try:
-        x = w1.X.double()
-        for i in range(4):
-            x = x @ w1.W[i].double() + w1.bias_vec[i].double()
-            if i < 3:
-                x = torch.relu(x)
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = prev
+    x = w1.X.double()
+    for i in range(4):
+        x = x @ w1.W[i].double() + w1.bias_vec[i].double()
+        if i < 3:
+            x = torch.relu(x)
     err = ((outs[0].double() - x).norm() / x.norm()).item()
     assert err <= 4 * 4096 * 2.0 ** -24, err  # 4*K*eps32 for the widest layer

@@ -359,14 +359,21 @@ int b2b_sgemm_strided_batched_simple(b2b_handle *h, size_t m, size_t n, size_t k
     };
     cudaError_t e = cudaEventRecord(start_ev, cs);  // earlier users of the staging buffer first
     if (e == cudaSuccess) e = cudaStreamWaitEvent(up, start_ev, 0);
+    // Each operand goes up once: a chunk copies only the part of its range
+    // beyond what earlier chunks copied (with a zero or overlapping stride,
+    // e.g. one A for every batch, later chunks reuse what is already there
+    // and nothing is rewritten under a running GEMM).
+    size_t hw_a = 0, hw_b = 0, hw_c = 0;
+    auto up_range = [&](float *d, const float *hsrc, std::pair<size_t, size_t> r, size_t &hw) {
+        const size_t from = r.first > hw ? r.first : hw;
+        if (r.second <= from) return cudaSuccess;
+        hw = r.second;
+        return cudaMemcpyAsync(d + from, hsrc + from, (r.second - from) * 4, cudaMemcpyHostToDevice, up);
+    };
     for (size_t c = 0; c < chunks && e == cudaSuccess; ++c) {
-        const auto ra = span(c, stride_a, m * k), rb = span(c, stride_b, k * n), rcn = span(c, stride_c, m * n);
-        e = cudaMemcpyAsync(dA + ra.first, A + ra.first, (ra.second - ra.first) * 4, cudaMemcpyHostToDevice, up);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(dB + rb.first, B + rb.first, (rb.second - rb.first) * 4, cudaMemcpyHostToDevice, up);
-        if (e == cudaSuccess && up_c)
-            e = cudaMemcpyAsync(dC + rcn.first, C + rcn.first, (rcn.second - rcn.first) * 4, cudaMemcpyHostToDevice,
-                                up);
+        e = up_range(dA, A, span(c, stride_a, m * k), hw_a);
+        if (e == cudaSuccess) e = up_range(dB, B, span(c, stride_b, k * n), hw_b);
+        if (e == cudaSuccess && up_c) e = up_range(dC, C, span(c, stride_c, m * n), hw_c);
         if (e == cudaSuccess) e = cudaEventRecord(ev_up[c], up);
     }
     if (e == cudaSuccess) e = cudaEventRecord(up_done, up);

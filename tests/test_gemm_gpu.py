@@ -461,3 +461,35 @@ def test_strided_batched_simple_pipelined(monkeypatch, oracle, gap, beta):
     ref = oracle.sgemm_strided_batched_f64(m, n, k, 1.25, A[:3 * sa], sa, B[:3 * sb], sb, beta, C[:3 * sc], sc, 3)
     got = np.concatenate([want[i * sc:i * sc + m * n] for i in range(3)])
     assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f32")
+
+
+def test_strided_batched_simple_pipelined_shared_a(monkeypatch, oracle):
+    # stride_a = 0: one A for every batch (the slice holds a single m x k
+    # matrix).  The pipelined host-slice call uploads it once and must give
+    # the device-buffer call's bits in both copy schedules.
+    import b2blas
+
+    batch, m, n, k = 1000, 128, 128, 128
+    A = oracle.uniform_f32(m * k, 24, 1)
+    B = oracle.uniform_f32(batch * k * n, 24, 2)
+    C = oracle.uniform_f32(batch * m * n, 24, 3)
+    cfg = b2blas.GemmConfig(m, n, k, 1.0, 0.5)
+    h = b2blas.Handle(0)
+    try:
+        a, b, c = h.upload(A), h.upload(B), h.upload(C)
+        h.strided_batched_sgemm(cfg, batch, a, 0, b, k * n, c, m * n)
+        h.synchronize()
+        want = h.download(c)
+    finally:
+        h.close()
+    for mode in ("0", "1"):
+        monkeypatch.setenv("B2B_COPY_MODE", mode)
+        h = b2blas.Handle(0)
+        try:
+            host = C.copy()
+            h.strided_batched_sgemm_simple(cfg, batch, A, 0, B, k * n, host, m * n)
+        finally:
+            h.close()
+        assert np.array_equal(host, want), mode
+    ref = oracle.sgemm_strided_batched_f64(m, n, k, 1.0, A, 0, B[:2 * k * n], k * n, 0.5, C[:2 * m * n], m * n, 2)
+    assert oracle.rel_err(want[:2 * m * n], ref) <= oracle.tol_normwise(k, "f32")

@@ -5,11 +5,15 @@
 
 One JSON line on rank 0.  The default workload is the HGEMM configuration:
 8192 x 8192 x 8192, f16 in / f32 accumulate / f16 out, alpha 1, beta 0,
-inputs i.i.d. normal(0, 0.1) rounded to f16 (seeded, synthetic).  On N GPUs
-(one process per GPU, torchrun) it is column-sharded with A replicated: rank
-r computes its own 8192 x 8192 panel of an 8192 x (8192*N) x 8192 product,
-so per-GPU work is fixed ("weak"); no collective runs in the data path
-unless --gather asks for the assembled C.
+inputs i.i.d. normal(0, 0.1) rounded to f16 (seeded, synthetic).  On N > 1
+GPUs (one process per GPU, torchrun) the same fixed 8192^3 problem is
+column-sharded with A replicated (8192/N columns of B and C per GPU) and
+the all-gather is fused into the GEMM: every rank's epilogue stores its
+panel into every rank's full row-major C over NVLink peer pointers, so each
+rank ends every step with the whole C ("strong" scaling; --no-gather keeps
+the panels, --gather-nccl gathers through NCCL + a re-layout kernel,
+--weak gives every rank its own 8192-column panel of an 8192 x 8192N x 8192
+product instead).
 
 A "step" is one GEMM call over one batch of resident device inputs, timed
 with CUDA events on the stream the kernels run on (K steps between a barrier
@@ -17,11 +21,22 @@ with CUDA events on the stream the kernels run on (K steps between a barrier
 through the host-slice API (b2b_hgemm_simple): every step copies A and B from
 page-locked host memory and C back.
 
+`secondary` carries the metric's other configurations, each device-timed
+the same way in its own region with its own clock record and roofline: on
+one GPU SGEMM 8192^3 (alpha 1.5, beta 0.5), SGEMV 16384^2 N, strided-batched
+SGEMM 4096 x 256^3 and DGEMM 4096^3; on N GPUs the batch-sharded
+strided-batched SGEMM (strong) and the weak-scaled HGEMM without a gather
+(--no-secondary skips them).
+
 Other workloads (--workload): sgemm (8192^3, alpha 1.5, beta 0.5), dgemm
 (4096^3), batched (4096 x 256^3 strided, batch-sharded), sgemv / dgemv /
 hgemv (16384^2, N, or T with --trans), reduce (sdot by default, --op
 nrm2|asum|iamax; 2^28-element f32 vectors), mlp (4 layers
 1024-4096-4096-4096-1024, batch 4096, sgemm + saxpy bias).
+
+Inputs: both arms draw every tensor from torch's CPU generator with a fixed
+seed per tensor (host_tensor), so the library and the reference arm see the
+same numbers; the library arm copies them to the device before timing.
 
 On one GPU the line also carries `reference_kernels`: the reference's own GPU
 kernels for the same operation (naive / tiled / vectorized / double_buf
@@ -32,7 +47,7 @@ same resident buffers (--no-ref-kernels skips them).
 
 --impl reference times the CPU restatement of the reference's algorithm
 (the oracle's host triple loop) on this machine's cores, rank 0 only, with a
-bounded sample of the same workload per step.
+bounded sample of the same workload per step, and prints the same config.
 """
 from __future__ import annotations
 
@@ -207,6 +222,140 @@ def _pinned_numpy(t):
     return ht, ht.numpy()
 
 
+# ------------------------------------------------------ seeded inputs
+
+DATA = ("synthetic: torch CPU generator, one fixed seed per tensor; normal(0,0.1)->f16 for HGEMM, "
+        "uniform[-1,1) otherwise")
+
+# Tensor ids of the seeded inputs: seed = INPUT_SEED + 1000 * chunk + id.
+INPUT_SEED = 4200
+TID = {"A": 1, "B": 2, "C": 3, "x": 4, "bias": 5, "y": 6, "W": 10}
+BATCH_CHUNK = 512  # strided-batched inputs are drawn 512 batches at a time
+
+
+def host_tensor(shape, tid, dtype, dist="uniform", std=0.1, chunk=0):
+    """A seeded synthetic input on the host (torch CPU generator): uniform
+    [-1, 1) or normal(0, std), then cast to `dtype` (f16 inputs are rounded
+    from f32).  Both bench arms call this, so they see the same numbers."""
+    import torch
+
+    g = torch.Generator().manual_seed(INPUT_SEED + 1000 * chunk + tid)
+    if dist == "normal":
+        t = torch.randn(shape, generator=g, dtype=torch.float64 if dtype == torch.float64 else torch.float32) * std
+    else:
+        t = torch.rand(shape, generator=g, dtype=torch.float64 if dtype == torch.float64 else torch.float32) * 2 - 1
+    return t.to(dtype)
+
+
+def batched_inputs(tid, b0, b1, m):
+    """Batches [b0, b1) of a strided-batched operand (m x m per batch), drawn
+    in chunks of BATCH_CHUNK batches so that each rank of a batch-sharded run
+    only generates its own range."""
+    import torch
+
+    parts = []
+    c = b0 // BATCH_CHUNK
+    while c * BATCH_CHUNK < b1:
+        lo, hi = c * BATCH_CHUNK, (c + 1) * BATCH_CHUNK
+        t = host_tensor((BATCH_CHUNK, m, m), tid, torch.float32, chunk=c)
+        parts.append(t[max(b0, lo) - lo:min(b1, hi) - lo])
+        c += 1
+    return torch.cat(parts) if len(parts) > 1 else parts[0].contiguous()
+
+
+def split_range(total, parts, index, align=1):
+    """[begin, end) of part `index` of `total` items in `parts` contiguous
+    pieces (boundaries multiples of `align`); the same rule as
+    b2blas.shard.split_range, restated so the reference arm needs no part of
+    the library."""
+    units = (total + align - 1) // align
+    base, rem = divmod(units, parts)
+    b = index * base + min(index, rem)
+    e = b + base + (1 if index < rem else 0)
+    return min(b * align, total), min(e * align, total)
+
+
+GEMM_KINDS = ("hgemm", "sgemm", "dgemm")
+GEMM_ALPHA_BETA = {"hgemm": (1.0, 0.0), "sgemm": (1.5, 0.5), "dgemm": (1.5, 0.5)}
+
+
+def gemm_dims(name, args):
+    d = 4096 if name == "dgemm" else 8192
+    return args.m or d, args.n or d, args.k or d
+
+
+def gather_mode(name, args, world):
+    """The gather a column-sharded GEMM asks for at `world` ranks: None,
+    "fused" (peer stores from the GEMM epilogue), "fused-multicast" or
+    "nccl".  HGEMM gathers by default on N > 1 GPUs (the fixed 8192^3
+    problem, every rank ends with the whole C)."""
+    if world <= 1 or name not in GEMM_KINDS:
+        return None
+    if args.gather_nccl:
+        return "nccl"
+    if args.gather_multicast:
+        return "fused-multicast"
+    if args.gather:
+        return "fused"
+    if args.no_gather or args.weak:
+        return None
+    return "fused" if name == "hgemm" else None
+
+
+def workload_config(name, args, world):
+    """The `config` record of a workload.  A function of the arguments and the
+    world size only, so that both arms print the same dict."""
+    if name in GEMM_KINDS:
+        m, n, k = gemm_dims(name, args)
+        alpha, beta = GEMM_ALPHA_BETA[name]
+        weak = bool(args.weak) and name == "hgemm"
+        n_glob = n * world if weak else n
+        per = n if weak else split_range(n, world, 0, 8)[1]
+        g = gather_mode(name, args, world)
+        if world > 1:
+            how = (f", column-sharded over {world} GPUs ({per} columns per GPU), A replicated"
+                   + (", C gathered on every GPU" if g else ""))
+        else:
+            how = ""
+        return {"workload": f"{name} {m}x{n_glob}x{k}" + how, "m": m, "n": n_glob, "k": k, "n_per_gpu": per,
+                "alpha": alpha, "beta": beta, "gather": g or False, "parallelism": f"column-shard x{world}",
+                "scaling": ("weak" if weak else "strong") if world > 1 else "weak",
+                "l2": "inputs larger than L2 (126 MB): no flush needed"}
+    if name == "batched":
+        b0, b1 = split_range(4096, world, 0)
+        return {"workload": "strided-batched sgemm 4096 x 256^3"
+                            + (f", {b1 - b0} batches per GPU" if world > 1 else ""),
+                "batch": 4096, "batch_per_gpu": b1 - b0, "m": 256, "n": 256, "k": 256,
+                "alpha": 1.0, "beta": 0.0, "parallelism": f"batch-shard x{world}",
+                "scaling": "strong" if world > 1 else "weak",
+                "l2": "inputs larger than L2 (3 GiB): no flush needed"}
+    if name in ("sgemv", "dgemv", "hgemv"):
+        esz = {"s": 4, "d": 8, "h": 2}[name[0]]
+        gib = 16384 * 16384 * esz / 2 ** 30
+        t = "T" if args.trans else "N"
+        return {"workload": f"{name} 16384x16384 {t}" + (", one replica per GPU" if world > 1 else ""),
+                "m": 16384, "n": 16384, "trans": t, "alpha": 1.0, "beta": 0.0,
+                "parallelism": f"replicas x{world}", "scaling": "weak",
+                "l2": f"A is {gib:g} GiB, larger than L2: no flush needed"}
+    if name == "reduce":
+        n = args.n or (1 << 28)
+        vec = 2 if args.op == "dot" else 1
+        return {"workload": f"s{args.op} n={n}" + (", one replica per GPU" if world > 1 else ""),
+                "n": n, "parallelism": f"replicas x{world}", "scaling": "weak",
+                "l2": f"{vec} x {n * 4 / 2 ** 30:g} GiB inputs, larger than L2: no flush needed"}
+    if name == "mlp":
+        how = ("fused sgemm+bias+ReLU epilogue" if args.fused else "sgemm + saxpy bias") + \
+            (", 3xTF32" if args.tf32x3 else "")
+        streams = 2 if getattr(args, "mlp_streams", 2) == 2 else 1
+        return {"workload": f"mlp forward 1024-4096-4096-4096-1024, batch 4096, {how}"
+                            + (", two half-batch streams" if streams == 2 else "")
+                            + (", one replica per GPU" if world > 1 else ""),
+                "layers": [1024, 4096, 4096, 4096, 1024], "batch": 4096, "streams": streams,
+                "parallelism": f"replicas x{world}", "scaling": "weak",
+                "l2": "weights + activations larger than L2: no flush needed"}
+    raise SystemExit(f"unknown workload {name}")
+
+
 class Workload:
     name = ""
     unit = "TFLOP/s"
@@ -215,24 +364,36 @@ class Workload:
     launches_per_step = 1
     kernel = ""
     bound = "tensor"
+    world = 1
+    args = None
 
     def units_per_step(self):  # flops (or bytes) this rank processes per step
         raise NotImplementedError
 
+    def total_units_per_step(self):  # over all ranks (replicas: world x this rank's)
+        return self.units_per_step() * self.world
+
     def scale(self, v):  # units/s -> unit
         return v / 1e12
+
+    def config(self):
+        return workload_config(self.name, self.args, self.world)
 
 
 class GemmWorkload(Workload):
     """C = alpha*A*B + beta*C with A replicated and B/C column panels."""
 
-    def __init__(self, h, rank, world, args, kind, m, n_total, k, alpha, beta, weak):
+    def __init__(self, h, rank, world, args, kind):
         import numpy as np
         import torch
 
         import b2blas
         from b2blas import shard
 
+        m, n_total, k = gemm_dims(kind, args)
+        alpha, beta = GEMM_ALPHA_BETA[kind]
+        weak = bool(args.weak) and kind == "hgemm"
+        self.name, self.args = kind, args
         self.h, self.kind = h, kind
         self.m, self.k, self.alpha, self.beta = m, k, alpha, beta
         self.world, self.rank = world, rank
@@ -246,23 +407,29 @@ class GemmWorkload(Workload):
             self.n = self.widths[rank]
             self.global_n = n_total
             self.scaling = "strong" if world > 1 else "weak"
+        self.col_off = sum(self.widths[:rank])
         dev = torch.device("cuda", torch.cuda.current_device())
         tdt = {"hgemm": torch.float16, "sgemm": torch.float32, "dgemm": torch.float64}[kind]
         self.dtype = {"hgemm": "f16", "sgemm": "f32", "dgemm": "f64"}[kind]
         self.np_dt = {"hgemm": np.uint16, "sgemm": np.float32, "dgemm": np.float64}[kind]
-        gA = torch.Generator(device=dev).manual_seed(42)  # replicated A: same on every rank
-        gB = torch.Generator(device=dev).manual_seed(1000 + rank)
-        gC = torch.Generator(device=dev).manual_seed(2000 + rank)
-        if kind == "hgemm":
-            self.A = (torch.randn(m, k, device=dev, generator=gA) * 0.1).to(tdt)
-            self.B = (torch.randn(k, self.n, device=dev, generator=gB) * 0.1).to(tdt)
-            self.C = (torch.randn(m, self.n, device=dev, generator=gC) * 0.1).to(tdt) if beta else \
-                torch.zeros(m, self.n, device=dev, dtype=tdt)
+        # The same seeded host inputs as the reference arm: A replicated; B
+        # and C the rank's column panel of the whole problem's (weak: the
+        # rank's own panel, drawn with the rank as chunk index).
+        dist = "normal" if kind == "hgemm" else "uniform"
+        self.A = host_tensor((m, k), TID["A"], tdt, dist).to(dev)
+        if weak:
+            self.B = host_tensor((k, self.n), TID["B"], tdt, dist, chunk=rank).to(dev)
         else:
-            self.A = (torch.rand(m, k, device=dev, generator=gA, dtype=tdt) * 2 - 1)
-            self.B = (torch.rand(k, self.n, device=dev, generator=gB, dtype=tdt) * 2 - 1)
-            self.C = (torch.rand(m, self.n, device=dev, generator=gC, dtype=tdt) * 2 - 1)
-        self.C0 = self.C.clone() if beta else None
+            self.B = host_tensor((k, n_total), TID["B"], tdt, dist)[:, self.col_off:self.col_off + self.n] \
+                .contiguous().to(dev)
+        if beta:
+            if weak:
+                self.C = host_tensor((m, self.n), TID["C"], tdt, dist, chunk=rank).to(dev)
+            else:
+                self.C = host_tensor((m, n_total), TID["C"], tdt, dist)[:, self.col_off:self.col_off + self.n] \
+                    .contiguous().to(dev)
+        else:
+            self.C = torch.zeros(m, self.n, device=dev, dtype=tdt)
         bdt = np.uint16 if kind == "hgemm" else self.np_dt
         self.a = b2blas.DeviceBuffer.from_ptr(h, self.A.data_ptr(), m * k, bdt, owner=self.A)
         self.b = b2blas.DeviceBuffer.from_ptr(h, self.B.data_ptr(), k * self.n, bdt, owner=self.B)
@@ -276,13 +443,15 @@ class GemmWorkload(Workload):
         self.bound = {"hgemm": "tensor", "sgemm": "fma", "dgemm": "fp64"}[kind]
         if kind == "sgemm" and args.tf32x3:
             self.kernel, self.bound = "sgemm_3xtf32_kernel", "tf32x3"
-        # --gather: every rank ends each step with the full C.  "fused": the
-        # GEMM writes its panel into every rank's C itself (b2b_*gemm_gather
-        # through IPC-mapped peer buffers), then a 1-element all-reduce orders
-        # the next step behind all ranks' writes.  "nccl": GEMM into the
-        # panel, NCCL all-gather of the panels, re-layout kernel.
-        self.gather = ("nccl" if args.gather_nccl else "fused") \
-            if (args.gather or args.gather_nccl or args.gather_multicast) and world > 1 else None
+        # A gathered C: every rank ends each step with the full C.  "fused":
+        # the GEMM writes its panel into every rank's C itself
+        # (b2b_*gemm_gather through IPC-mapped peer buffers), then a
+        # 1-element all-reduce orders the next step behind all ranks' writes.
+        # "nccl": GEMM into the panel, NCCL all-gather of the panels,
+        # re-layout kernel.
+        self.gather = gather_mode(kind, args, world)
+        if self.gather == "fused-multicast":
+            self.gather = "fused"  # becomes "fused-multicast" below once the multicast object exists
         self.mc = 0
         gemm_kernels = sgemm_kernels_per_call(m, self.n, k, args.tf32x3) if kind == "sgemm" else 1
         self.launches_per_step = gemm_kernels
@@ -293,7 +462,6 @@ class GemmWorkload(Workload):
         elif self.gather == "fused":
             if args.tf32x3:
                 raise SystemExit("--gather with --tf32x3 is not supported")
-            self.col_off = sum(self.widths[:rank])
             if kind == "hgemm" and not beta and args.gather_multicast:
                 # NVLink multicast (torch symmetric memory binds one buffer per
                 # rank): each output store leaves the GPU once.  Every GPU
@@ -395,15 +563,6 @@ class GemmWorkload(Workload):
     def e2e_step(self):
         self.simple(self.cfg, self.hA, self.hB, self.hC)
 
-    def config(self):
-        d = {"workload": f"{self.kind} {self.m}x{self.global_n}x{self.k}"
-                         + (f", column-sharded over {self.world} GPUs ({self.n} columns per GPU), A replicated"
-                            if self.world > 1 else ""),
-             "m": self.m, "n": self.global_n, "k": self.k, "n_per_gpu": self.n, "alpha": self.alpha,
-             "beta": self.beta, "gather": self.gather or False, "parallelism": f"column-shard x{self.world}",
-             "l2": "inputs larger than L2 (126 MB): no flush needed"}
-        return d
-
     def cpu_sample(self, oracle, target_s):
         """Times the host triple loop on a row sample of this rank's problem."""
         import numpy as np
@@ -456,6 +615,7 @@ class BatchedWorkload(Workload):
         from b2blas import shard
 
         self.h = h
+        self.name, self.args = "batched", args
         self.total_batch, self.m = 4096, 256
         b0, b1 = shard.batch_shard(self.total_batch, world, rank)
         self.batch = b1 - b0
@@ -463,9 +623,8 @@ class BatchedWorkload(Workload):
         self.scaling = "strong" if world > 1 else "weak"
         m = self.m
         dev = torch.device("cuda", torch.cuda.current_device())
-        g = torch.Generator(device=dev).manual_seed(42 + rank)
-        self.A = torch.rand(self.batch, m, m, device=dev, generator=g) * 2 - 1
-        self.B = torch.rand(self.batch, m, m, device=dev, generator=g) * 2 - 1
+        self.A = batched_inputs(TID["A"], b0, b1, m).to(dev)
+        self.B = batched_inputs(TID["B"], b0, b1, m).to(dev)
         self.C = torch.zeros(self.batch, m, m, device=dev)
         mk = m * m
         self.a = b2blas.DeviceBuffer.from_ptr(h, self.A.data_ptr(), self.batch * mk, "float32", owner=self.A)
@@ -481,6 +640,9 @@ class BatchedWorkload(Workload):
 
     def units_per_step(self):
         return 2.0 * self.batch * self.m ** 3
+
+    def total_units_per_step(self):
+        return 2.0 * self.total_batch * self.m ** 3
 
     def e2e_setup(self):
         self._hA, self.hA = _pinned_numpy(self.A)
@@ -502,13 +664,6 @@ class BatchedWorkload(Workload):
         pa, pb, pc, st = self.A.data_ptr(), self.B.data_ptr(), self._ref_c.data_ptr(), _cur_stream()
         return [("strided_batched_sgemm", lambda: R.sgemm_strided_batched(m, m, m, 1.0, pa, mk, pb, mk, 0.0, pc, mk,
                                                                           nb, st))]
-
-    def config(self):
-        return {"workload": f"strided-batched sgemm {self.total_batch} x {self.m}^3"
-                            + (f", {self.batch} batches per GPU" if self.world > 1 else ""),
-                "batch": self.total_batch, "batch_per_gpu": self.batch, "m": self.m, "n": self.m, "k": self.m,
-                "alpha": 1.0, "beta": 0.0, "parallelism": f"batch-shard x{self.world}",
-                "l2": "inputs larger than L2 (3 GiB): no flush needed"}
 
     def cpu_sample(self, oracle, target_s):
         import numpy as np
@@ -547,17 +702,16 @@ class GemvWorkload(Workload):
         import b2blas
 
         self.h, self.world, self.prec = h, world, prec
+        self.name, self.args = prec + "gemv", args
         self.m = self.n = 16384
         self.trans = 1 if args.trans else 0
         tdt, ndt, self.esize, self.dtype = {"s": (torch.float32, "float32", 4, "f32"),
                                            "d": (torch.float64, "float64", 8, "f64"),
                                            "h": (torch.float16, "uint16", 2, "f16")}[prec]
         dev = torch.device("cuda", torch.cuda.current_device())
-        g = torch.Generator(device=dev).manual_seed(42 + rank)
-        mk = lambda *shape: (torch.rand(*shape, device=dev, generator=g, dtype=torch.float32) * 2 - 1).to(tdt)  # noqa: E731
-        self.A = mk(self.m, self.n)
+        self.A = host_tensor((self.m, self.n), TID["A"], tdt).to(dev)
         xl, yl = (self.n, self.m) if self.trans == 0 else (self.m, self.n)
-        self.x = mk(xl)
+        self.x = host_tensor((xl,), TID["x"], tdt).to(dev)
         self.y = torch.zeros(yl, device=dev, dtype=tdt)
         buf = lambda t, n: b2blas.DeviceBuffer.from_ptr(h, t.data_ptr(), n, ndt, owner=t)  # noqa: E731
         self.a, self.xd, self.yd = buf(self.A, self.m * self.n), buf(self.x, xl), buf(self.y, yl)
@@ -605,14 +759,6 @@ class GemvWorkload(Workload):
         if self.prec == "d":
             return [("dgemv", lambda: R.dgemv(t, m, n, 1.0, pa, px, 0.0, py, st))]
         return [("hgemv", lambda: R.hgemv(t, m, n, 1.0, pa, px, 0.0, py, st))]
-
-    def config(self):
-        gib = self.m * self.n * self.esize / 2 ** 30
-        return {"workload": f"{self.prec}gemv {self.m}x{self.n} {'NT'[self.trans]}"
-                            + (f", one replica per GPU" if self.world > 1 else ""),
-                "m": self.m, "n": self.n, "trans": "NT"[self.trans], "alpha": 1.0, "beta": 0.0,
-                "parallelism": f"replicas x{self.world}",
-                "l2": f"A is {gib:g} GiB, larger than L2: no flush needed"}
 
     def cpu_sample(self, oracle, target_s):
         np = self._np
@@ -663,12 +809,12 @@ class ReduceWorkload(Workload):
         import b2blas
 
         self.h, self.world = h, world
+        self.name, self.args = "reduce", args
         self.op = args.op
         self.n = args.n or (1 << 28)
         dev = torch.device("cuda", torch.cuda.current_device())
-        g = torch.Generator(device=dev).manual_seed(42 + rank)
-        self.x = torch.rand(self.n, device=dev, generator=g) * 2 - 1
-        self.y = torch.rand(self.n, device=dev, generator=g) * 2 - 1 if self.op == "dot" else None
+        self.x = host_tensor((self.n,), TID["x"], torch.float32).to(dev)
+        self.y = host_tensor((self.n,), TID["y"], torch.float32).to(dev) if self.op == "dot" else None
         self.res = torch.zeros(1, device=dev, dtype=torch.int64 if self.op == "iamax" else torch.float32)
         self.xd = b2blas.DeviceBuffer.from_ptr(h, self.x.data_ptr(), self.n, "float32", owner=self.x)
         self.yd = (b2blas.DeviceBuffer.from_ptr(h, self.y.data_ptr(), self.n, "float32", owner=self.y)
@@ -712,11 +858,6 @@ class ReduceWorkload(Workload):
         py, po, op = (self.y.data_ptr() if self.y is not None else 0), self._ref_out.data_ptr(), self.op
         return [("s" + op if op != "iamax" else "isamax", lambda: R.sreduce(op, n, px, py, po, st))]
 
-    def config(self):
-        return {"workload": f"s{self.op} n={self.n}" + (f", one replica per GPU" if self.world > 1 else ""),
-                "n": self.n, "parallelism": f"replicas x{self.world}",
-                "l2": f"{self.vectors} x {self.n * 4 / 2 ** 30:g} GiB inputs, larger than L2: no flush needed"}
-
     def cpu_sample(self, oracle, target_s):
         import numpy as np
 
@@ -740,6 +881,20 @@ class ReduceWorkload(Workload):
                           + ("threaded f32 partial sums" if self.op == "dot" else "single-thread loop")}
 
 
+def mlp_weight(i, fi, fo):
+    """Layer i's weights, normal(0, 1/sqrt(fan_in)), on the host."""
+    import torch
+
+    return host_tensor((fi, fo), TID["W"] + i, torch.float32, "normal", std=1.0 / fi ** 0.5)
+
+
+def mlp_bias(i, fo):
+    """Layer i's bias vector, normal(0, 0.01), on the host."""
+    import torch
+
+    return host_tensor((fo,), TID["bias"], torch.float32, "normal", std=0.01, chunk=i)
+
+
 class MlpWorkload(Workload):
     """Resident-weight fp32 MLP forward: 4 x (sgemm + saxpy bias), batch 4096."""
 
@@ -749,16 +904,16 @@ class MlpWorkload(Workload):
         import b2blas
 
         self.h, self.world = h, world
+        self.name, self.args = "mlp", args
         self.dims = [1024, 4096, 4096, 4096, 1024]
         self.batch = 4096
         dev = torch.device("cuda", torch.cuda.current_device())
-        g = torch.Generator(device=dev).manual_seed(42 + rank)
-        self.X = torch.rand(self.batch, self.dims[0], device=dev, generator=g) * 2 - 1
+        self.X = host_tensor((self.batch, self.dims[0]), TID["x"], torch.float32).to(dev)
         self.W, self.bias, self.Z = [], [], []
         for i in range(4):
             fi, fo = self.dims[i], self.dims[i + 1]
-            self.W.append(torch.randn(fi, fo, device=dev, generator=g) / fi ** 0.5)
-            b = torch.randn(fo, device=dev, generator=g) * 0.01
+            self.W.append(mlp_weight(i, fi, fo).to(dev))
+            b = mlp_bias(i, fo).to(dev)
             self.bias.append(b.repeat(self.batch, 1).contiguous())  # pre-broadcast, as the example does
             self.Z.append(torch.empty(self.batch, fo, device=dev))
         wrap = lambda t: b2blas.DeviceBuffer.from_ptr(h, t.data_ptr(), t.numel(), "float32", owner=t)  # noqa
@@ -858,16 +1013,6 @@ class MlpWorkload(Workload):
 
         return [("sgemm_tiled + saxpy (mlp forward)", forward)]
 
-    def config(self):
-        how = ("fused sgemm+bias+ReLU epilogue" if self.fused else "sgemm + saxpy bias") + \
-            (", 3xTF32" if self.algo == __import__("b2blas").Algo.Tf32x3 else "")
-        return {"workload": f"mlp forward 1024-4096-4096-4096-1024, batch 4096, {how}"
-                            + (", two half-batch streams" if self.streams == 2 else "")
-                            + (", one replica per GPU" if self.world > 1 else ""),
-                "layers": self.dims, "batch": self.batch, "streams": self.streams,
-                "parallelism": f"replicas x{self.world}",
-                "l2": "weights + activations larger than L2: no flush needed"}
-
     def close(self):
         if self.streams == 2:
             import torch
@@ -898,18 +1043,8 @@ class MlpWorkload(Workload):
 
 
 def make_workload(name, h, rank, world, args):
-    def dims(d):
-        return (args.m or d, args.n or d, args.k or d)
-
-    if name == "hgemm":
-        m, n, k = dims(8192)
-        return GemmWorkload(h, rank, world, args, "hgemm", m, n, k, 1.0, 0.0, weak=True)
-    if name == "sgemm":
-        m, n, k = dims(8192)
-        return GemmWorkload(h, rank, world, args, "sgemm", m, n, k, 1.5, 0.5, weak=False)
-    if name == "dgemm":
-        m, n, k = dims(4096)
-        return GemmWorkload(h, rank, world, args, "dgemm", m, n, k, 1.5, 0.5, weak=False)
+    if name in GEMM_KINDS:
+        return GemmWorkload(h, rank, world, args, name)
     if name == "batched":
         return BatchedWorkload(h, rank, world, args)
     if name in ("sgemv", "dgemv", "hgemv"):
@@ -923,8 +1058,11 @@ def make_workload(name, h, rank, world, args):
 
 # ----------------------------------------------------------------- peaks
 
-def roofline_peak(w, peaks, handle_info):
-    """(peak value, unit, source) for the workload's dominant kernel."""
+def roofline_peak(w, peaks, handle_info, mhz=None):
+    """(peak value, unit, source) for the workload's dominant kernel.  The
+    FP32 / FP64 pipe peaks are computed from the SM count and a clock: `mhz`
+    (the median SM clock sampled during the timed region) when given, else
+    the maximum SM clock."""
     if w.bound == "tensor":
         return peaks["bf16_tflops"], "TFLOP/s", \
             f"dense f16/bf16 tensor, cuBLAS bf16 burst, {peaks['_source']}"
@@ -936,53 +1074,63 @@ def roofline_peak(w, peaks, handle_info):
     if w.bound == "hbm":
         return peaks["hbm_gbs"], "GB/s", f"HBM copy bandwidth, {peaks['_source']}"
     sms = handle_info["sm_count"]
-    mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    sampled = mhz is not None
+    mhz = float(mhz) if sampled else float(peaks.get("sm_max_mhz", 1965.0))
     lanes = 64 if w.dtype == "f64" else 128
     what = "FP64 (DMMA = DFMA rate)" if w.bound == "fp64" else "FP32 FFMA"
     return sms * lanes * 2 * mhz * 1e6 / 1e12, "TFLOP/s", \
-        f"computed {what} peak: {sms} SMs x {lanes} FMA/clk x 2 x {mhz:.0f} MHz (no measured figure in MEASURED_PEAKS.json)"
+        (f"computed {what} peak: {sms} SMs x {lanes} FMA/clk x 2 x {mhz:.0f} MHz "
+         + ("(median SM clock sampled during the timed region)" if sampled else "(maximum SM clock)")
+         + "; no measured figure for this pipe in MEASURED_PEAKS.json")
 
 
 # ------------------------------------------------------------ reference
 
 def run_reference(args, rank, world):
     """The reference arm: the CPU restatement of the reference's algorithm
-    (the oracle's host loops), rank 0 only, a bounded sample per step."""
+    (the oracle's host loops), rank 0 only, a bounded sample per step, on
+    the same seeded inputs (host_tensor) and with the same config record as
+    the library arm at this world size."""
     if rank != 0:
         return 0
     import numpy as np
+    import torch
 
     from oracle import oracle
 
     oracle.set_num_threads(os.cpu_count() or 1)
     nt = oracle.num_threads()
-    rng = np.random.default_rng(42)
     wl = args.workload
+    cfg = workload_config(wl, args, world)
     per_step = 1.5  # seconds of CPU work per step
-    if wl in ("hgemm", "sgemm", "dgemm"):
-        m, n, k = (8192, 8192, 8192) if wl != "dgemm" else (4096, 4096, 4096)
-        alpha, beta = (1.0, 0.0) if wl == "hgemm" else (1.5, 0.5)
+    if wl in GEMM_KINDS:
+        m, n, k = cfg["m"], cfg["n"], cfg["k"]
+        alpha, beta = GEMM_ALPHA_BETA[wl]
+        tdt = {"hgemm": torch.float16, "sgemm": torch.float32, "dgemm": torch.float64}[wl]
+        dist = "normal" if wl == "hgemm" else "uniform"
+        # The whole problem's B (weak: rank 0's panel, the others' are drawn
+        # the same way); A and C are read by row sample.
+        weak = cfg.get("scaling") == "weak" and world > 1
+        nb = n // world if weak else n
+        Afull = host_tensor((m, k), TID["A"], tdt, dist).numpy()
+        B = np.ascontiguousarray(host_tensor((k, nb), TID["B"], tdt, dist).numpy()).reshape(-1)
+        Cfull = host_tensor((m, nb), TID["C"], tdt, dist).numpy() if beta else np.zeros((m, nb), Afull.dtype)
         if wl == "hgemm":
-            B = (rng.standard_normal(k * n, dtype=np.float32) * 0.1).astype(np.float16).view(np.uint16)
-        else:
-            B = (rng.random(k * n) * 2 - 1).astype(np.float32 if wl == "sgemm" else np.float64)
+            Afull, B, Cfull = Afull.view(np.uint16), B.view(np.uint16), Cfull.view(np.uint16)
+        n = nb
 
         def run(rows):
+            A = np.ascontiguousarray(Afull[:rows]).reshape(-1)
+            C = np.ascontiguousarray(Cfull[:rows]).reshape(-1)
             if wl == "hgemm":
-                A = (rng.standard_normal(rows * k, dtype=np.float32) * 0.1).astype(np.float16).view(np.uint16)
-                C = np.zeros(rows * n, np.uint16)
                 bf, acc = np.empty(k * n, np.float32), np.empty(rows * n, np.float32)
                 t0 = time.perf_counter()
                 oracle.cpu_hgemm_rows(rows, n, k, alpha, A, B, beta, C, bf, acc)
             elif wl == "sgemm":
-                A = (rng.random(rows * k) * 2 - 1).astype(np.float32)
-                C = (rng.random(rows * n) * 2 - 1).astype(np.float32)
                 acc = np.empty(rows * n, np.float32)
                 t0 = time.perf_counter()
                 oracle.cpu_sgemm_rows(rows, n, k, alpha, A, B, beta, C, acc)
             else:
-                A = rng.random(rows * k) * 2 - 1
-                C = rng.random(rows * n) * 2 - 1
                 acc = np.empty(rows * n)
                 t0 = time.perf_counter()
                 oracle.cpu_dgemm_rows(rows, n, k, alpha, A, B, beta, C, acc)
@@ -993,75 +1141,68 @@ def run_reference(args, rank, world):
         rows = min(rows, m)
         unit = "TFLOP/s"
         sample = f"{rows} of {m} rows of C per step ({rows}x{n}x{k}), i-k-j host loop, {nt} threads"
-        cfg = {"workload": f"{wl} {m}x{n}x{k}", "m": m, "n": n, "k": k, "alpha": alpha, "beta": beta}
         step = lambda: run(rows)  # noqa: E731
         scale = 1e12
         dtype = {"hgemm": "f16", "sgemm": "f32", "dgemm": "f64"}[wl]
     elif wl == "batched":
         m = 256
-        A = (rng.random(m * m) * 2 - 1).astype(np.float32)
-        B = (rng.random(m * m) * 2 - 1).astype(np.float32)
+        A = batched_inputs(TID["A"], 0, BATCH_CHUNK, m).numpy()
+        B = batched_inputs(TID["B"], 0, BATCH_CHUNK, m).numpy()
         C = np.zeros(m * m, np.float32)
         acc = np.empty(m * m, np.float32)
+        state = {"i": 0}
 
         def run1():
+            i = state["i"] % BATCH_CHUNK
+            state["i"] += 1
+            a, b = np.ascontiguousarray(A[i]).reshape(-1), np.ascontiguousarray(B[i]).reshape(-1)
             t0 = time.perf_counter()
-            oracle.cpu_sgemm_rows(m, m, m, 1.0, A, B, 0.0, C, acc)
+            oracle.cpu_sgemm_rows(m, m, m, 1.0, a, b, 0.0, C, acc)
             return time.perf_counter() - t0
 
-        nb = max(1, int(per_step / max(run1(), 1e-9)))
+        nb = max(1, min(BATCH_CHUNK, int(per_step / max(run1(), 1e-9))))
 
         def step():
+            state["i"] = 0
             t = sum(run1() for _ in range(nb))
             return t, 2.0 * nb * m ** 3
 
         unit, scale, dtype = "TFLOP/s", 1e12, "f32"
-        sample = f"{nb} of the 4096 256^3 batches per step, i-k-j host loop, {nt} threads"
-        cfg = {"workload": "strided-batched sgemm 4096 x 256^3", "batch": 4096, "m": m, "n": m, "k": m}
-    elif wl == "sgemv":
+        sample = f"the first {nb} of the 4096 256^3 batches per step, i-k-j host loop, {nt} threads"
+    elif wl in ("sgemv", "dgemv", "hgemv"):
         n = 16384
-        rows = 4096
-        A = (rng.random(rows * n) * 2 - 1).astype(np.float32)
-        x = (rng.random(n) * 2 - 1).astype(np.float32)
-        y = np.zeros(rows, np.float32)
-
-        def step():
-            t0 = time.perf_counter()
-            oracle.cpu_sgemv_rows(rows, n, 1.0, A, x, 0.0, y)
-            return time.perf_counter() - t0, 4.0 * (rows * n + n + rows)
-
-        unit, scale, dtype = "GB/s", 1e9, "f32"
-        sample = f"{rows} of 16384 rows per step, row loop, {nt} threads"
-        cfg = {"workload": "sgemv 16384x16384 N", "m": 16384, "n": n}
-    elif wl in ("dgemv", "hgemv"):
-        n = 16384
-        rows = 2048
-        if wl == "dgemv":
-            A = rng.random(rows * n) * 2 - 1
-            x = rng.random(n) * 2 - 1
-            y = np.zeros(rows)
-        else:
-            A = (rng.random(rows * n, dtype=np.float32) * 2 - 1).astype(np.float16).view(np.uint16)
-            x = (rng.random(n, dtype=np.float32) * 2 - 1).astype(np.float16).view(np.uint16)
+        rows = 4096 if wl == "sgemv" else 2048
+        tdt = {"s": torch.float32, "d": torch.float64, "h": torch.float16}[wl[0]]
+        trans = 1 if args.trans else 0
+        Afull = host_tensor((16384, n), TID["A"], tdt).numpy()
+        x = host_tensor((n,), TID["x"], tdt).numpy()
+        # N: the first rows of A; T: y_j = sum_i A[i][j] x[i] over the first
+        # columns, i.e. the same row loop over rows of A^T
+        A = np.ascontiguousarray(Afull[:, :rows].T if trans else Afull[:rows]).reshape(-1)
+        if wl == "hgemv":
+            A, x = A.view(np.uint16), x.view(np.uint16)
             y = np.zeros(rows, np.uint16)
             xf = np.empty(n, np.float32)
-        es = 8 if wl == "dgemv" else 2
+        else:
+            y = np.zeros(rows, A.dtype)
+        es = {"s": 4, "d": 8, "h": 2}[wl[0]]
 
         def step():
             t0 = time.perf_counter()
-            if wl == "dgemv":
+            if wl == "sgemv":
+                oracle.cpu_sgemv_rows(rows, n, 1.0, A, x, 0.0, y)
+            elif wl == "dgemv":
                 oracle.cpu_dgemv_rows(rows, n, 1.0, A, x, 0.0, y)
             else:
                 oracle.cpu_hgemv_rows(rows, n, 1.0, A, x, 0.0, y, xf)
             return time.perf_counter() - t0, float(es) * (rows * n + n + rows)
 
-        unit, scale, dtype = "GB/s", 1e9, "f64" if wl == "dgemv" else "f16"
+        unit, scale, dtype = "GB/s", 1e9, {"s": "f32", "d": "f64", "h": "f16"}[wl[0]]
         sample = f"{rows} of 16384 rows per step, row loop, {nt} threads"
-        cfg = {"workload": f"{wl} 16384x16384 N", "m": 16384, "n": n}
     elif wl == "reduce":
-        n = 1 << 26
-        x = (rng.random(n, dtype=np.float32) * 2 - 1)
-        y = (rng.random(n, dtype=np.float32) * 2 - 1)
+        n = min(cfg["n"], 1 << 26)
+        x = host_tensor((cfg["n"],), TID["x"], torch.float32)[:n].numpy()
+        y = host_tensor((cfg["n"],), TID["y"], torch.float32)[:n].numpy() if args.op == "dot" else x
         op = args.op
         vec = 2 if op == "dot" else 1
 
@@ -1080,27 +1221,31 @@ def run_reference(args, rank, world):
             nt = 1
         sample = (f"first {n} elements per step, "
                   + (f"threaded f32 partial sums, {nt} threads" if op == "dot" else "the reference's 32-lane loop, 1 thread"))
-        cfg = {"workload": f"s{op} n={1 << 28}", "n": 1 << 28}
     else:
         dims = [1024, 4096, 4096, 4096, 1024]
-        Ws = [(rng.standard_normal(dims[i] * dims[i + 1], dtype=np.float32) / dims[i] ** 0.5) for i in range(4)]
+        Ws = [mlp_weight(i, dims[i], dims[i + 1]).numpy().reshape(-1) for i in range(4)]
+        bs = [mlp_bias(i, dims[i + 1]).numpy() for i in range(4)]
         rows = nt * 4
+        X = host_tensor((4096, dims[0]), TID["x"], torch.float32).numpy()
+        state = {"r": 0}
 
         def step():
-            inp = (rng.random(rows * dims[0]) * 2 - 1).astype(np.float32)
+            r0 = state["r"] % (4096 // rows) * rows
+            state["r"] += 1
+            inp = np.ascontiguousarray(X[r0:r0 + rows]).reshape(-1)
             t0 = time.perf_counter()
             fl = 0.0
             for i in range(4):
                 z = np.zeros(rows * dims[i + 1], np.float32)
                 acc = np.empty_like(z)
                 oracle.cpu_sgemm_rows(rows, dims[i + 1], dims[i], 1.0, inp, Ws[i], 0.0, z, acc)
+                z += np.tile(bs[i], rows)  # the example's saxpy of the pre-broadcast bias
                 fl += 2.0 * rows * dims[i] * dims[i + 1]
                 inp = z
             return time.perf_counter() - t0, fl
 
         unit, scale, dtype = "TFLOP/s", 1e12, "f32"
-        sample = f"{rows} rows of the batch-4096 forward per step, i-k-j host loop, {nt} threads"
-        cfg = {"workload": "mlp forward 1024-4096-4096-4096-1024, batch 4096", "layers": dims, "batch": 4096}
+        sample = f"{rows} rows of the batch-4096 forward per step (sgemm + saxpy bias), i-k-j host loop, {nt} threads"
 
     for _ in range(args.warmup):
         step()
@@ -1112,8 +1257,8 @@ def run_reference(args, rank, world):
     value = uu / tt / scale
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": tt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
-            "data": "synthetic (seeded)", "config": cfg,
+            "higher_is_better": True, "scaling": cfg["scaling"], "vs_baseline": None, "dtype": dtype,
+            "data": DATA, "config": cfg,
             "cpu_baseline": {"value": value, "unit": unit, "cores": nt, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference = CPU restatement of cublas-rs's kernels (Rust/cuda-oxide cannot be built here)"}
@@ -1141,7 +1286,7 @@ def run_e2e(w, h, stream, steps, world, dist, barrier, host_alloc="b2b"):
     t = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    value = w.scale(w.units_per_step() * world * steps / (float(t.item()) / 1e3))
+    value = w.scale(w.total_units_per_step() * steps / (float(t.item()) / 1e3))
     return {"value": value, "unit": w.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": steps, "api": "host-slice (_simple) calls on page-locked host buffers",
             "host_alloc": "b2b_host_alloc (cudaHostAlloc)" if host_alloc == "b2b" else "torch pin_memory"}
@@ -1186,6 +1331,100 @@ def time_ref_kernels(w, stream, budget_ms=2500.0, max_launches=10):
             "best_kernel": best["kernel"], "best_value": best["value"]}
 
 
+def timed_region(w, stream, steps, dist, barrier, local):
+    """K steps of `w` between a barrier + synchronize on both sides, CUDA
+    events on the launch stream, NVML clocks sampled meanwhile.  Returns
+    (this rank's ms, max-over-ranks ms, clock summary)."""
+    import torch
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier()
+    with sampler:
+        start.record(stream)
+        for _ in range(steps):
+            w.step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    w.h.synchronize()  # raises if a bounded device wait gave up
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    barrier()
+    return ms, ms_max, sampler.summary()
+
+
+def secondary_names(args, world):
+    """The metric's other configurations, measured after the headline one."""
+    if args.no_secondary or args.workload != "hgemm" or args.m or args.n or args.k:
+        return []
+    if world == 1:
+        return ["sgemm", "sgemv", "batched", "dgemm"]
+    return ["batched", "hgemm-weak"]
+
+
+def run_secondary(names, h, stream, rank, world, dist, barrier, local, args, peaks, info):
+    """Each secondary configuration in its own timed region: 3 warm-up steps,
+    then at least --steps steps and at least ~50 ms of device time."""
+    import copy
+    import math
+
+    import torch
+
+    out = []
+    for name in names:
+        sa = copy.copy(args)
+        sa.trans = sa.tf32x3 = sa.gather = sa.gather_nccl = sa.gather_multicast = False
+        sa.no_gather, sa.weak = True, name == "hgemm-weak"
+        sa.m = sa.n = sa.k = None
+        wname = "hgemm" if name == "hgemm-weak" else name
+        sa.workload = wname
+        w = make_workload(wname, h, rank, world, sa)
+        torch.cuda.synchronize()
+        for _ in range(3):
+            w.step()
+        barrier()
+        # one step's duration sets the count (the same on every rank)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        w.step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        est = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(est, op=dist.ReduceOp.MAX)
+        steps = int(min(4000, max(args.steps, math.ceil(50.0 / max(float(est.item()), 1e-3)))))
+        ms, ms_max, clocks = timed_region(w, stream, steps, dist, barrier, local)
+        value = w.scale(w.total_units_per_step() * steps / (ms_max / 1e3))
+        per_launch = ms / steps
+        achieved = w.scale(w.units_per_step() / (per_launch / 1e3))
+        mhz = clocks.get("sm_mhz") if w.bound in ("fma", "fp64") else None
+        peak, punit, psrc = roofline_peak(w, peaks, info, mhz)
+        rec = {"name": name, "config": w.config(), "metric": f"{w.unit} ({w.dtype})", "value": value,
+               "unit": w.unit, "dtype": w.dtype, "steps": steps, "warmup": 3, "ms_per_step": ms_max / steps,
+               "scaling": w.scaling, "kernel": w.kernel, "gpu_launches": w.launches_per_step * steps,
+               "roofline": {"bound": {"hbm": "hbm", "tensor": "tensor", "fp64": "fp64"}.get(w.bound, "fma"),
+                            "achieved": achieved, "peak": peak, "unit": punit, "frac": achieved / peak,
+                            "peak_source": psrc, "ms_per_launch": per_launch,
+                            "algorithmic_units_per_launch": w.units_per_step(),
+                            "traffic": None if world > 1 and name != "batched" else load_traffic().get(wname)},
+               "clocks": clocks}
+        if w.bound in ("fma", "fp64"):
+            pmax, _, _ = roofline_peak(w, peaks, info)
+            rec["roofline"]["frac_at_max_clock"] = achieved / pmax
+        if world > 1 and name == "batched" and rec["roofline"]["traffic"]:
+            rec["roofline"]["traffic"] = rec["roofline"]["traffic"] * w.batch / w.total_batch
+        out.append(rec)
+        if hasattr(w, "close"):
+            w.close()
+        del w
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1197,11 +1436,16 @@ def main():
     ap.add_argument("--op", choices=["dot", "nrm2", "asum", "iamax"], default="dot", help="reduce: which reduction")
     ap.add_argument("--trans", action="store_true", help="sgemv: A^T x")
     ap.add_argument("--gather", action="store_true",
-                    help="column-sharded GEMMs: every rank ends each step with the full C (GEMM with the gather fused)")
+                    help="column-sharded GEMMs: every rank ends each step with the full C (GEMM with the gather "
+                         "fused; the default for HGEMM on N > 1 GPUs)")
     ap.add_argument("--gather-multicast", action="store_true",
                     help="as --gather, HGEMM stores through an NVLink multicast object (torch symmetric memory)")
     ap.add_argument("--gather-nccl", action="store_true",
                     help="as --gather, but GEMM into the panel + NCCL all-gather + re-layout kernel")
+    ap.add_argument("--no-gather", action="store_true", help="column-sharded HGEMM on N > 1 GPUs: keep the panels")
+    ap.add_argument("--weak", action="store_true",
+                    help="HGEMM on N GPUs: every rank its own 8192-column panel of an 8192 x 8192N x 8192 product")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the metric's other configurations")
     ap.add_argument("--tf32x3", action="store_true", help="sgemm/mlp: the opt-in 3xTF32 tensor-core kernel")
     ap.add_argument("--fused", action="store_true", help="mlp: bias (+ReLU) fused into the SGEMM epilogue")
     ap.add_argument("--mlp-streams", type=int, choices=[1, 2], default=2,
@@ -1235,11 +1479,6 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
-        # Keep stdout to the one JSON line: NCCL's version banner goes away,
-        # warnings still reach stderr.
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
-
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
 
@@ -1266,31 +1505,13 @@ def main():
     barrier()
     h.synchronize()
 
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
-    barrier()
-    with sampler:
-        start.record(stream)
-        for _ in range(args.steps):
-            w.step()
-        end.record(stream)
-        torch.cuda.synchronize()
-    h.synchronize()  # raises if a bounded device wait gave up
-    ms = start.elapsed_time(end)
-    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    barrier()
-
-    units_local = w.units_per_step() * args.steps
-    total_units = units_local * world
-    value = w.scale(total_units / (ms_max / 1e3))
+    ms, ms_max, clocks = timed_region(w, stream, args.steps, dist, barrier, local)
+    value = w.scale(w.total_units_per_step() * args.steps / (ms_max / 1e3))
 
     # dominant kernel roofline (per launch, this rank)
     peaks = load_peaks()
     info = h.device_info()
-    peak, punit, psrc = roofline_peak(w, peaks, info)
+    peak, punit, psrc = roofline_peak(w, peaks, info, clocks.get("sm_mhz") if w.bound in ("fma", "fp64") else None)
     per_launch_ms = ms / args.steps
     if isinstance(w, MlpWorkload):
         # time the GEMMs alone for the kernel figure
@@ -1305,12 +1526,8 @@ def main():
         e1.record(stream)
         torch.cuda.synchronize()
         per_launch_ms = e0.elapsed_time(e1) / args.steps
-        achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
-    elif isinstance(w, GemvWorkload) or (isinstance(w, GemmWorkload) and w.gather == "nccl"):
-        achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
-    else:
-        achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
-    traffic = load_traffic().get(args.workload)
+    achieved = w.scale(w.units_per_step() / (per_launch_ms / 1e3))
+    traffic = load_traffic().get(args.workload) if world == 1 and not (args.m or args.n or args.k) else None
     roof = {"bound": {"hbm": "hbm", "tensor": "tensor", "fp64": "tensor", "tf32x3": "tensor"}.get(w.bound, "fma"),
             "kernel": w.kernel, "achieved": achieved, "peak": peak, "unit": punit, "frac": achieved / peak,
             "peak_source": psrc, "traffic": traffic,
@@ -1326,8 +1543,9 @@ def main():
         nvl_bytes = (world - 1) * w.m * w.n * esz
         t_math = w.units_per_step() / (peak * 1e12) * 1e3 if punit == "TFLOP/s" else 0.0
         t_link = nvl_bytes / 770e9 * 1e3
-        roof["fused_collective"] = {"nvlink_bytes_per_step": nvl_bytes, "link_gbs": 770.0,
+        roof["fused_collective"] = {"gather": w.gather, "nvlink_bytes_per_step": nvl_bytes, "link_gbs": 770.0,
                                     "math_ms": t_math, "link_ms": t_link, "target_ms": max(t_math, t_link),
+                                    "limiter": "nvlink" if t_link > t_math else "math",
                                     "frac_of_target": max(t_math, t_link) / per_launch_ms}
 
     # end to end through the host-slice API
@@ -1349,18 +1567,28 @@ def main():
         cpu = {"value": s["value"], "unit": w.unit, "cores": s.get("threads", oracle.num_threads()), "kind": "port",
                "sample": s["sample"], "seconds": round(s["seconds"], 2)}
 
+    launches = w.launches_per_step * args.steps
+    config, scaling, wunit, wdtype = w.config(), w.scaling, w.unit, w.dtype
+    if hasattr(w, "close"):
+        w.close()
+    del w
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+    secondary = run_secondary(secondary_names(args, world), h, stream, rank, world, dist, barrier, local, args,
+                              peaks, info)
+
     if dist is not None:
         dist.barrier()
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": w.unit, "n_gpus": world, "steps": args.steps,
+        line = {"metric": METRIC, "value": value, "unit": wunit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-                "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype,
-                "data": "synthetic (seeded torch generators; normal(0,0.1)->f16 for HGEMM, uniform[-1,1) else)",
-                "config": w.config(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "reference_kernels": refk,
-                "gpu_launches": w.launches_per_step * args.steps, "clocks": sampler.summary()}
+                "scaling": scaling, "vs_baseline": None, "dtype": wdtype,
+                "data": DATA, "config": config, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "reference_kernels": refk, "gpu_launches": launches, "clocks": clocks}
+        if secondary:
+            line["secondary"] = secondary
         print(json.dumps(line), flush=True)
-    if hasattr(w, "close"):
-        w.close()
     h.set_stream(None)
     h.close()
     if dist is not None:

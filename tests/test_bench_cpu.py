@@ -58,3 +58,80 @@ def test_sgemm_kernels_per_call(monkeypatch):
     assert bench.sgemm_kernels_per_call(8192, 8192, 8192) == 1
     monkeypatch.setenv("B2B_SGEMM_VARIANT", "21")
     assert bench.sgemm_kernels_per_call(8192, 8192, 8192) == 2
+
+
+def _bench_args(argv):
+    sys.path.insert(0, ROOT)
+    import argparse
+
+    import bench
+
+    # the parser bench.main() builds, without running it
+    ns = argparse.Namespace(workload="hgemm", op="dot", trans=False, gather=False, gather_multicast=False,
+                            gather_nccl=False, no_gather=False, weak=False, no_secondary=False, tf32x3=False,
+                            fused=False, mlp_streams=2, m=None, n=None, k=None)
+    for a in argv:
+        k, _, v = a.partition("=")
+        setattr(ns, k, v if v else True)
+    return bench, ns
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_reference_arm_prints_the_library_config(world):
+    # The reference arm's config record is the one the library arm prints at
+    # the same world size (both come from workload_config).
+    bench, ns = _bench_args(["workload=batched"])
+    p = _run_bench(["--impl", "reference", "--workload", "batched", "--steps", "1", "--warmup", "3"],
+                   {"RANK": "0", "WORLD_SIZE": str(world), "LOCAL_RANK": "0"})
+    assert p.returncode == 0, p.stderr[-2000:]
+    d = json.loads(p.stdout.strip().splitlines()[-1])
+    assert d["config"] == bench.workload_config("batched", ns, world)
+    assert d["scaling"] == d["config"]["scaling"] == ("strong" if world > 1 else "weak")
+    assert d["data"] == bench.DATA
+
+
+def test_hgemm_config_at_n_gpus():
+    # One GPU: the 8192^3 problem, no gather.  N GPUs: the same fixed problem,
+    # 8192/N columns per GPU, C gathered by the fused kernel; --weak and
+    # --no-gather give the panel-only forms.
+    bench, ns = _bench_args([])
+    c1 = bench.workload_config("hgemm", ns, 1)
+    assert (c1["m"], c1["n"], c1["k"], c1["gather"], c1["scaling"]) == (8192, 8192, 8192, False, "weak")
+    c8 = bench.workload_config("hgemm", ns, 8)
+    assert (c8["n"], c8["n_per_gpu"], c8["gather"], c8["scaling"]) == (8192, 1024, "fused", "strong")
+    _, ns_w = _bench_args(["weak"])
+    cw = bench.workload_config("hgemm", ns_w, 8)
+    assert (cw["n"], cw["n_per_gpu"], cw["gather"], cw["scaling"]) == (65536, 8192, False, "weak")
+    _, ns_n = _bench_args(["no_gather"])
+    assert bench.workload_config("hgemm", ns_n, 4)["gather"] is False
+    _, ns_c = _bench_args(["gather_nccl"])
+    assert bench.workload_config("hgemm", ns_c, 2)["gather"] == "nccl"
+    # SGEMM / DGEMM gather only when asked
+    assert bench.workload_config("sgemm", ns, 8)["gather"] is False
+
+
+def test_secondary_configurations():
+    bench, ns = _bench_args([])
+    assert bench.secondary_names(ns, 1) == ["sgemm", "sgemv", "batched", "dgemm"]
+    assert bench.secondary_names(ns, 8) == ["batched", "hgemm-weak"]
+    _, ns2 = _bench_args(["no_secondary"])
+    assert bench.secondary_names(ns2, 1) == []
+    _, ns3 = _bench_args(["workload=sgemm"])
+    assert bench.secondary_names(ns3, 1) == []
+
+
+def test_seeded_inputs_are_shared_and_chunked():
+    import torch
+
+    bench, _ = _bench_args([])
+    a = bench.host_tensor((64, 32), bench.TID["A"], torch.float16, "normal")
+    b = bench.host_tensor((64, 32), bench.TID["A"], torch.float16, "normal")
+    assert torch.equal(a, b) and a.dtype == torch.float16
+    assert float(a.float().std()) == pytest.approx(0.1, rel=0.2)
+    u = bench.host_tensor((1 << 16,), bench.TID["B"], torch.float32)
+    assert float(u.min()) >= -1.0 and float(u.max()) < 1.0
+    assert not torch.equal(u[:2048].reshape(64, 32).half(), a)  # different tensor ids, different numbers
+    # a rank's batch range is the same numbers as that range of the whole
+    whole = bench.batched_inputs(bench.TID["A"], 0, 1024, 8)
+    part = bench.batched_inputs(bench.TID["A"], 300, 700, 8)
+    assert torch.equal(part, whole[300:700])

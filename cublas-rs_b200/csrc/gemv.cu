@@ -19,6 +19,7 @@
 //     that about 4 CTAs per SM are in flight.  The partials live in the
 //     handle's workspace (S * n floats).
 // beta == 0 does not read y.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -242,6 +243,27 @@ __global__ void sgemv_t_reduce_kernel(const float *__restrict__ partial, float *
     y[j] = v;
 }
 
+// Split-row plan of the transposed SGEMV, shared by b2b_sgemv and
+// b2b_sgemv_noalloc so both give the same bits: enough slices for ~4 CTAs per
+// SM, each slice at least 64 rows, at most 65535 slices.
+struct TSlicing {
+    int64_t col_blocks, slices, rows_per;
+};
+
+TSlicing sgemv_t_slicing(int sm_count, int64_t m, int64_t n) {
+    TSlicing p;
+    p.col_blocks = (n + 127) / 128;
+    const int64_t target = 4LL * sm_count;
+    int64_t slices = (target + p.col_blocks - 1) / p.col_blocks;
+    const int64_t max_slices = (m + 63) / 64;
+    if (slices > max_slices) slices = max_slices;
+    if (slices > 65535) slices = 65535;
+    if (slices < 1) slices = 1;
+    p.rows_per = (m + slices - 1) / slices;
+    p.slices = (m + p.rows_per - 1) / p.rows_per;
+    return p;
+}
+
 }  // namespace
 
 namespace b2b {
@@ -252,17 +274,9 @@ int launch_sgemv(b2b_handle *h, int trans, size_t m_, size_t n_, float alpha, co
     cudaError_t e;
     if (trans == B2B_OP_N) return launch_sgemv_n(h, A, x, y, m, n, alpha, beta);
     const bool vec_t = (n % 4 == 0) && aligned16(A);
-    const int64_t col_blocks = (n + 127) / 128;
+    const TSlicing plan = sgemv_t_slicing(h->sm_count, m, n);
+    const int64_t col_blocks = plan.col_blocks, slices = plan.slices, rows_per = plan.rows_per;
     if (col_blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemv: n too large");
-    // Enough slices for ~4 CTAs per SM, each slice at least 64 rows.
-    int64_t target = 4LL * h->sm_count;
-    int64_t slices = (target + col_blocks - 1) / col_blocks;
-    int64_t max_slices = (m + 63) / 64;
-    if (slices > max_slices) slices = max_slices;
-    if (slices > 65535) slices = 65535;
-    if (slices < 1) slices = 1;
-    int64_t rows_per = (m + slices - 1) / slices;
-    slices = (m + rows_per - 1) / rows_per;
     if (slices == 1) {
         dim3 grid((unsigned)col_blocks, 1);
         if (vec_t)
@@ -310,22 +324,59 @@ constexpr size_t kNoAllocScratchFloats = size_t(1) << 18;
 static __device__ __align__(256) float g_sgemv_noalloc_scratch[kNoAllocScratchFloats];
 
 // Host code cannot use the array's name as a device address, so the address
-// is looked up once per device (with that device current) and cached.
+// is looked up once per device (with that device current) and cached, keyed
+// by the context's unique id as well: after cudaDeviceReset the device gets
+// a new context, in which the array may sit elsewhere, and the next call
+// looks the address up again instead of using the old one.
 constexpr int kNoAllocMaxDevices = 64;
-float *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+struct NoAllocSlot {
+    unsigned long long ctx_id;
+    float *ptr;
+};
+NoAllocSlot g_noalloc[kNoAllocMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
+using PfnCtxGetCurrent = CUresult (*)(CUcontext *);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long *);
+
+// The unique id of the current context (cuCtxGetId, never reused within a
+// process), through the runtime's driver entry points.
+int current_context_id(unsigned long long *id) {
+    static PfnCtxGetCurrent get_current = nullptr;
+    static PfnCtxGetId get_id = nullptr;
+    if (!get_current || !get_id) {
+        void *p1 = nullptr, *p2 = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p1, 4000, cudaEnableDefault, &q1) != cudaSuccess ||
+            q1 != cudaDriverEntryPointSuccess ||
+            cudaGetDriverEntryPointByVersion("cuCtxGetId", &p2, 12000, cudaEnableDefault, &q2) != cudaSuccess ||
+            q2 != cudaDriverEntryPointSuccess)
+            return b2b::fail(B2B_ERR_CUDA, "b2b_sgemv_noalloc: cuCtxGetCurrent / cuCtxGetId not available");
+        get_current = reinterpret_cast<PfnCtxGetCurrent>(p1);
+        get_id = reinterpret_cast<PfnCtxGetId>(p2);
+    }
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, id) != CUDA_SUCCESS)
+        return b2b::fail(B2B_ERR_CUDA, "b2b_sgemv_noalloc: no current CUDA context");
+    return B2B_OK;
+}
+
+// Call with the handle's device current (DeviceGuard).
 int noalloc_scratch(int device, float **out) {
     if (device < 0 || device >= kNoAllocMaxDevices)
         return b2b::fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: device ordinal out of range");
+    unsigned long long ctx_id = 0;
+    if (int rc = current_context_id(&ctx_id)) return rc;
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_ptr[device]) {
+    NoAllocSlot &slot = g_noalloc[device];
+    if (!slot.ptr || slot.ctx_id != ctx_id) {
         void *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_sgemv_noalloc_scratch);
         if (e != cudaSuccess) return b2b::fail_cuda(e, "b2b_sgemv_noalloc: cudaGetSymbolAddress");
-        g_noalloc_ptr[device] = static_cast<float *>(p);
+        slot.ptr = static_cast<float *>(p);
+        slot.ctx_id = ctx_id;
     }
-    *out = g_noalloc_ptr[device];
+    *out = slot.ptr;
     return B2B_OK;
 }
 
@@ -346,15 +397,9 @@ extern "C" int b2b_sgemv_noalloc(b2b_handle *h, int trans, size_t m_, size_t n_,
     if (trans == B2B_OP_N) return launch_sgemv_n(h, A, x, y, m, n, alpha, beta);  // needs no scratch
     // T: the same slicing as b2b_sgemv, so both give the same bits.
     const bool vec_t = (n % 4 == 0) && aligned16(A);
-    const int64_t col_blocks = (n + 127) / 128;
+    const TSlicing plan = sgemv_t_slicing(h->sm_count, m, n);
+    const int64_t col_blocks = plan.col_blocks, slices = plan.slices, rows_per = plan.rows_per;
     if (col_blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: n too large");
-    int64_t slices = (4LL * h->sm_count + col_blocks - 1) / col_blocks;
-    const int64_t max_slices = (m + 63) / 64;
-    if (slices > max_slices) slices = max_slices;
-    if (slices > 65535) slices = 65535;
-    if (slices < 1) slices = 1;
-    const int64_t rows_per = (m + slices - 1) / slices;
-    slices = (m + rows_per - 1) / rows_per;
     if (slices == 1) {
         dim3 grid((unsigned)col_blocks, 1);
         if (vec_t)
@@ -364,11 +409,17 @@ extern "C" int b2b_sgemv_noalloc(b2b_handle *h, int trans, size_t m_, size_t n_,
         e = cudaGetLastError();
         return e == cudaSuccess ? B2B_OK : fail_cuda(e, "b2b_sgemv_noalloc: T launch");
     }
-    if (static_cast<uint64_t>(slices) * static_cast<uint64_t>(n) > kNoAllocScratchFloats)
+    // The limit is the array's size, or a lower one the handle was created
+    // with (B2B_NOALLOC_SCRATCH_FLOATS; lets tests reach this rejection,
+    // which no shape reaches on a 148-SM GPU: slices x n stays below
+    // 4 * 148 * 128 + n <= 151,424 floats whenever slices > 1).
+    const size_t limit = (h->noalloc_limit_floats > 0 && h->noalloc_limit_floats < kNoAllocScratchFloats)
+                             ? h->noalloc_limit_floats
+                             : kNoAllocScratchFloats;
+    if (static_cast<uint64_t>(slices) * static_cast<uint64_t>(n) > limit)
         return fail(B2B_ERR_INVALID_ARG, "b2b_sgemv_noalloc: this shape needs " + std::to_string(slices) + " x " +
                                              std::to_string(n) + " partial sums, more than the " +
-                                             std::to_string(kNoAllocScratchFloats) +
-                                             "-float fixed scratch holds; use b2b_sgemv");
+                                             std::to_string(limit) + "-float fixed scratch holds; use b2b_sgemv");
     float *partial = nullptr;
     if (int rc = noalloc_scratch(h->device, &partial)) return rc;
     dim3 grid((unsigned)col_blocks, (unsigned)slices);

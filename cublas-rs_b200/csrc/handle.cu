@@ -184,6 +184,7 @@ int b2b_create(int device, b2b_handle **out) {
     const char *single = getenv("B2B_HGEMM_SINGLE_CTA");
     h->force_single_cta = single && single[0] == '1';
     if (const char *v = getenv("B2B_SGEMM_VARIANT")) h->sgemm_variant = atoi(v);
+    if (const char *v = getenv("B2B_SGEMM_GROUP_M")) h->sgemm_group_m = atoi(v);
     if (const char *v = getenv("B2B_HGEMM_VARIANT")) h->hgemm_variant = atoi(v);
     if (const char *v = getenv("B2B_HGEMM_GROUP_M")) h->hgemm_group_m = atoi(v);
     if (const char *v = getenv("B2B_GEMV_SEG_KB")) {
@@ -191,6 +192,7 @@ int b2b_create(int device, b2b_handle **out) {
         if (kb > 0) h->gemv_seg_bytes = static_cast<int64_t>(kb) * 1024;
     }
     if (const char *v = getenv("B2B_DGEMM_VARIANT")) h->dgemm_variant = atoi(v);
+    if (const char *v = getenv("B2B_NOALLOC_SCRATCH_FLOATS")) h->noalloc_limit_floats = strtoull(v, nullptr, 10);
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
     *out = h;
     return B2B_OK;

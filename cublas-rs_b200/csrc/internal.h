@@ -63,11 +63,13 @@ struct b2b_handle {
     bool force_single_cta = false;
     // SGEMM kernel configuration (B2B_SGEMM_VARIANT; 0 = the default).
     int sgemm_variant = 0;
+    int sgemm_group_m = 0;              // TMA-fed SGEMM raster group override (B2B_SGEMM_GROUP_M; 0 = default)
     int hgemm_variant = 0;              // 0 auto, 1 single CTA, 2 pair 256x256, 3 pair 256x512
     int hgemm_group_m = 0;              // pair kernels' raster group override (0 = default)
     int64_t gemv_seg_bytes = 16384;     // GEMV-N row segment size (B2B_GEMV_SEG_KB)
     // DGEMM kernel configuration (B2B_DGEMM_VARIANT; 0 = the default).
     int dgemm_variant = 0;
+    size_t noalloc_limit_floats = 0;    // b2b_sgemv_noalloc: lower scratch limit (0 = the whole array)
 };
 
 namespace b2b {

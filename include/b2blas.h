@@ -211,12 +211,18 @@ B2B_API int b2b_sgemv_simple(b2b_handle *h, int algo, int trans, size_t m, size_
  * loads it until the process exits).  Same arguments and results as b2b_sgemv.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress, with that device current); make that first call
- *     before any stream capture.
- *   - All calls share the array, which keeps the last call's contents;
- *     nothing in it needs clearing (every partial is written before it is
- *     read), but calls that overlap on the GPU race on it.
+ *     before any stream capture.  The address is cached per device and
+ *     context: after cudaDeviceReset the next call looks it up again (so
+ *     make one call before capturing in the new context too).
+ *   - All calls, across handles and streams, share the one array, which
+ *     keeps the last call's contents; nothing in it needs clearing (every
+ *     partial is written before it is read), but calls that may overlap on
+ *     the GPU race on it and must be serialised by the caller.
  *   - A shape whose partial sums do not fit the array is rejected with
- *     B2B_ERR_INVALID_ARG and a message naming the sizes. */
+ *     B2B_ERR_INVALID_ARG, before any launch, and a message naming the
+ *     sizes (on a 148-SM GPU every shape fits; a handle created with
+ *     B2B_NOALLOC_SCRATCH_FLOATS=<n> in the environment uses n as a lower
+ *     limit). */
 B2B_API int b2b_sgemv_noalloc(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A,
                               const float *x, float beta, float *y);
 

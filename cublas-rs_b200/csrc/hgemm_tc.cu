@@ -29,8 +29,10 @@
 //   * No TMA multicast: each CTA loads its own tiles from this GPU's memory.
 //
 // Shapes that TMA cannot describe (K or N not a multiple of 8, or operands
-// not 16-byte aligned) run hgemm_simt_kernel below, a plain CUDA-core kernel
-// with the same arithmetic.
+// not 16-byte aligned) are copied into zero-padded workspace and run on the
+// tensor cores when the GEMM is large enough to pay for the copies
+// (launch_hgemm); small ones run hgemm_simt_kernel below, a plain CUDA-core
+// kernel with the same arithmetic.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -411,12 +413,20 @@ struct Cfg {
 constexpr int THREADS = 192;
 }  // namespace hg2
 
-template <int NSPLIT>
+// HALVES (256 x 512 tiles only): the accumulator is released in two
+// 256-column halves.  The epilogue arrives on tempty[0] once it has read
+// columns 0..255 and on tempty[1] after columns 256..511; the MMA issuer
+// starts the next tile as soon as half 0 is free, issuing the hs = 0 MMAs of
+// the first STAGES k-blocks (the stages the producer loaded meanwhile), then
+// waits for half 1 and issues those k-blocks' hs = 1 MMAs before going on as
+// usual.  Each column's k order is unchanged, so the bits are the same.
+template <int NSPLIT, bool HALVES>
 __global__ void __launch_bounds__(hg2::THREADS, 1)
     hgemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, HgemmArgs args) {
     using namespace sm100;
     using Cf = hg2::Cfg<NSPLIT>;
+    static_assert(!HALVES || NSPLIT == 2, "accumulator halves need the 256 x 512 tile");
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -549,7 +559,54 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cf::ACC_COLS);
-                for (int kb = 0; kb < kblocks; ++kb) {
+                int kb0 = 0;
+                if constexpr (HALVES) {
+                    // Half 0 is free: the hs = 0 MMAs of the first P k-blocks,
+                    // holding their stages.
+                    const int P = kblocks < Cf::STAGES ? kblocks : Cf::STAGES;
+                    const int stage0 = stage;
+                    for (int kb = 0; kb < P; ++kb) {
+                        if (!mbar_wait(&full[stage], phase, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x13,
+                                       args.wait_ns)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_base = smem_u32(sA + stage * Cf::A_BYTES);
+                        const uint32_t b_base = smem_u32(sB + stage * Cf::B_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < Cf::BK / 16; ++kk)
+                            umma_f16_pair(d_tmem, sdesc_sw128(a_base + kk * 32, 16, 1024),
+                                          sdesc_sw128(b_base + kk * 2048, Cf::B_BOX_BYTES, 1024), Cf::IDESC,
+                                          (kb | kk) != 0 ? 1u : 0u);
+                        issued_any = true;
+                        if (++stage == Cf::STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    // Half 1: its MMAs of those k-blocks, then the stages go back.
+                    if (!mbar_wait(&tempty[1], acc_phase ^ 1u, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x15,
+                                   args.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int kb = 0; kb < P; ++kb) {
+                        const int s = (stage0 + kb) % Cf::STAGES;
+                        const uint32_t a_base = smem_u32(sA + s * Cf::A_BYTES);
+                        const uint32_t b_base = smem_u32(sB + s * Cf::B_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < Cf::BK / 16; ++kk)
+                            umma_f16_pair(d_tmem + 256u, sdesc_sw128(a_base + kk * 32, 16, 1024),
+                                          sdesc_sw128(b_base + Cf::B_SPLIT_BYTES + kk * 2048, Cf::B_BOX_BYTES, 1024),
+                                          Cf::IDESC, (kb | kk) != 0 ? 1u : 0u);
+                        umma_commit_pair(&empty[s], 0x3);
+                    }
+                    kb0 = P;
+                }
+                for (int kb = kb0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x13,
                                    args.wait_ns)) {
                         ok = false;
@@ -622,14 +679,18 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                     tmem_ld_32x32b_x32(taddr, r0);
                     tmem_ld_32x32b_x32(taddr + 32, r1);
                     tmem_ld_wait();
-                    if (c == Cf::BN / 64 - 1) {
+                    if (c == Cf::BN / 64 - 1 || (HALVES && c == Cf::BN / 128 - 1)) {
+                        // this warp has read the whole accumulator (or, with
+                        // HALVES, its first half): one arrival per warp on the
+                        // leader's barrier
+                        uint64_t *bar = HALVES ? &tempty[c == Cf::BN / 64 - 1 ? 1 : 0] : &tempty[acc];
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) {
                             if (leader)
-                                mbar_arrive(&tempty[acc]);
+                                mbar_arrive(bar);
                             else
-                                mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+                                mbar_arrive_cluster(mapa_shared(smem_u32(bar), 0));
                         }
                     }
                     const int col0 = tn * Cf::BN + c * 64;
@@ -707,16 +768,18 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                 __syncwarp();
                 tmem_ld_32x32b_x32(tmem_base + lane_off + static_cast<uint32_t>(acc * Cf::ACC_COLS + c * 32), r);
                 tmem_ld_wait();
-                if (c == Cf::BN / 32 - 1) {
-                    // This warp's share of the accumulator is in registers:
-                    // one arrival per warp on the leader's barrier.
+                if (c == Cf::BN / 32 - 1 || (HALVES && c == Cf::BN / 64 - 1)) {
+                    // This warp's share of the accumulator (with HALVES, of
+                    // its first half) is in registers: one arrival per warp
+                    // on the leader's barrier.
+                    uint64_t *bar = HALVES ? &tempty[c == Cf::BN / 32 - 1 ? 1 : 0] : &tempty[acc];
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
                         if (leader)
-                            mbar_arrive(&tempty[acc]);
+                            mbar_arrive(bar);
                         else
-                            mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+                            mbar_arrive_cluster(mapa_shared(smem_u32(bar), 0));
                     }
                 }
                 const int col0 = tn * Cf::BN + c * 32;
@@ -814,38 +877,39 @@ namespace {
 
 struct DeviceLaunchState {
     bool attr1 = false;
-    bool attr2[2] = {false, false};
-    int max_pairs[2] = {0, 0};  // co-resident CTA pairs of hgemm_tc2_kernel<1>, <2>
+    bool attr2[3] = {false, false, false};
+    int max_pairs[3] = {0, 0, 0};  // co-resident CTA pairs of hgemm_tc2_kernel<1,0>, <2,0>, <2,1>
 };
 DeviceLaunchState g_hgemm_state[64];
 std::mutex g_hgemm_mu;
 
-template <int NSPLIT>
+template <int NSPLIT, bool HALVES>
 int max_pairs_of(b2b_handle *h, cudaLaunchConfig_t &cfg) {
     using Cf = hg2::Cfg<NSPLIT>;
+    constexpr int slot = NSPLIT - 1 + (HALVES ? 1 : 0);
     std::lock_guard<std::mutex> lk(g_hgemm_mu);
     DeviceLaunchState &st = g_hgemm_state[h->device & 63];
-    if (!st.attr2[NSPLIT - 1]) {
-        cudaError_t e =
-            cudaFuncSetAttribute(hgemm_tc2_kernel<NSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES);
+    if (!st.attr2[slot]) {
+        cudaError_t e = cudaFuncSetAttribute(hgemm_tc2_kernel<NSPLIT, HALVES>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES);
         if (e != cudaSuccess) {
             fail_cuda(e, "hgemm pair smem attribute");
             return -1;
         }
         cfg.gridDim = dim3(2 * (h->sm_count / 2));
         int clusters = 0;
-        e = cudaOccupancyMaxActiveClusters(&clusters, (void *)hgemm_tc2_kernel<NSPLIT>, &cfg);
+        e = cudaOccupancyMaxActiveClusters(&clusters, (void *)hgemm_tc2_kernel<NSPLIT, HALVES>, &cfg);
         if (e != cudaSuccess) {
             fail_cuda(e, "cudaOccupancyMaxActiveClusters");
             return -1;
         }
-        st.max_pairs[NSPLIT - 1] = clusters > 0 ? clusters : h->sm_count / 2;
-        st.attr2[NSPLIT - 1] = true;
+        st.max_pairs[slot] = clusters > 0 ? clusters : h->sm_count / 2;
+        st.attr2[slot] = true;
     }
-    return st.max_pairs[NSPLIT - 1];
+    return st.max_pairs[slot];
 }
 
-template <int NSPLIT>
+template <int NSPLIT, bool HALVES>
 int launch_pair_kernel(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmC,
                        const HgemmArgs &args, size_t m, size_t n, int max_pairs) {
     using Cf = hg2::Cfg<NSPLIT>;
@@ -863,7 +927,7 @@ int launch_pair_kernel(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap 
     const size_t tiles = ((m + 255) / 256) * ((n + Cf::BN - 1) / Cf::BN);
     const int pairs = static_cast<int>(tiles < static_cast<size_t>(max_pairs) ? tiles : max_pairs);
     cfg.gridDim = dim3(2 * pairs);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, hgemm_tc2_kernel<NSPLIT>, tmA, tmB, tmC, args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, hgemm_tc2_kernel<NSPLIT, HALVES>, tmA, tmB, tmC, args);
     if (e != cudaSuccess) return fail_cuda(e, "hgemm tcgen05 pair launch");
     return B2B_OK;
 }
@@ -889,19 +953,25 @@ int launch_pairs(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, 
     probe.attrs = attr;
     probe.numAttrs = 1;
     probe.dynamicSmemBytes = hg2::Cfg<2>::SMEM_BYTES;
-    const int wide_pairs = max_pairs_of<2>(h, probe);
+    const int wide_pairs = max_pairs_of<2, false>(h, probe);
     if (wide_pairs < 0) return B2B_ERR_CUDA;
     const size_t wide_tiles = ((m + 255) / 256) * ((n + 511) / 512);
     // A fused all-gather makes the epilogue long (its stores cross NVLink to
     // every rank): keep the double-buffered accumulators of the 256 x 256
     // tiles so the next tile's MMAs run meanwhile.
-    const bool wide = h->hgemm_variant == 3 || (h->hgemm_variant != 2 && args.ndst <= 1 && n >= 512 &&
+    const bool wide = h->hgemm_variant == 3 || h->hgemm_variant == 4 ||
+                      (h->hgemm_variant != 2 && args.ndst <= 1 && n >= 512 &&
                                                  args.K >= 2048 && wide_tiles >= static_cast<size_t>(wide_pairs));
-    if (wide) return launch_pair_kernel<2>(h, tmA, tmB, tmC, args, m, n, wide_pairs);
+    if (wide) {
+        if (h->hgemm_variant == 3) return launch_pair_kernel<2, false>(h, tmA, tmB, tmC, args, m, n, wide_pairs);
+        const int halves_pairs = max_pairs_of<2, true>(h, probe);
+        if (halves_pairs < 0) return B2B_ERR_CUDA;
+        return launch_pair_kernel<2, true>(h, tmA, tmB, tmC, args, m, n, halves_pairs);
+    }
     probe.dynamicSmemBytes = hg2::Cfg<1>::SMEM_BYTES;
-    const int pairs = max_pairs_of<1>(h, probe);
+    const int pairs = max_pairs_of<1, false>(h, probe);
     if (pairs < 0) return B2B_ERR_CUDA;
-    return launch_pair_kernel<1>(h, tmA, tmB, tmC, args, m, n, pairs);
+    return launch_pair_kernel<1, false>(h, tmA, tmB, tmC, args, m, n, pairs);
 }
 }  // namespace
 
@@ -954,34 +1024,81 @@ int launch_hgemm_gather_multicast(b2b_handle *h, size_t m, size_t n, size_t k, f
     return rc;
 }
 
+namespace {
+
+// Copies a rows x cols f16 matrix (row pitch src_ld elements) into dst with
+// row pitch dst_ld >= cols, zero-filling columns cols..dst_ld-1 and rows
+// rows..dst_rows-1.  Stream-ordered (capturable) memset/memcpy nodes only.
+int pad_copy_f16(b2b_handle *h, uint16_t *dst, size_t dst_ld, size_t dst_rows, const uint16_t *src, size_t src_ld,
+                 size_t rows, size_t cols) {
+    cudaError_t e = cudaSuccess;
+    if (dst_ld > cols)
+        e = cudaMemset2DAsync(dst + cols, dst_ld * 2, 0, (dst_ld - cols) * 2, rows, h->stream);
+    if (e == cudaSuccess && dst_rows > rows)
+        e = cudaMemsetAsync(dst + rows * dst_ld, 0, (dst_rows - rows) * dst_ld * 2, h->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpy2DAsync(dst, dst_ld * 2, src, src_ld * 2, cols * 2, rows, cudaMemcpyDeviceToDevice, h->stream);
+    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "hgemm padding copy");
+}
+
+int launch_hgemm_tc(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A, const uint16_t *B,
+                    float beta, uint16_t *C);
+
+}  // namespace
+
+// HGEMM entry: the tensor-core kernels where the tensor maps can describe the
+// operands; else, for GEMMs large enough (m*n*k >= 2^27) that the tensor
+// cores pay for the copies, the operands the maps cannot describe (K or N not
+// a multiple of 8, or not 16-byte aligned) are copied into zero-padded
+// workspace (K and N rounded up to 8; the zero columns of A and rows of B add
+// exact zeros to every sum, so each output is the same f32 sum as without
+// padding), the padded GEMM runs on the tensor cores and C's columns are
+// copied back; smaller ones run the CUDA-core kernel.  hgemm_variant 5
+// forces the CUDA-core kernel for those shapes.
 int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A, const uint16_t *B,
                  float beta, uint16_t *C) {
-    if (hgemm_tc_eligible(m, n, k, A, B, C)) {
-        CUtensorMap tmA, tmB;
-        int rc = encode_2d_f16(&tmA, A, m, k, hg::BK, hg::BM);
-        if (rc) return rc;
-        rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
-        if (rc) return rc;
-        HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns, h->hgemm_group_m, 0, 0, 0, {}, nullptr};
-        // More than one 128-row tile: CTA pairs with 256 x 256 tiles.
-        if (m > static_cast<size_t>(hg::BM) && !h->force_single_cta && h->hgemm_variant != 1)
-            return launch_pairs(h, tmA, tmB, args, m, n);
-        {
-            std::lock_guard<std::mutex> lk(g_hgemm_mu);
-            DeviceLaunchState &st = g_hgemm_state[h->device & 63];
-            if (!st.attr1) {
-                cudaError_t e =
-                    cudaFuncSetAttribute(hgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hg::SMEM_BYTES);
-                if (e != cudaSuccess) return fail_cuda(e, "hgemm smem attribute");
-                st.attr1 = true;
+    if (hgemm_tc_eligible(m, n, k, A, B, C)) return launch_hgemm_tc(h, m, n, k, alpha, A, B, beta, C);
+    const size_t k8 = (k + 7) / 8 * 8, n8 = (n + 7) / 8 * 8;
+    const double work = static_cast<double>(m) * static_cast<double>(n) * static_cast<double>(k);
+    if (h->hgemm_variant != 5 && work >= 134217728.0 && m < (1ull << 31) && n8 < (1ull << 31) && k8 < (1ull << 31) &&
+        ((m + 127) / 128) * ((n8 + 255) / 256) < (1ull << 31)) {
+        const bool pad_a = k8 != k || !aligned16(A);
+        const bool pad_b = k8 != k || n8 != n || !aligned16(B);
+        const bool pad_c = n8 != n || !aligned16(C);
+        auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+        const size_t bytes_a = pad_a ? up(m * k8 * 2) : 0, bytes_b = pad_b ? up(k8 * n8 * 2) : 0,
+                     bytes_c = pad_c ? up(m * n8 * 2) : 0;
+        void *ws = nullptr;
+        if (int rc = workspace(h, bytes_a + bytes_b + bytes_c, &ws)) return rc;
+        uint8_t *w = static_cast<uint8_t *>(ws);
+        const uint16_t *a = A, *b = B;
+        uint16_t *c = C;
+        int rc = B2B_OK;
+        if (pad_a) {
+            uint16_t *ap = reinterpret_cast<uint16_t *>(w);
+            rc = pad_copy_f16(h, ap, k8, m, A, k, m, k);
+            a = ap;
+        }
+        if (rc == B2B_OK && pad_b) {
+            uint16_t *bp = reinterpret_cast<uint16_t *>(w + bytes_a);
+            rc = pad_copy_f16(h, bp, n8, k8, B, n, k, n);
+            b = bp;
+        }
+        if (rc == B2B_OK && pad_c) {
+            c = reinterpret_cast<uint16_t *>(w + bytes_a + bytes_b);
+            // beta != 0 reads C: bring it in (the padding columns' outputs
+            // are discarded, so they need no defined value)
+            if (beta != 0.0f) {
+                cudaError_t e = cudaMemcpy2DAsync(c, n8 * 2, C, n * 2, n * 2, m, cudaMemcpyDeviceToDevice, h->stream);
+                if (e != cudaSuccess) rc = fail_cuda(e, "hgemm padding copy");
             }
         }
-        const int tiles = static_cast<int>(((m + hg::BM - 1) / hg::BM) * ((n + hg::BN - 1) / hg::BN));
-        const int grid = tiles < h->sm_count ? tiles : h->sm_count;
-        hgemm_tc_kernel<<<grid, hg::THREADS, hg::SMEM_BYTES, h->stream>>>(tmA, tmB, args);
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return fail_cuda(e, "hgemm tcgen05 launch");
-        return B2B_OK;
+        if (rc == B2B_OK) rc = launch_hgemm_tc(h, m, n8, k8, alpha, a, b, beta, c);
+        if (rc == B2B_OK && pad_c) {
+            cudaError_t e = cudaMemcpy2DAsync(C, n * 2, c, n8 * 2, n * 2, m, cudaMemcpyDeviceToDevice, h->stream);
+            if (e != cudaSuccess) rc = fail_cuda(e, "hgemm padding copy back");
+        }
+        return rc;
     }
     dim3 grid(static_cast<unsigned>((n + 63) / 64), static_cast<unsigned>((m + 63) / 64));
     if (grid.y > 65535u) return fail(B2B_ERR_INVALID_ARG, "hgemm: m too large for the generic path");
@@ -990,5 +1107,38 @@ int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const
     if (e != cudaSuccess) return fail_cuda(e, "hgemm generic launch");
     return B2B_OK;
 }
+
+namespace {
+
+int launch_hgemm_tc(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const uint16_t *A, const uint16_t *B,
+                    float beta, uint16_t *C) {
+    CUtensorMap tmA, tmB;
+    int rc = encode_2d_f16(&tmA, A, m, k, hg::BK, hg::BM);
+    if (rc) return rc;
+    rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
+    if (rc) return rc;
+    HgemmArgs args{C, (int)m, (int)n, (int)k, alpha, beta, h->d_status, h->wait_limit_ns, h->hgemm_group_m, 0, 0, 0, {}, nullptr};
+    // More than one 128-row tile: CTA pairs with 256 x 256 tiles.
+    if (m > static_cast<size_t>(hg::BM) && !h->force_single_cta && h->hgemm_variant != 1)
+        return launch_pairs(h, tmA, tmB, args, m, n);
+    {
+        std::lock_guard<std::mutex> lk(g_hgemm_mu);
+        DeviceLaunchState &st = g_hgemm_state[h->device & 63];
+        if (!st.attr1) {
+            cudaError_t e =
+                cudaFuncSetAttribute(hgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hg::SMEM_BYTES);
+            if (e != cudaSuccess) return fail_cuda(e, "hgemm smem attribute");
+            st.attr1 = true;
+        }
+    }
+    const int tiles = static_cast<int>(((m + hg::BM - 1) / hg::BM) * ((n + hg::BN - 1) / hg::BN));
+    const int grid = tiles < h->sm_count ? tiles : h->sm_count;
+    hgemm_tc_kernel<<<grid, hg::THREADS, hg::SMEM_BYTES, h->stream>>>(tmA, tmB, args);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "hgemm tcgen05 launch");
+    return B2B_OK;
+}
+
+}  // namespace
 
 }  // namespace b2b

@@ -141,11 +141,13 @@ VARIANT_SHAPES = [(1024, 1280, 768), (257, 520, 1000), (300, 264, 72), (256, 512
 @pytest.mark.parametrize("m,n,k", VARIANT_SHAPES)
 @pytest.mark.parametrize("beta", [0.0, -0.5])
 def test_hgemm_kernel_variants_agree(oracle, monkeypatch, m, n, k, beta):
-    # Single-CTA 128x256 (variant 1), pair 256x256 (2) and pair 256x512 (3),
-    # forced through B2B_HGEMM_VARIANT, on shapes with ragged M/N/K edges:
-    # each within the FP64 bound, and all three within an f16 ulp or two.
-    # beta == 0 takes the pair kernels' TMA-store epilogue, beta != 0 the
-    # read-modify-write one.
+    # Single-CTA 128x256 (variant 1), pair 256x256 (2), pair 256x512 (3) and
+    # pair 256x512 releasing its accumulator in halves (4), forced through
+    # B2B_HGEMM_VARIANT, on shapes with ragged M/N/K edges (K from one k-block
+    # to more than the stage ring): each within the FP64 bound, all within an
+    # f16 ulp or two, and 3 and 4 bit-identical (same MMAs, same k order per
+    # column).  beta == 0 takes the pair kernels' TMA-store epilogue, beta != 0
+    # the read-modify-write one.
     import b2blas
 
     A = oracle.normal_f16(m * k, 6, 1, 0.0, 0.1)
@@ -153,7 +155,7 @@ def test_hgemm_kernel_variants_agree(oracle, monkeypatch, m, n, k, beta):
     C = oracle.normal_f16(m * n, 6, 3, 0.0, 0.1)
     ref = oracle.hgemm_f64(m, n, k, 0.75, A, B, beta, C)
     outs = []
-    for v in ("1", "2", "3"):
+    for v in ("1", "2", "3", "4"):
         monkeypatch.setenv("B2B_HGEMM_VARIANT", v)
         h = b2blas.Handle(0)
         try:
@@ -166,3 +168,45 @@ def test_hgemm_kernel_variants_agree(oracle, monkeypatch, m, n, k, beta):
     for o in outs[1:]:
         d = np.abs(o.view(np.float16).astype(np.float64) - outs[0].view(np.float16).astype(np.float64))
         assert np.max(d) <= scale
+    assert np.array_equal(outs[2], outs[3])
+
+
+@pytest.mark.parametrize("m,n,k,beta,off", [(777, 1000, 1001, 0.0, 0), (1024, 1030, 1024, 0.5, 0),
+                                            (600, 1024, 1000, -0.5, 1), (300, 1536, 2000, 0.0, 1)])
+def test_hgemm_unaligned_large_takes_padded_tensor_path(oracle, monkeypatch, m, n, k, beta, off):
+    # Large GEMMs whose K or N is not a multiple of 8, or whose operands are
+    # not 16-byte aligned (off = 1: every pointer 2 bytes past an aligned
+    # address), run on the tensor cores through zero-padded workspace; the
+    # CUDA-core kernel (variant 5) is the comparison.  Both are checked
+    # against the FP64 evaluation; the padded call must write C's m x n
+    # elements only (the guard elements around C stay as they were).
+    import b2blas
+
+    A = oracle.normal_f16(m * k, 9, 1, 0.0, 0.1)
+    B = oracle.normal_f16(k * n, 9, 2, 0.0, 0.1)
+    C = oracle.normal_f16(m * n, 9, 3, 0.0, 0.1)
+    ref = oracle.hgemm_f64(m, n, k, 0.75, A, B, beta, C)
+    guard = np.full(8, np.float16(7.0)).view(np.uint16)
+    outs = []
+    for v in (None, "5"):
+        if v is None:
+            monkeypatch.delenv("B2B_HGEMM_VARIANT", raising=False)
+        else:
+            monkeypatch.setenv("B2B_HGEMM_VARIANT", v)
+        h = b2blas.Handle(0)
+        try:
+            bufs = []
+            for X in (A, B, C):
+                host = np.concatenate([guard[:off], X, guard])
+                d = h.upload(host)
+                bufs.append((d, b2blas.DeviceBuffer.from_ptr(h, d.ptr + 2 * off, X.size, np.uint16)))
+            (a, av), (b, bv), (c, cv) = bufs
+            h.hgemm(b2blas.GemmConfig(m, n, k, 0.75, beta), av, bv, cv)
+            h.synchronize()
+            full = h.download(c)
+            assert np.array_equal(full[:off], guard[:off]) and np.array_equal(full[off + m * n:], guard)
+            outs.append(full[off:off + m * n].copy())
+        finally:
+            h.close()
+    for o in outs:
+        assert oracle.rel_err(o, ref) <= 2e-3

@@ -17,9 +17,18 @@
 //     16-byte chunks).
 //   * A is stored transposed in shared memory (As[k][m], padded by 4) so
 //     that fragments along M are contiguous; B is stored as-is (Bs[k][n]).
-//   * Two shared stages; the next k-tile is fetched from global memory into
-//     registers while the current one is multiplied, then stored to the
-//     other stage -- one __syncthreads per k-tile.
+//   * Two kernels share that layout:
+//       - gemm_async_kernel (the default where the 16-byte path applies):
+//         a STAGES-deep cp.async ring (4 stages of k-tile 8 for SGEMM), A
+//         transposed on the way in with 4-byte copies, B as 16-byte copies,
+//         fragments double-buffered in registers, copy addresses derived from
+//         two base pointers so the FMA loop keeps its registers;
+//       - gemm_simt_kernel (any shape or alignment): two shared stages, the
+//         next k-tile fetched from global memory into registers while the
+//         current one is multiplied, then stored to the other stage -- one
+//         __syncthreads per k-tile.
+//     Single large SGEMMs and batched SGEMMs normally take the TMA-fed
+//     kernels of sgemm_tma.cu instead, with the same per-element arithmetic.
 //   * The epilogue skips reading C when beta == 0.
 //   * The batch and tile indices come from one flattened grid index, so there
 //     is no 65535 limit on the batch count (the reference puts the batch in
@@ -661,7 +670,7 @@ int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float
     // Batched calls (and variant 23): the TMA-fed kernel on row-major A (no
     // transpose pass), batched through 3-D tensor maps; same bits, 2.5%
     // faster than the cp.async kernel on 4096 x 256^3.
-    if ((variant == 23 || (variant == 0 && batch > 1)) &&
+    if ((variant == 23 || variant == 24 || variant == 25 || (variant == 0 && batch > 1)) &&
         b2b::sgemm_tma_rowa_eligible(M, N, K, sA, sB, sC, batch, A, B, C))
         return b2b::launch_sgemm_tma_rowa(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi.bias, epi.relu);
     if (!vec_ok(K, N, sA, sB, sC, A, B, C) || variant == 1)

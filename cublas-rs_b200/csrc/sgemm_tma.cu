@@ -63,6 +63,7 @@ struct SArgs {
     int relu;
     int *status;
     uint64_t wait_ns;
+    int group_m;  // raster group in M tiles
 };
 
 // kPack selects the FFMA form of the 16 x 8 outer product (each output is
@@ -93,10 +94,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t tiles_m = (args.M + kBM - 1) / kBM, tiles_n = (args.N + kBN - 1) / kBN;
     // grouped raster
     const int64_t t = blockIdx.x;
-    const int64_t span = kGroupM * tiles_n;
+    const int64_t group_m = args.group_m;
+    const int64_t span = group_m * tiles_n;
     const int64_t g = t / span;
-    const int64_t first = g * kGroupM;
-    const int64_t gm = tiles_m - first < kGroupM ? tiles_m - first : kGroupM;
+    const int64_t first = g * group_m;
+    const int64_t gm = tiles_m - first < group_m ? tiles_m - first : group_m;
     const int64_t r = t - g * span;
     const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * kBN;
     const int64_t ktiles = (args.K + kBK - 1) / kBK;
@@ -271,19 +273,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // The same FFMA loop fed from row-major A directly, batched (the default for
-// strided-batched calls: 53.9 vs 52.6 TFLOP/s for the cp.async kernel on
-// 4096 x 256^3; on single large GEMMs the transposed-A kernel above is
-// faster, 60.2 vs 55.5 at 8192^3, since it loads a 16-byte A fragment where
-// this one loads four 4-byte values).  A tiles arrive
-// as they lie in memory, As[m][k] (box 32 k x 128 m), with the 128-byte
-// swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8).  A thread owns
-// rows wm*64 + ty + 4i (i < 16), so at any k the four row groups of a warp
-// read four consecutive rows -- four distinct chunks, no bank conflicts -- and
+// strided-batched calls; on single large GEMMs the transposed-A kernel above
+// is faster, 60.2 vs 55.5 TFLOP/s at 8192^3, since it loads a 16-byte A
+// fragment where this one loads four 4-byte values).  A tiles arrive as they
+// lie in memory, As[m][k] (box 32 k x 128 m), with the 128-byte swizzle:
+// 16-byte chunk c of row r sits at chunk c ^ (r % 8).  A thread owns rows
+// wm*64 + ty + 4i (i < 16), so at any k the four row groups of a warp read
+// four consecutive rows -- four distinct chunks, no bank conflicts -- and
 // each a value is one 4-byte shared load; the row pair (i, i+1) of an FFMA2
 // comes from two such loads straight into a register pair, so no transpose
-// pass and no extra moves for A (b is duplicated as in form 1).  Operands are
-// 3-D tensor maps (x innermost, then rows, then batch), so a tile never reads
-// across a batch boundary and out-of-range rows/columns arrive as zeros.
+// pass and no extra moves for A (b is duplicated as in form 1).  Operands
+// are 3-D tensor maps (x innermost, then rows, then batch), so a tile never
+// reads across a batch boundary and out-of-range rows/columns arrive as
+// zeros.
+//
+// Two CTA shapes, the same per-thread work (16 x 8 outputs, 248 registers):
+//   WN = 4: 8 warps, 128 x 256 tiles, 4 stages of 48 KiB -- one CTA per SM.
+//   WN = 2: 4 warps, 128 x 128 tiles, 3 stages of 32 KiB -- two CTAs per SM,
+//     so one CTA's prologue (the first TMA round trip) and epilogue (the C
+//     stores) overlap the other's FFMA loop (variant 25; slower on the
+//     4096 x 256^3 batched workload, 51.5 vs 54.0 TFLOP/s).
+// (A persistent form of WN = 4 whose load stream ran across tile boundaries
+// measured 45.1 vs 53.7 TFLOP/s on 4096 x 256^3: the bookkeeping took it to
+// 255 registers and slowed the FFMA loop more than it hid.)
 struct RArgs {
     float *C;
     int64_t M, N, K, sC, tiles_m, tiles_n;
@@ -294,19 +306,34 @@ struct RArgs {
     uint64_t wait_ns;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <int WN>
+struct RowaCfg {
+    static constexpr int BN = WN * (kTN / 4) * 32;  // 256 or 128
+    static constexpr int WARPS = kWM * WN;
+    static constexpr int THREADS = WARPS * 32;
+    static constexpr int STAGES = WN == 4 ? 4 : 3;
+    static constexpr int MIN_BLOCKS = WN == 4 ? 1 : 2;
+    static constexpr int B_STAGE_F = kBK * BN;
+    static constexpr uint32_t STAGE_BYTES = (kAStageF + B_STAGE_F) * 4;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <int WN>
+__global__ void __launch_bounds__(RowaCfg<WN>::THREADS, RowaCfg<WN>::MIN_BLOCKS)
     sgemm_tma_rowa_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           RArgs args) {
     using namespace sm100;
+    using Cf = RowaCfg<WN>;
+    constexpr int S = Cf::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
     float *As = reinterpret_cast<float *>(smem);  // stages of [128 m][32 k], swizzled
-    float *Bs = As + kStages * kAStageF;          // stages of [32 k][256 n]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+    float *Bs = As + S * kAStageF;                // stages of [32 k][BN n]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cf::STAGE_BYTES);
     uint64_t *full = bars;
-    uint64_t *empty = bars + kStages;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * kStages);
+    uint64_t *empty = bars + S;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * S);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t per_batch = args.tiles_m * args.tiles_n;
@@ -318,13 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t first = g * kGroupM;
     const int64_t gm = args.tiles_m - first < kGroupM ? args.tiles_m - first : kGroupM;
     const int64_t r = tb - g * span;
-    const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * kBN;
+    const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * Cf::BN;
     const int64_t ktiles = (args.K + kBK - 1) / kBK;
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kComputeWarps);
+            mbar_init(&empty[s], Cf::WARPS);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -336,18 +363,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool loader = tid == 0;
     int64_t issued = 0;
     auto issue = [&](int64_t kt) {
-        const int s = static_cast<int>(kt % kStages);
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        const int s = static_cast<int>(kt % S);
+        mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
         tma_load_3d(As + s * kAStageF, &tmA, &full[s], static_cast<int32_t>(kt * kBK), static_cast<int32_t>(m0),
                     static_cast<int32_t>(batch));
-        tma_load_3d(Bs + s * kBStageF, &tmB, &full[s], static_cast<int32_t>(n0), static_cast<int32_t>(kt * kBK),
+        tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], static_cast<int32_t>(n0), static_cast<int32_t>(kt * kBK),
                     static_cast<int32_t>(batch));
         ++issued;
     };
     if (loader)
-        for (int64_t kt = 0; kt < kStages && kt < ktiles; ++kt) issue(kt);
+        for (int64_t kt = 0; kt < S && kt < ktiles; ++kt) issue(kt);
 
-    const int wm = warp / kWN, wn = warp % kWN;
+    const int wm = warp / WN, wn = warp % WN;
     const int ty = lane >> 3, tx = lane & 7;
     const int row0 = wm * (kTM / 4) * 16 + ty;  // this thread's rows: row0 + 4i
     const int col_base = wn * (kTN / 4) * 32 + tx * 4;
@@ -369,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kTM; ++i) af[i] = (i & 1) ? ao[4 * i * 32] : ae[4 * i * 32];
 #pragma unroll
         for (int q = 0; q < kTN / 4; ++q) {
-            const float4 v = *reinterpret_cast<const float4 *>(bs + kk * kBN + col_base + q * 32);
+            const float4 v = *reinterpret_cast<const float4 *>(bs + kk * Cf::BN + col_base + q * 32);
             bf[q * 4 + 0] = v.x;
             bf[q * 4 + 1] = v.y;
             bf[q * 4 + 2] = v.z;
@@ -379,15 +406,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     bool ok = true;
     for (int64_t kt = 0; kt < ktiles; ++kt) {
-        const int s = static_cast<int>(kt % kStages);
-        const uint32_t ph = static_cast<uint32_t>((kt / kStages) & 1);
+        const int s = static_cast<int>(kt % S);
+        const uint32_t ph = static_cast<uint32_t>((kt / S) & 1);
         const bool w = mbar_wait(&full[s], ph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x34, args.wait_ns);
         if (!__all_sync(0xffffffffu, w)) {
             ok = false;
             break;
         }
         const float *as = As + s * kAStageF;
-        const float *bs = Bs + s * kBStageF;
+        const float *bs = Bs + s * Cf::B_STAGE_F;
         float af[2][kTM], bf[2][kTN];
         load_frags(as, bs, 0, af[0], bf[0]);
 #pragma unroll
@@ -405,10 +432,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         if (loader && kt >= 1) {
-            const int64_t done = kt - 1, next = done + kStages;
+            const int64_t done = kt - 1, next = done + S;
             if (next < ktiles) {
-                const int ds = static_cast<int>(done % kStages);
-                const uint32_t dph = static_cast<uint32_t>((done / kStages) & 1);
+                const int ds = static_cast<int>(done % S);
+                const uint32_t dph = static_cast<uint32_t>((done / S) & 1);
                 if (!mbar_wait(&empty[ds], dph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x33, args.wait_ns)) {
                     ok = false;
                 } else {
@@ -423,9 +450,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (!ok) {
         if (loader && issued) {
-            const int64_t first_pending = issued > kStages ? issued - kStages : 0;
+            const int64_t first_pending = issued > S ? issued - S : 0;
             for (int64_t kt = first_pending; kt < issued; ++kt)
-                mbar_wait_drain(&full[kt % kStages], static_cast<uint32_t>((kt / kStages) & 1), 1000000000ull);
+                mbar_wait_drain(&full[kt % S], static_cast<uint32_t>((kt / S) & 1), 1000000000ull);
         }
         return;
     }
@@ -523,7 +550,8 @@ int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha
     }
     const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     if (tiles > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
-    SArgs args{C, M, N, K, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns};
+    SArgs args{C, M, N, K, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns,
+               h->sgemm_group_m > 0 ? h->sgemm_group_m : kGroupM};
     kern<<<static_cast<unsigned>(tiles), kThreads, kSmem, h->stream>>>(tmAt, tmB, args);
     e = cudaGetLastError();
     return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm TMA launch");
@@ -539,9 +567,35 @@ bool sgemm_tma_rowa_eligible(int64_t M, int64_t N, int64_t K, int64_t sA, int64_
     if (batch > 1 && (sA < M * K || sB < K * N || sC < M * N)) return false;
     const int64_t lim = int64_t(1) << 31;
     if (M >= lim || N >= lim || K >= lim || batch >= lim) return false;
-    const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN) * batch;
+    const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + 127) / 128) * batch;  // the 128-wide form's count
     return tiles < lim;
 }
+
+namespace {
+
+template <int WN>
+int launch_rowa(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, RArgs args, int64_t batch) {
+    using Cf = RowaCfg<WN>;
+    {
+        static std::mutex mu;
+        static bool attr_set[64] = {};
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set[h->device & 63]) {
+            cudaError_t e =
+                cudaFuncSetAttribute(sgemm_tma_rowa_kernel<WN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+            if (e != cudaSuccess) return fail_cuda(e, "sgemm (row-major A) smem attribute");
+            attr_set[h->device & 63] = true;
+        }
+    }
+    args.tiles_n = (args.N + Cf::BN - 1) / Cf::BN;
+    const int64_t blocks = args.tiles_m * args.tiles_n * batch;
+    if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
+    sgemm_tma_rowa_kernel<WN><<<static_cast<unsigned>(blocks), Cf::THREADS, Cf::SMEM, h->stream>>>(tmA, tmB, args);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm (row-major A) TMA launch");
+}
+
+}  // namespace
 
 int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
                           int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch,
@@ -551,33 +605,24 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
         sB = K * N;
         sC = M * N;
     }
+    const int64_t tiles_m = (M + kBM - 1) / kBM;
+    // 128 x 256 tiles; variant 25 takes the 128 x 128 form (two CTAs per SM),
+    // which measured slower on 4096 x 256^3 (51.5 vs 54.0 TFLOP/s): half the
+    // B tile per CTA costs more L2 -> SM traffic per flop than overlapping two
+    // CTAs' prologues and epilogues saves.
+    const bool narrow = h->sgemm_variant == 25;
+    const int bn = narrow ? RowaCfg<2>::BN : RowaCfg<4>::BN;
     CUtensorMap tmA, tmB;
     int rc = encode_tma_3d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, A, static_cast<uint64_t>(K),
                            static_cast<uint64_t>(M), static_cast<uint64_t>(batch), static_cast<uint64_t>(K) * 4,
                            static_cast<uint64_t>(sA) * 4, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     rc = encode_tma_3d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, B, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
-                       static_cast<uint64_t>(batch), static_cast<uint64_t>(N) * 4, static_cast<uint64_t>(sB) * 4, kBN,
+                       static_cast<uint64_t>(batch), static_cast<uint64_t>(N) * 4, static_cast<uint64_t>(sB) * 4, bn,
                        kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    cudaError_t e;
-    {
-        static std::mutex mu;
-        static bool attr_set[64] = {};
-        std::lock_guard<std::mutex> lk(mu);
-        if (!attr_set[h->device & 63]) {
-            e = cudaFuncSetAttribute(sgemm_tma_rowa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-            if (e != cudaSuccess) return fail_cuda(e, "sgemm (row-major A) smem attribute");
-            attr_set[h->device & 63] = true;
-        }
-    }
-    const int64_t tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN;
-    const int64_t blocks = tiles_m * tiles_n * batch;
-    if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
-    RArgs args{C, M, N, K, sC, tiles_m, tiles_n, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns};
-    sgemm_tma_rowa_kernel<<<static_cast<unsigned>(blocks), kThreads, kSmem, h->stream>>>(tmA, tmB, args);
-    e = cudaGetLastError();
-    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm (row-major A) TMA launch");
+    RArgs args{C, M, N, K, sC, tiles_m, 0, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns};
+    return narrow ? launch_rowa<2>(h, tmA, tmB, args, batch) : launch_rowa<4>(h, tmA, tmB, args, batch);
 }
 
 }  // namespace b2b

@@ -396,19 +396,22 @@ def test_sgemm_ffma_kernels_bit_identical(monkeypatch, oracle, m, n, k, alpha, b
         assert np.array_equal(outs[v], outs["11"]), v
 
 
-def test_strided_batched_tma_kernel_bit_identical(monkeypatch, oracle):
+@pytest.mark.parametrize("batch", [12, 300])
+def test_strided_batched_tma_kernel_bit_identical(monkeypatch, oracle, batch):
     # The batched default (TMA-fed on row-major A, 3-D tensor maps) against
-    # the cp.async kernel, with gaps between batches and ragged M/N edges.
+    # the cp.async kernel (variant 11) and the TMA kernel's 128 x 256 and
+    # 128 x 128 (two CTAs per SM) forms (variants 24, 25), with gaps between
+    # batches and ragged M/N edges.
     import b2blas
 
-    batch, m, n, k = 12, 200, 136, 100
+    m, n, k = 200, 136, 100
     sa, sb, sc = m * k + 4, k * n + 8, m * n + 12
     A = oracle.uniform_f32(batch * sa, 22, 1)
     B = oracle.uniform_f32(batch * sb, 22, 2)
     C = oracle.uniform_f32(batch * sc, 22, 3)
     cfg = b2blas.GemmConfig(m, n, k, 1.5, 0.5)
     outs = {}
-    for v in ("0", "11"):
+    for v in ("0", "11", "24", "25"):
         monkeypatch.setenv("B2B_SGEMM_VARIANT", v)
         h = b2blas.Handle(0)
         try:
@@ -419,6 +422,8 @@ def test_strided_batched_tma_kernel_bit_identical(monkeypatch, oracle):
         finally:
             h.close()
     assert np.array_equal(outs["0"], outs["11"])
+    assert np.array_equal(outs["0"], outs["24"])
+    assert np.array_equal(outs["0"], outs["25"])
     ref = oracle.sgemm_strided_batched_f64(m, n, k, 1.5, A, sa, B, sb, 0.5, C, sc, batch)
     got = np.concatenate([outs["0"][i * sc:i * sc + m * n] for i in range(batch)])
     assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f32")

@@ -4,7 +4,7 @@
 //
 // This is NOT part of the library: nothing in cublas-rs_b200 links or calls
 // it.  bench.py times it beside the product kernels on the same resident
-// buffers, and tests/test_refkernels_gpu.py checks it against the FP64
+// buffers, and tests/test_refkernels.py checks it against the FP64
 // oracle, so the numbers it gives are those of a working restatement.
 //
 // Each kernel keeps the reference's algorithm, launch geometry and summation

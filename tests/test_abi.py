@@ -31,11 +31,18 @@ def test_library_exports_every_declared_symbol():
     assert sorted(_lib.SIGNATURES) == names
 
 
-def test_integration_binding_covers_the_header():
-    # INTEGRATION.md's Rust FFI block declares every entry point, once.
-    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    declared = re.findall(r"pub fn (b2b_\w+)\(", doc)
-    assert sorted(declared) == _header_functions()
+def test_rust_binding_covers_the_header():
+    # The cublas-sys crate declares every entry point once, in header order,
+    # and the header's constants with the same values.
+    src = open(os.path.join(ROOT, "cublas-rs_b200", "rust", "cublas-sys", "src", "lib.rs")).read()
+    declared = re.findall(r"pub fn (b2b_\w+)\(", src)
+    hdr = open(os.path.join(ROOT, "include", "b2blas.h")).read()
+    in_order = re.findall(r"B2B_API\s+[\w\s\*]+?\b(b2b_\w+)\s*\(", hdr)
+    assert declared == in_order
+    consts = dict(re.findall(r"pub const (B2B_\w+): \w+ = (\d+);", src))
+    for name, value in re.findall(r"\b(B2B_\w+)\s*=\s*(\d+)", hdr):
+        assert consts.get(name) == value, name
+    assert consts.get("B2B_IPC_HANDLE_BYTES") == "64"
 
 
 def test_library_exports_nothing_else():

@@ -188,16 +188,47 @@ class ClockSampler:
 E2E_HOST = {"handle": None}
 
 
-def sgemm_kernels_per_call(m, n, k, tf32x3=False):
-    """Kernels one single SGEMM call launches: 2 on the TMA-fed FFMA path (the
-    transpose of A, then the GEMM), else 1.  Mirrors the library's dispatch
-    (run_sgemm in gemm_simt.cu, sgemm_tma_eligible in sgemm_tma.cu) for
-    16-byte aligned operands."""
+def sgemm_ksplit(sm_count, m, n, k):
+    """The library's split-K choice for the TMA-fed SGEMM (sgemm_ksplit in
+    sgemm_tma.cu), restated to count launches: S in {1, 2, 3, 4, 6, 8} with
+    the least estimated time, taken only when it saves 10% or more."""
+    import math
+
+    tiles = ((m + 127) // 128) * ((n + 255) // 256)
+    kt = (k + 31) // 32
+
+    def est(S):
+        t = math.ceil(tiles * S / sm_count) * ((kt + S - 1) // S) * 5.2
+        if S > 1:
+            t += 8.0 * S * m * n / 6e12 * 1e6 + 4.0
+        return t
+
+    t1 = est(1)
+    best, tb = 1, t1
+    for S in (2, 3, 4, 6, 8):
+        if (kt + S - 1) // S < 8:
+            break
+        t = est(S)
+        if t < tb:
+            best, tb = S, t
+    return best if tb <= 0.9 * t1 else 1
+
+
+def sgemm_kernels_per_call(m, n, k, tf32x3=False, sm_count=148):
+    """Kernels one single SGEMM call launches: on the TMA-fed FFMA path the
+    transpose of A, the GEMM and, when split-K applies, the reduce; else 1.
+    Mirrors the library's dispatch (run_sgemm in gemm_simt.cu,
+    sgemm_tma_eligible and sgemm_ksplit in sgemm_tma.cu) for 16-byte aligned
+    operands."""
     variant = int(os.environ.get("B2B_SGEMM_VARIANT", "0") or 0)
     if tf32x3 or variant not in (0, 20, 21, 22):
         return 1
     ok = m % 4 == 0 and n % 4 == 0 and m >= 128 and n >= 1024 and 32 <= k <= 65535 * 32
-    return 2 if ok else 1
+    if not ok:
+        return 1
+    forced = int(os.environ.get("B2B_SGEMM_KSPLIT", "0") or 0)
+    S = forced if forced > 0 else sgemm_ksplit(sm_count, m, n, k)
+    return 3 if S > 1 else 2
 
 
 def _cur_stream():
@@ -944,7 +975,10 @@ class MlpWorkload(Workload):
             self.lane_bufs.append({"x": lw(self.X[r0:r0 + rows]), "w": [lw(t) for t in self.W],
                                    "b": [lw(t[r0:r0 + rows]) for t in self.bias], "bv": [lw(t) for t in self.bias_vec],
                                    "z": [lw(t[r0:r0 + rows]) for t in self.Z]})
-        per_gemm = [sgemm_kernels_per_call(rows, self.dims[i + 1], self.dims[i], bool(args.tf32x3))
+        self.whole_splits = [h.sgemm_splits(self.batch, self.dims[i + 1], self.dims[i]) for i in range(4)]
+        per_gemm = [(1 if args.tf32x3 else
+                     3 if self.whole_splits[i] > 1 else
+                     min(2, sgemm_kernels_per_call(rows, self.dims[i + 1], self.dims[i])))
                     for _, _, rows in self.lanes for i in range(4)]
         self.launches_per_step = sum(per_gemm) + (0 if self.fused else 4 * self.streams)  # + a saxpy per layer
         self.kernel = "sgemm_tma_kernel"
@@ -964,6 +998,10 @@ class MlpWorkload(Workload):
             for i in range(4):
                 fi, fo = self.dims[i], self.dims[i + 1]
                 cfg = b2blas.GemmConfig(rows, fo, fi, 1.0, 0.0)
+                if self.streams == 2:
+                    # each half sums the k ranges of the whole-batch GEMM
+                    # (its split-K factor), so two lanes give one lane's bits
+                    lh.set_sgemm_splits(self.whole_splits[i])
                 if self.fused:
                     # bias (and, for hidden layers, ReLU) in the GEMM epilogue
                     lh.sgemm_bias(cfg, inp, bufs["w"][i], bufs["z"][i], bufs["bv"][i], relu=i < 3, algo=self.algo)
@@ -972,6 +1010,8 @@ class MlpWorkload(Workload):
                     lh.sgemm_tiled(cfg, inp, bufs["w"][i], bufs["z"][i])
                     lh.saxpy(rows * fo, 1.0, bufs["b"][i], bufs["z"][i])
                 inp = bufs["z"][i]
+            if self.streams == 2:
+                lh.set_sgemm_splits(0)
         if self.streams == 2:  # and the step ends behind it
             self.ev_done.record(self.s2)
             torch.cuda.current_stream().wait_event(self.ev_done)

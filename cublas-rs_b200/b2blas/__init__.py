@@ -357,6 +357,18 @@ class Handle:
                                         ctypes.c_void_p(b.ptr), config.beta, ctypes.c_void_p(c.ptr),
                                         ctypes.c_void_p(bias.ptr if bias is not None else 0), 1 if relu else 0))
 
+    def sgemm_splits(self, m: int, n: int, k: int) -> int:
+        """Number of k ranges the FFMA SGEMM sums separately for an m x n x k
+        call (b2b_sgemm_splits; 1 = no split-K)."""
+        out = ctypes.c_int(0)
+        _check(self._lib.b2b_sgemm_splits(self._h, m, n, k, ctypes.byref(out)))
+        return out.value
+
+    def set_sgemm_splits(self, splits: int) -> None:
+        """Fix the split-K factor of this handle's later SGEMMs
+        (b2b_set_sgemm_splits): 0 = per call (default), 1 = never."""
+        _check(self._lib.b2b_set_sgemm_splits(self._h, int(splits)))
+
     def sgemm_3xtf32(self, config, a, b, c):
         """Opt-in split-precision tensor-core SGEMM (no reference counterpart)."""
         self.sgemm(config, a, b, c, Algo.Tf32x3)

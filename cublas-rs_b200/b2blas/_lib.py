@@ -43,6 +43,8 @@ SIGNATURES = {
     "b2b_sgemm": (_i, [_vp, _i, _sz, _sz, _sz, _f, _vp, _vp, _f, _vp]),
     "b2b_sgemm_simple": (_i, [_vp, _i, _sz, _sz, _sz, _f, _vp, _sz, _vp, _sz, _f, _vp, _sz]),
     "b2b_sgemm_bias": (_i, [_vp, _i, _sz, _sz, _sz, _f, _vp, _vp, _f, _vp, _vp, _i]),
+    "b2b_sgemm_splits": (_i, [_vp, _sz, _sz, _sz, ctypes.POINTER(_i)]),
+    "b2b_set_sgemm_splits": (_i, [_vp, _i]),
     "b2b_dgemm": (_i, [_vp, _i, _sz, _sz, _sz, _d, _vp, _vp, _d, _vp]),
     "b2b_dgemm_simple": (_i, [_vp, _i, _sz, _sz, _sz, _d, _vp, _sz, _vp, _sz, _d, _vp, _sz]),
     "b2b_hgemm": (_i, [_vp, _sz, _sz, _sz, _f, _vp, _vp, _f, _vp]),

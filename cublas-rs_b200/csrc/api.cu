@@ -54,6 +54,27 @@ int b2b_sgemm(b2b_handle *h, int algo, size_t m, size_t n, size_t k, float alpha
     return launch_sgemm(h, m, n, k, alpha, A, B, beta, C);
 }
 
+int b2b_sgemm_splits(b2b_handle *h, size_t m, size_t n, size_t k, int *splits) {
+    if (!h || !splits) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemm_splits: NULL argument");
+    *splits = 1;
+    if (m == 0 || n == 0 || k == 0) return B2B_OK;
+    const int64_t M = static_cast<int64_t>(m), N = static_cast<int64_t>(n), K = static_cast<int64_t>(k);
+    if (h->sgemm_variant != 0 && !(h->sgemm_variant >= 20 && h->sgemm_variant <= 22)) return B2B_OK;
+    if (!sgemm_tma_eligible(M, N, K, nullptr, nullptr, nullptr, h->sgemm_ksplit_forced > 1)) return B2B_OK;
+    int S = h->sgemm_ksplit_forced > 0 ? h->sgemm_ksplit_forced : sgemm_ksplit(h->sm_count, M, N, K);
+    const int64_t kt = (K + 31) / 32;
+    if (S > kt) S = static_cast<int>(kt);
+    *splits = S < 1 ? 1 : S;
+    return B2B_OK;
+}
+
+int b2b_set_sgemm_splits(b2b_handle *h, int splits) {
+    if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_set_sgemm_splits: NULL handle");
+    if (splits < 0 || splits > 64) return fail(B2B_ERR_INVALID_ARG, "b2b_set_sgemm_splits: splits must be 0..64");
+    h->sgemm_ksplit_forced = splits;
+    return B2B_OK;
+}
+
 int b2b_sgemm_bias(b2b_handle *h, int algo, size_t m, size_t n, size_t k, float alpha, const float *A,
                    const float *B, float beta, float *C, const float *bias, int relu) {
     if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_sgemm_bias: NULL handle");

@@ -664,7 +664,10 @@ int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float
     // arithmetic, 10% faster at 8192^3), packed FFMA2 on row pairs by default;
     // variants 20/21/22 force its scalar / row-pair / column-pair forms and
     // variant 11 the cp.async kernel below.
-    if ((variant == 0 || (variant >= 20 && variant <= 22)) && batch == 1 && b2b::sgemm_tma_eligible(M, N, K, A, B, C))
+    // A forced split-K (the tiles of a split host-slice call) must take this
+    // kernel whatever the tile's size.
+    if ((variant == 0 || (variant >= 20 && variant <= 22)) && batch == 1 &&
+        b2b::sgemm_tma_eligible(M, N, K, A, B, C, h->sgemm_ksplit_forced > 1))
         return b2b::launch_sgemm_tma(h, M, N, K, alpha, beta, A, B, C, epi.bias, epi.relu,
                                      variant == 0 ? 1 : variant - 20);
     // Batched calls (and variant 23): the TMA-fed kernel on row-major A (no

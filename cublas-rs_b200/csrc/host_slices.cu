@@ -261,6 +261,19 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     return finish(h);
 }
 
+// Sets the handle's forced SGEMM split-K factor for its lifetime (unless an
+// environment override already forces one), then restores it.
+struct ForcedKsplit {
+    b2b_handle *h;
+    int saved;
+    ForcedKsplit(b2b_handle *hh, int S) : h(hh), saved(hh ? hh->sgemm_ksplit_forced : 0) {
+        if (h && saved == 0) h->sgemm_ksplit_forced = S;
+    }
+    ~ForcedKsplit() {
+        if (h) h->sgemm_ksplit_forced = saved;
+    }
+};
+
 int h2d(b2b_handle *h, void *d, const void *s, size_t bytes) {
     if (!bytes) return B2B_OK;
     cudaError_t e = cudaMemcpyAsync(d, s, bytes, cudaMemcpyHostToDevice, h->stream);
@@ -281,6 +294,16 @@ int b2b_sgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t k, floa
                      size_t a_len, const float *B, size_t b_len, float beta, float *C, size_t c_len) {
     if (algo < B2B_ALGO_DEFAULT || algo > B2B_ALGO_3XTF32)
         return fail(B2B_ERR_INVALID_ARG, "b2b_sgemm_simple: unknown algo " + std::to_string(algo));
+    // The tiles of a pipelined call sum the k ranges that the device call on
+    // the whole (16-byte aligned) GEMM would: its split-K factor, computed
+    // once here, is forced on every tile, so the result has the device call's
+    // bits however the output is tiled.
+    ForcedKsplit fk(h, h && algo != B2B_ALGO_3XTF32 && m && n && k &&
+                               sgemm_tma_eligible(static_cast<int64_t>(m), static_cast<int64_t>(n),
+                                                  static_cast<int64_t>(k), nullptr, nullptr, nullptr)
+                           ? sgemm_ksplit(h->sm_count, static_cast<int64_t>(m), static_cast<int64_t>(n),
+                                          static_cast<int64_t>(k))
+                           : 1);
     return gemm_simple<float, float>(
         h, "b2b_sgemm_simple", m, n, k, alpha, A, a_len, B, b_len, beta, C, c_len,
         [algo](b2b_handle *hh, size_t mm, size_t nn, size_t kk, float al, const float *a, const float *b, float be,

@@ -64,6 +64,10 @@ struct b2b_handle {
     // SGEMM kernel configuration (B2B_SGEMM_VARIANT; 0 = the default).
     int sgemm_variant = 0;
     int sgemm_group_m = 0;              // TMA-fed SGEMM raster group override (B2B_SGEMM_GROUP_M; 0 = default)
+    // TMA-fed SGEMM split-K factor for the next launches (0 = chosen per call;
+    // set by host-slice calls so that their tiles share the whole GEMM's k
+    // ranges; B2B_SGEMM_KSPLIT sets it for every call, 1 turns split-K off).
+    int sgemm_ksplit_forced = 0;
     int hgemm_variant = 0;              // 0 auto, 1 single CTA, 2 pair 256x256, 3 pair 256x512
     int hgemm_group_m = 0;              // pair kernels' raster group override (0 = default)
     int64_t gemv_seg_bytes = 16384;     // GEMV-N row segment size (B2B_GEMV_SEG_KB)
@@ -127,7 +131,9 @@ int launch_hgemm(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const
 int launch_sgemm_3xtf32(b2b_handle *h, size_t m, size_t n, size_t k, float alpha, const float *A,
                         const float *B, float beta, float *C);
 bool dgemm_dmma_eligible(int64_t N, int64_t K, const void *A, const void *B, const void *C);
-bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C);
+bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C,
+                        bool any_size = false);
+int sgemm_ksplit(int sm_count, int64_t M, int64_t N, int64_t K);
 int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
                      const float *B, float *C, const float *bias, int relu, int pack);
 // The TMA-fed FFMA kernel reading row-major A directly (no transpose pass),

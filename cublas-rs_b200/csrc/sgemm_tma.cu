@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cmath>
 #include <mutex>
 
 #include "internal.h"
@@ -64,6 +65,12 @@ struct SArgs {
     int *status;
     uint64_t wait_ns;
     int group_m;  // raster group in M tiles
+    // Split-K: with ksplit > 1, CTA (split s, tile t) sums k-blocks
+    // [s * kb_per_split, (s + 1) * kb_per_split) and stores its raw sums to
+    // partial[s][M][N]; sgemm_splitk_reduce_kernel finishes the outputs.
+    int ksplit;
+    int64_t kb_per_split;
+    float *partial;
 };
 
 // kPack selects the FFMA form of the 16 x 8 outer product (each output is
@@ -92,8 +99,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t tiles_m = (args.M + kBM - 1) / kBM, tiles_n = (args.N + kBN - 1) / kBN;
-    // grouped raster
-    const int64_t t = blockIdx.x;
+    const int64_t ntiles = tiles_m * tiles_n;
+    // split (k range) and tile of this CTA; grouped raster within a split
+    const int64_t split = args.ksplit > 1 ? static_cast<int64_t>(blockIdx.x) / ntiles : 0;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) - split * ntiles;
     const int64_t group_m = args.group_m;
     const int64_t span = group_m * tiles_n;
     const int64_t g = t / span;
@@ -101,7 +110,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t gm = tiles_m - first < group_m ? tiles_m - first : group_m;
     const int64_t r = t - g * span;
     const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * kBN;
-    const int64_t ktiles = (args.K + kBK - 1) / kBK;
+    const int64_t ktiles_all = (args.K + kBK - 1) / kBK;
+    // this CTA's k-blocks: kb0 + [0, ktiles)
+    const int64_t kb0 = args.ksplit > 1 ? split * args.kb_per_split : 0;
+    const int64_t ktiles = args.ksplit > 1
+                               ? (ktiles_all - kb0 < args.kb_per_split ? ktiles_all - kb0 : args.kb_per_split)
+                               : ktiles_all;
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -119,9 +133,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int64_t issued = 0;  // k-blocks whose loads warp 0's lane 0 has issued
     auto issue = [&](int64_t kt) {
         const int s = static_cast<int>(kt % kStages);
+        const int32_t kc = static_cast<int32_t>((kb0 + kt) * kBK);
         mbar_arrive_expect_tx(&full[s], kStageBytes);
-        tma_load_2d(As + s * kAStageF, &tmAt, &full[s], static_cast<int32_t>(m0), static_cast<int32_t>(kt * kBK));
-        tma_load_2d(Bs + s * kBStageF, &tmB, &full[s], static_cast<int32_t>(n0), static_cast<int32_t>(kt * kBK));
+        tma_load_2d(As + s * kAStageF, &tmAt, &full[s], static_cast<int32_t>(m0), kc);
+        tma_load_2d(Bs + s * kBStageF, &tmB, &full[s], static_cast<int32_t>(n0), kc);
         ++issued;
     };
     if (loader)
@@ -237,6 +252,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         return;
     }
 
+    if (args.ksplit > 1) {
+        // raw sums of this k range; the reduce applies alpha, beta, bias, ReLU
+        float *P = args.partial + split * args.M * args.N;
+#pragma unroll
+        for (int gi = 0; gi < kTM / 4; ++gi) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int64_t row = m0 + row_base + gi * 16 + i;
+                if (row >= args.M) continue;
+#pragma unroll
+                for (int gj = 0; gj < kTN / 4; ++gj) {
+                    const int64_t col = n0 + col_base + gj * 32;
+                    if (col >= args.N) continue;
+                    *reinterpret_cast<float4 *>(P + row * args.N + col) =
+                        make_float4(acc_at(gi * 4 + i, gj * 4 + 0), acc_at(gi * 4 + i, gj * 4 + 1),
+                                    acc_at(gi * 4 + i, gj * 4 + 2), acc_at(gi * 4 + i, gj * 4 + 3));
+                }
+            }
+        }
+        return;
+    }
     const bool read_c = args.beta != 0.0f;
 #pragma unroll
     for (int gi = 0; gi < kTM / 4; ++gi) {
@@ -490,6 +526,43 @@ __global__ void __launch_bounds__(RowaCfg<WN>::THREADS, RowaCfg<WN>::MIN_BLOCKS)
     }
 }
 
+// Split-K finish: C = alpha * (P_0 + P_1 + ... + P_{S-1}) (+ beta * C, + bias,
+// ReLU), the partial sums added in split order -- the same bits on every run
+// and for every tiling of the output.  4 elements per thread (N % 4 == 0).
+__global__ void __launch_bounds__(256) sgemm_splitk_reduce_kernel(const float *__restrict__ P, int S, int64_t M,
+                                                                  int64_t N, float *__restrict__ C, float alpha,
+                                                                  float beta, const float *__restrict__ bias, int relu) {
+    const int64_t MN = M * N;
+    for (int64_t q = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; q < MN;
+         q += static_cast<int64_t>(gridDim.x) * blockDim.x * 4) {
+        float4 s = *reinterpret_cast<const float4 *>(P + q);
+        for (int i = 1; i < S; ++i) {
+            const float4 v = *reinterpret_cast<const float4 *>(P + i * MN + q);
+            s.x += v.x;
+            s.y += v.y;
+            s.z += v.z;
+            s.w += v.w;
+        }
+        float o[4] = {alpha * s.x, alpha * s.y, alpha * s.z, alpha * s.w};
+        if (beta != 0.0f) {
+            const float4 old = *reinterpret_cast<const float4 *>(C + q);
+            o[0] = fmaf(beta, old.x, o[0]);
+            o[1] = fmaf(beta, old.y, o[1]);
+            o[2] = fmaf(beta, old.z, o[2]);
+            o[3] = fmaf(beta, old.w, o[3]);
+        }
+        if (bias || relu) {
+            const int64_t col = q % N;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (bias) o[e] += bias[col + e];
+                if (relu) o[e] = o[e] > 0.0f ? o[e] : 0.0f;
+            }
+        }
+        *reinterpret_cast<float4 *>(C + q) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
+
 // At[k][m] = A[m][k]: 32 x 32 tiles through shared memory (padded row).
 __global__ void __launch_bounds__(256) transpose_f32_kernel(const float *__restrict__ A, float *__restrict__ At,
                                                             int64_t M, int64_t K) {
@@ -513,20 +586,66 @@ __global__ void __launch_bounds__(256) transpose_f32_kernel(const float *__restr
 
 namespace b2b {
 
-bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C) {
-    // N >= 1024 keeps the transpose below ~3.5% of the GEMM's time.
-    return M % 4 == 0 && N % 4 == 0 && aligned16(A) && aligned16(B) && aligned16(C) && M >= kBM && N >= 1024 &&
-           K >= kBK && (K + kBK - 1) / kBK < (int64_t(1) << 30) && M < (int64_t(1) << 31) &&
-           N < (int64_t(1) << 31) && K < (int64_t(1) << 31) && K <= 65535LL * 32;
+bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C,
+                        bool any_size) {
+    // N >= 1024 keeps the transpose below ~3.5% of the GEMM's time; any_size
+    // drops that preference (and M >= 128) for calls that must take this
+    // kernel (the tiles of a split host-slice call).
+    return M % 4 == 0 && N % 4 == 0 && aligned16(A) && aligned16(B) && aligned16(C) &&
+           (any_size || (M >= kBM && N >= 1024)) && K >= kBK && (K + kBK - 1) / kBK < (int64_t(1) << 30) &&
+           M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31) && K <= 65535LL * 32;
+}
+
+// Split-K factor for an M x N x K SGEMM on the TMA-fed kernel: the S in
+// {1, 2, 3, 4, 6, 8} with the least estimated time, where the GEMM costs
+// waves x k-blocks per CTA (a 128 x 256 x 32 k-block takes ~5.2 us at the
+// kernel's FFMA rate) and a split adds its partial sums' HBM round trip
+// (8 S M N bytes at ~6 TB/s) plus a launch.  Each split keeps at least 8
+// k-blocks.  Taken only when it saves 10% or more: grids under one wave
+// (1024^3: 32 tiles, S = 4) and wave counts just past a whole number
+// (4096^3: 3.46 waves, S = 2).
+int sgemm_ksplit(int sm_count, int64_t M, int64_t N, int64_t K) {
+    const double tiles = static_cast<double>(((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN));
+    const int64_t kt = (K + kBK - 1) / kBK;
+    const double kb_us = 5.2;
+    auto est = [&](int S) {
+        const double waves = std::ceil(tiles * S / sm_count);
+        const double kbs = static_cast<double>((kt + S - 1) / S);
+        double t = waves * kbs * kb_us;
+        if (S > 1) t += 8.0 * S * static_cast<double>(M) * static_cast<double>(N) / 6e12 * 1e6 + 4.0;
+        return t;
+    };
+    const double t1 = est(1);
+    int best = 1;
+    double tb = t1;
+    for (int S : {2, 3, 4, 6, 8}) {
+        if ((kt + S - 1) / S < 8) break;
+        const double t = est(S);
+        if (t < tb) {
+            tb = t;
+            best = S;
+        }
+    }
+    return tb <= 0.9 * t1 ? best : 1;
 }
 
 int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
                      const float *B, float *C, const float *bias, int relu, int pack) {
     const int pk = pack == 1 || pack == 2 ? pack : 0;
     auto kern = pk == 1 ? sgemm_tma_kernel<1> : pk == 2 ? sgemm_tma_kernel<2> : sgemm_tma_kernel<0>;
+    // The split: forced by the caller (a host-slice call's tiles take the
+    // whole GEMM's, so every tile sums the same k ranges), else chosen here.
+    const int64_t ktiles = (K + kBK - 1) / kBK;
+    int S = h->sgemm_ksplit_forced > 0 ? h->sgemm_ksplit_forced : sgemm_ksplit(h->sm_count, M, N, K);
+    if (S > ktiles) S = static_cast<int>(ktiles);
+    if (S < 1) S = 1;
+    const int64_t kbps = (ktiles + S - 1) / S;
+    const size_t at_bytes = (static_cast<size_t>(M) * static_cast<size_t>(K) * 4 + 255) / 256 * 256;
+    const size_t part_bytes = S > 1 ? static_cast<size_t>(S) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4 : 0;
     void *ws = nullptr;
-    if (int rc = workspace(h, static_cast<size_t>(M) * static_cast<size_t>(K) * 4, &ws)) return rc;
+    if (int rc = workspace(h, at_bytes + part_bytes, &ws)) return rc;
     float *At = static_cast<float *>(ws);
+    float *partial = S > 1 ? reinterpret_cast<float *>(static_cast<char *>(ws) + at_bytes) : nullptr;
     const dim3 tgrid(static_cast<unsigned>((M + 31) / 32), static_cast<unsigned>((K + 31) / 32));
     transpose_f32_kernel<<<tgrid, 256, 0, h->stream>>>(A, At, M, K);
     cudaError_t e = cudaGetLastError();
@@ -549,12 +668,23 @@ int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha
         }
     }
     const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-    if (tiles > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
+    if (tiles * S > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
     SArgs args{C, M, N, K, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns,
-               h->sgemm_group_m > 0 ? h->sgemm_group_m : kGroupM};
-    kern<<<static_cast<unsigned>(tiles), kThreads, kSmem, h->stream>>>(tmAt, tmB, args);
+               h->sgemm_group_m > 0 ? h->sgemm_group_m : kGroupM, S, kbps, partial};
+    kern<<<static_cast<unsigned>(tiles * S), kThreads, kSmem, h->stream>>>(tmAt, tmB, args);
     e = cudaGetLastError();
-    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm TMA launch");
+    if (e != cudaSuccess) return fail_cuda(e, "sgemm TMA launch");
+    if (S > 1) {
+        const int64_t quads = M * N / 4;
+        int64_t blocks = (quads + 255) / 256;
+        const int64_t cap = 8LL * h->sm_count;
+        if (blocks > cap) blocks = cap;
+        sgemm_splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, h->stream>>>(partial, S, M, N, C, alpha,
+                                                                                          beta, bias, relu);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fail_cuda(e, "sgemm split-K reduce launch");
+    }
+    return B2B_OK;
 }
 
 bool sgemm_tma_rowa_eligible(int64_t M, int64_t N, int64_t K, int64_t sA, int64_t sB, int64_t sC, int64_t batch,

@@ -64,6 +64,8 @@ extern "C" {
     pub fn b2b_sgemm_bias(h: *mut b2b_handle, algo: c_int, m: usize, n: usize, k: usize, alpha: f32,
                           a: *const f32, b: *const f32, beta: f32, c: *mut f32, bias: *const f32,
                           relu: c_int) -> c_int;
+    pub fn b2b_sgemm_splits(h: *mut b2b_handle, m: usize, n: usize, k: usize, splits: *mut c_int) -> c_int;
+    pub fn b2b_set_sgemm_splits(h: *mut b2b_handle, splits: c_int) -> c_int;
     pub fn b2b_dgemm(h: *mut b2b_handle, algo: c_int, m: usize, n: usize, k: usize, alpha: f64,
                      a: *const f64, b: *const f64, beta: f64, c: *mut f64) -> c_int;
     pub fn b2b_dgemm_simple(h: *mut b2b_handle, algo: c_int, m: usize, n: usize, k: usize, alpha: f64,

@@ -140,6 +140,21 @@ B2B_API int b2b_sgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t
 B2B_API int b2b_sgemm_bias(b2b_handle *h, int algo, size_t m, size_t n, size_t k, float alpha, const float *A,
                            const float *B, float beta, float *C, const float *bias, int relu);
 
+/* Split-K of the FP32 FFMA SGEMM; no counterpart in the reference (its
+ * kernels have no K split).  A GEMM whose output tiles fill the GPU badly
+ * (under one wave of 128 x 256 tiles, or just past a whole number of waves)
+ * is computed as S independent k ranges whose raw sums are added in range
+ * order by a second kernel; the result is deterministic, but its bits depend
+ * on S.  b2b_sgemm_splits returns the S that b2b_sgemm / b2b_sgemm_bias
+ * (default algo, 16-byte aligned operands) choose for an m x n x k call;
+ * b2b_set_sgemm_splits fixes S for the handle's later calls: 0 = choose per
+ * call (the default), 1 = never split, S > 1 = always S where the TMA-fed
+ * kernel takes the call.  A caller that computes one GEMM as several row or
+ * column pieces gets the whole GEMM's bits by fixing the whole GEMM's S for
+ * the pieces (the host-slice calls do this themselves). */
+B2B_API int b2b_sgemm_splits(b2b_handle *h, size_t m, size_t n, size_t k, int *splits);
+B2B_API int b2b_set_sgemm_splits(b2b_handle *h, int splits);
+
 /* ------------------------------------------------------ Level 3: DGEMM */
 
 /* Handle::dgemm_* (lib.rs:527-612) -> crates/cublas-l3/src/dgemm.rs:342-569. */

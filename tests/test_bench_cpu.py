@@ -49,8 +49,18 @@ def test_sgemm_kernels_per_call(monkeypatch):
     import bench
 
     monkeypatch.delenv("B2B_SGEMM_VARIANT", raising=False)
+    monkeypatch.delenv("B2B_SGEMM_KSPLIT", raising=False)
     assert bench.sgemm_kernels_per_call(8192, 8192, 8192) == 2
     assert bench.sgemm_kernels_per_call(4096, 1024, 4096) == 2
+    # split-K adds the reduce: grids under one wave, or just past a whole one
+    assert bench.sgemm_ksplit(148, 1024, 1024, 1024) == 4
+    assert bench.sgemm_ksplit(148, 4096, 4096, 4096) == 2
+    assert bench.sgemm_ksplit(148, 8192, 8192, 8192) == 1
+    assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 3
+    assert bench.sgemm_kernels_per_call(2048, 1024, 4096) == 3
+    monkeypatch.setenv("B2B_SGEMM_KSPLIT", "1")
+    assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 2
+    monkeypatch.delenv("B2B_SGEMM_KSPLIT")
     assert bench.sgemm_kernels_per_call(512, 512, 512) == 1        # N < 1024
     assert bench.sgemm_kernels_per_call(100, 2048, 64) == 1        # M < 128
     assert bench.sgemm_kernels_per_call(8192, 8192, 8192, tf32x3=True) == 1

@@ -375,9 +375,11 @@ def test_sgemm_ffma_kernels_bit_identical(monkeypatch, oracle, m, n, k, alpha, b
     # step, so the forms must agree bit for bit: the cp.async kernel (variant
     # 11), the TMA-fed kernel on a transposed A with scalar FFMA (20), FFMA2
     # on row pairs (21, the default), FFMA2 on column pairs (22), and the
-    # TMA-fed kernel on row-major A (23).
+    # TMA-fed kernel on row-major A (23).  Split-K is off here (it sums k
+    # ranges separately, so a split call has other bits by design).
     import b2blas
 
+    monkeypatch.setenv("B2B_SGEMM_KSPLIT", "1")
     A = oracle.uniform_f32(m * k, 21, 1)
     B = oracle.uniform_f32(k * n, 21, 2)
     C = oracle.uniform_f32(m * n, 21, 3)
@@ -498,3 +500,114 @@ def test_strided_batched_simple_pipelined_shared_a(monkeypatch, oracle):
         assert np.array_equal(host, want), mode
     ref = oracle.sgemm_strided_batched_f64(m, n, k, 1.0, A, 0, B[:2 * k * n], k * n, 0.5, C[:2 * m * n], m * n, 2)
     assert oracle.rel_err(want[:2 * m * n], ref) <= oracle.tol_normwise(k, "f32")
+
+
+@pytest.mark.parametrize("m,n,k,ks", [(1024, 1024, 1024, None), (1000, 1024, 1000, "3"), (4096, 1028, 512, "2"),
+                                      (256, 2048, 4096, "8"), (128, 1024, 300, "2")])
+@pytest.mark.parametrize("beta", [0.0, 0.5])
+def test_sgemm_split_k(oracle, monkeypatch, m, n, k, ks, beta):
+    # Split-K on the TMA-fed SGEMM (chosen for 1024^3: 32 tiles under one
+    # wave; forced through B2B_SGEMM_KSPLIT for the others, including a K
+    # whose last range is short): raw sums per k range in workspace, then a
+    # fixed-order reduce applying alpha, beta, bias and ReLU.  Within the
+    # FP32 bound of the FP64 evaluation; the same bits on a second call; the
+    # bias + ReLU epilogue equals sgemm followed by the bias and ReLU on the
+    # host (both round alpha*sum + beta*c the same way before adding bias).
+    import b2blas
+
+    if ks is None:
+        monkeypatch.delenv("B2B_SGEMM_KSPLIT", raising=False)
+    else:
+        monkeypatch.setenv("B2B_SGEMM_KSPLIT", ks)
+    A = oracle.uniform_f32(m * k, 31, 1)
+    B = oracle.uniform_f32(k * n, 31, 2)
+    C = oracle.uniform_f32(m * n, 31, 3)
+    bias = oracle.uniform_f32(n, 31, 5)
+    h = b2blas.Handle(0)
+    try:
+        cfg = b2blas.GemmConfig(m, n, k, 1.5, beta)
+        a, b = h.upload(A), h.upload(B)
+        outs = []
+        for _ in range(2):
+            c = h.upload(C)
+            h.sgemm(cfg, a, b, c)
+            h.synchronize()
+            outs.append(h.download(c))
+        assert np.array_equal(outs[0], outs[1])
+        ref = oracle.sgemm_f64(m, n, k, 1.5, A, B, beta, C)
+        assert oracle.rel_err(outs[0], ref) <= oracle.tol_normwise(k, "f32")
+        c, bd = h.upload(C), h.upload(bias)
+        h.sgemm_bias(cfg, a, b, c, bias=bd, relu=True)
+        h.synchronize()
+        fused = h.download(c)
+        expect = np.maximum(outs[0].reshape(m, n) + bias[None, :], np.float32(0)).ravel()
+        assert np.array_equal(fused, expect.astype(np.float32))
+    finally:
+        h.close()
+
+
+def test_sgemm_split_k_simple_matches_device_bits(oracle):
+    # 4096^3 splits in two (512 tiles are 3.46 waves on 148 SMs).  The
+    # pipelined host-slice call computes 512 x 2048 tiles, each far under a
+    # wave; it forces the whole GEMM's split on every tile, so every output
+    # sums the same k ranges in the same order: the device call's bits.
+    import b2blas
+
+    m = n = k = 4096
+    A = oracle.uniform_f32(m * k, 32, 1)
+    B = oracle.uniform_f32(k * n, 32, 2)
+    C = oracle.uniform_f32(m * n, 32, 3)
+    h = b2blas.Handle(0)
+    try:
+        cfg = b2blas.GemmConfig(m, n, k, 1.25, -0.5)
+        host = C.copy()
+        h.sgemm_simple(cfg, A, B, host)
+        a, b, c = h.upload(A), h.upload(B), h.upload(C)
+        h.sgemm(cfg, a, b, c)
+        h.synchronize()
+        dev = h.download(c)
+        assert np.array_equal(dev, host)
+        for r in (0, 2049, m - 1):
+            ref = oracle.sgemm_f64(m, n, k, 1.25, A, B, -0.5, C, row0=r, nrows=1)
+            assert oracle.rel_err(np.ascontiguousarray(host.reshape(m, n)[r]), ref) <= oracle.tol_normwise(k, "f32")
+    finally:
+        h.close()
+
+
+def test_sgemm_splits_query_and_row_pieces_reproduce_whole(oracle):
+    # b2b_sgemm_splits reports the split the device call takes; fixing the
+    # whole GEMM's split with b2b_set_sgemm_splits makes two row halves,
+    # computed as separate calls, reproduce the whole call's bits (without
+    # it each half, a different shape, may split differently).
+    import b2blas
+
+    h = b2blas.Handle(0)
+    try:
+        assert h.sgemm_splits(1024, 1024, 1024) == 4
+        assert h.sgemm_splits(8192, 8192, 8192) == 1
+        assert h.sgemm_splits(512, 512, 512) == 1  # the cp.async kernel's shape: no split
+        m, n, k = 4096, 1024, 4096
+        whole = h.sgemm_splits(m, n, k)
+        A = oracle.uniform_f32(m * k, 33, 1)
+        B = oracle.uniform_f32(k * n, 33, 2)
+        a, b, c = h.upload(A), h.upload(B), h.upload(np.zeros(m * n, np.float32))
+        h.sgemm(b2blas.GemmConfig(m, n, k, 1.0, 0.0), a, b, c)
+        h.synchronize()
+        ref = h.download(c)
+        half = m // 2
+        assert h.sgemm_splits(half, n, k) != whole  # the halves alone would split otherwise
+        h.set_sgemm_splits(whole)
+        assert h.sgemm_splits(half, n, k) == whole
+        outs = []
+        for r0 in (0, half):
+            ah = b2blas.DeviceBuffer.from_ptr(h, a.ptr + 4 * r0 * k, half * k, np.float32)
+            ch = h.upload(np.zeros(half * n, np.float32))
+            h.sgemm(b2blas.GemmConfig(half, n, k, 1.0, 0.0), ah, b, ch)
+            h.synchronize()
+            outs.append(h.download(ch))
+        h.set_sgemm_splits(0)
+        assert np.array_equal(np.concatenate(outs), ref)
+        with pytest.raises(b2blas.CublasError):
+            h.set_sgemm_splits(-1)
+    finally:
+        h.close()

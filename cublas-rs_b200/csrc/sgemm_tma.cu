@@ -344,9 +344,26 @@ struct RArgs {
     int relu;
     int *status;
     uint64_t wait_ns;
+    int64_t tiles;  // tiles of the whole call (persistent form)
 };
 
-template <int WN>
+// (batch, first row, first column) of tile t: batches in order, each
+// batch's tiles raster-grouped by kGroupM tile rows.
+__device__ __forceinline__ void rowa_tile(const RArgs &args, int64_t t, int bn, int64_t &batch, int64_t &m0,
+                                          int64_t &n0) {
+    const int64_t per_batch = args.tiles_m * args.tiles_n;
+    batch = t / per_batch;
+    const int64_t tb = t - batch * per_batch;
+    const int64_t span = kGroupM * args.tiles_n;
+    const int64_t g = tb / span;
+    const int64_t first = g * kGroupM;
+    const int64_t gm = args.tiles_m - first < kGroupM ? args.tiles_m - first : kGroupM;
+    const int64_t r = tb - g * span;
+    m0 = (first + r % gm) * kBM;
+    n0 = (r / gm) * bn;
+}
+
+template <int WN, bool XP>
 struct RowaCfg {
     static constexpr int BN = WN * (kTN / 4) * 32;  // 256 or 128
     static constexpr int WARPS = kWM * WN;
@@ -355,38 +372,62 @@ struct RowaCfg {
     static constexpr int MIN_BLOCKS = WN == 4 ? 1 : 2;
     static constexpr int B_STAGE_F = kBK * BN;
     static constexpr uint32_t STAGE_BYTES = (kAStageF + B_STAGE_F) * 4;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int XPOSE_BYTES = XP ? 2 * kAStageF * 4 : 0;  // two transposed A tiles
+    static constexpr int SMEM = STAGES * STAGE_BYTES + XPOSE_BYTES + 1024 + 256;
+    static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-template <int WN>
-__global__ void __launch_bounds__(RowaCfg<WN>::THREADS, RowaCfg<WN>::MIN_BLOCKS)
+// Barrier 1 over `threads` threads that returns whether `pred` held in all of
+// them (bar.red.and): every thread reaches it each k-block, failed waits
+// included, so no warp can be left waiting on warps that gave up.
+__device__ __forceinline__ bool bar1_and(bool pred, int threads) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(out)
+        : "r"(pred ? 1u : 0u), "r"(threads)
+        : "memory");
+    return out != 0;
+}
+
+// XP = true: the warps transpose each landed A tile into At_s[k][m] (two
+// buffers, alternating by k-block) before the FFMA loop reads it, so A
+// fragments are 16-byte loads of four rows as in sgemm_tma_kernel instead of
+// four 4-byte loads; one barrier per k-block separates the transpose from
+// the reads.  MULTI = true (with XP): persistent, CTA b takes tiles b,
+// b + gridDim.x, ...; the k-blocks of all its tiles form one load stream
+// through the stage ring, so the next tile's first loads are in flight while
+// the warps finish and store the current one; the loader's position lives in
+// shared memory.  Same per-element arithmetic (and bits) in every form.
+template <int WN, bool XP, bool MULTI>
+__global__ void __launch_bounds__(RowaCfg<WN, XP>::THREADS, RowaCfg<WN, XP>::MIN_BLOCKS)
     sgemm_tma_rowa_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           RArgs args) {
     using namespace sm100;
-    using Cf = RowaCfg<WN>;
+    using Cf = RowaCfg<WN, XP>;
     constexpr int S = Cf::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
     float *As = reinterpret_cast<float *>(smem);  // stages of [128 m][32 k], swizzled
     float *Bs = As + S * kAStageF;                // stages of [32 k][BN n]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cf::STAGE_BYTES);
+    float *At_s = reinterpret_cast<float *>(smem + S * Cf::STAGE_BYTES);  // XP: 2 x [32 k][128 m]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cf::STAGE_BYTES + Cf::XPOSE_BYTES);
     uint64_t *full = bars;
     uint64_t *empty = bars + S;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * S);
+    // loader position (MULTI): tile of this CTA, k-block, batch, m0, n0
+    int *ld = reinterpret_cast<int *>(bars + 2 * S + 1);
+    static_assert(!MULTI || XP, "the persistent form is built on the transposing one");
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t per_batch = args.tiles_m * args.tiles_n;
-    const int64_t t = blockIdx.x;
-    const int64_t batch = t / per_batch;
-    const int64_t tb = t - batch * per_batch;
-    const int64_t span = kGroupM * args.tiles_n;
-    const int64_t g = tb / span;
-    const int64_t first = g * kGroupM;
-    const int64_t gm = args.tiles_m - first < kGroupM ? args.tiles_m - first : kGroupM;
-    const int64_t r = tb - g * span;
-    const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * Cf::BN;
+    int64_t batch, m0, n0;
+    rowa_tile(args, blockIdx.x, Cf::BN, batch, m0, n0);
     const int64_t ktiles = (args.K + kBK - 1) / kBK;
+    // this CTA's tiles and its whole k-block stream
+    const int64_t ntiles = MULTI ? (args.tiles - static_cast<int64_t>(blockIdx.x) + gridDim.x - 1) / gridDim.x : 1;
+    const int64_t total = ntiles * ktiles;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -397,26 +438,55 @@ __global__ void __launch_bounds__(RowaCfg<WN>::THREADS, RowaCfg<WN>::MIN_BLOCKS)
         fence_barrier_init();
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
+        ld[0] = 0;
+        ld[1] = 0;
+        ld[2] = static_cast<int>(batch);
+        ld[3] = static_cast<int>(m0);
+        ld[4] = static_cast<int>(n0);
     }
     __syncthreads();
 
     const bool loader = tid == 0;
     int64_t issued = 0;
-    auto issue = [&](int64_t kt) {
-        const int s = static_cast<int>(kt % S);
+    // Loads k-block `issued` of the stream (MULTI: the loader's position in
+    // shared memory names its tile) into stage issued % S.
+    auto issue = [&]() {
+        const int s = static_cast<int>(issued % S);
         mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
-        tma_load_3d(As + s * kAStageF, &tmA, &full[s], static_cast<int32_t>(kt * kBK), static_cast<int32_t>(m0),
-                    static_cast<int32_t>(batch));
-        tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], static_cast<int32_t>(n0), static_cast<int32_t>(kt * kBK),
-                    static_cast<int32_t>(batch));
+        if constexpr (MULTI) {
+            const int kt = ld[1];
+            tma_load_3d(As + s * kAStageF, &tmA, &full[s], kt * kBK, ld[3], ld[2]);
+            tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], ld[4], kt * kBK, ld[2]);
+            if (kt + 1 == ktiles) {
+                const int i = ld[0] + 1;
+                if (i < ntiles) {
+                    int64_t b1, mm, nn;
+                    rowa_tile(args, blockIdx.x + static_cast<int64_t>(i) * gridDim.x, Cf::BN, b1, mm, nn);
+                    ld[2] = static_cast<int>(b1);
+                    ld[3] = static_cast<int>(mm);
+                    ld[4] = static_cast<int>(nn);
+                }
+                ld[0] = i;
+                ld[1] = 0;
+            } else {
+                ld[1] = kt + 1;
+            }
+        } else {
+            const int64_t kt = issued;
+            tma_load_3d(As + s * kAStageF, &tmA, &full[s], static_cast<int32_t>(kt * kBK), static_cast<int32_t>(m0),
+                        static_cast<int32_t>(batch));
+            tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], static_cast<int32_t>(n0),
+                        static_cast<int32_t>(kt * kBK), static_cast<int32_t>(batch));
+        }
         ++issued;
     };
     if (loader)
-        for (int64_t kt = 0; kt < S && kt < ktiles; ++kt) issue(kt);
+        for (int64_t q = 0; q < S && q < total; ++q) issue();
 
     const int wm = warp / WN, wn = warp % WN;
     const int ty = lane >> 3, tx = lane & 7;
-    const int row0 = wm * (kTM / 4) * 16 + ty;  // this thread's rows: row0 + 4i
+    const int row0 = wm * (kTM / 4) * 16 + ty;  // this thread's rows: row0 + 4i (XP: row_base + 16q + j)
+    const int row_base = wm * (kTM / 4) * 16 + ty * 4;
     const int col_base = wn * (kTN / 4) * 32 + tx * 4;
     // Swizzle of row r = row0 + 4i: (r % 8) = ty + 4 (i & 1); float k of that
     // row sits at r*32 + (k ^ (4 (r % 8))).
@@ -430,10 +500,21 @@ __global__ void __launch_bounds__(RowaCfg<WN>::THREADS, RowaCfg<WN>::MIN_BLOCKS)
     auto acc_at = [&](int i, int j) -> float & { return (i & 1) ? acc2[i >> 1][j].y : acc2[i >> 1][j].x; };
 
     auto load_frags = [&](const float *as, const float *bs, int kk, float (&af)[kTM], float (&bf)[kTN]) {
-        const float *ae = as + row0 * 32 + (kk ^ swz_even);
-        const float *ao = as + row0 * 32 + (kk ^ swz_odd);
+        if constexpr (XP) {
 #pragma unroll
-        for (int i = 0; i < kTM; ++i) af[i] = (i & 1) ? ao[4 * i * 32] : ae[4 * i * 32];
+            for (int q = 0; q < kTM / 4; ++q) {
+                const float4 v = *reinterpret_cast<const float4 *>(as + kk * kBM + row_base + q * 16);
+                af[q * 4 + 0] = v.x;
+                af[q * 4 + 1] = v.y;
+                af[q * 4 + 2] = v.z;
+                af[q * 4 + 3] = v.w;
+            }
+        } else {
+            const float *ae = as + row0 * 32 + (kk ^ swz_even);
+            const float *ao = as + row0 * 32 + (kk ^ swz_odd);
+#pragma unroll
+            for (int i = 0; i < kTM; ++i) af[i] = (i & 1) ? ao[4 * i * 32] : ae[4 * i * 32];
+        }
 #pragma unroll
         for (int q = 0; q < kTN / 4; ++q) {
             const float4 v = *reinterpret_cast<const float4 *>(bs + kk * Cf::BN + col_base + q * 32);
@@ -445,88 +526,131 @@ __global__ void __launch_bounds__(RowaCfg<WN>::THREADS, RowaCfg<WN>::MIN_BLOCKS)
     };
 
     bool ok = true;
-    for (int64_t kt = 0; kt < ktiles; ++kt) {
-        const int s = static_cast<int>(kt % S);
-        const uint32_t ph = static_cast<uint32_t>((kt / S) & 1);
-        const bool w = mbar_wait(&full[s], ph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x34, args.wait_ns);
-        if (!__all_sync(0xffffffffu, w)) {
-            ok = false;
-            break;
+    int64_t gk = 0;  // position in this CTA's k-block stream
+#pragma unroll 1
+    for (int64_t ti = 0; ti < ntiles && ok; ++ti) {
+        if (MULTI && ti > 0) {
+#pragma unroll
+            for (int i = 0; i < kTM / 2; ++i)
+#pragma unroll
+                for (int j = 0; j < kTN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
         }
-        const float *as = As + s * kAStageF;
-        const float *bs = Bs + s * Cf::B_STAGE_F;
-        float af[2][kTM], bf[2][kTN];
-        load_frags(as, bs, 0, af[0], bf[0]);
+        for (int64_t kt = 0; kt < ktiles; ++kt, ++gk) {
+            const int s = static_cast<int>(gk % S);
+            const uint32_t ph = static_cast<uint32_t>((gk / S) & 1);
+            bool w = ok && mbar_wait(&full[s], ph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x34, args.wait_ns);
+            w = __all_sync(0xffffffffu, w);
+            const float *as;
+            if constexpr (XP) {
+                // A tile -> At_s[kt & 1] as [k][m]: thread q of 1024 moves the
+                // 16-byte chunk c = q / 128 (k = 4c..4c+3) of row m = q % 128, so a
+                // warp reads 32 rows (4 wavefronts, the swizzle spreads the chunks)
+                // and writes 32 consecutive m of each k (conflict-free).
+                float *at = At_s + (gk & 1) * kAStageF;
+                if (w) {
+                    const float *src = As + s * kAStageF;
 #pragma unroll
-        for (int kk = 0; kk < kBK; ++kk) {
-            if (kk + 1 < kBK) load_frags(as, bs, kk + 1, af[(kk + 1) & 1], bf[(kk + 1) & 1]);
-            const float *a = af[kk & 1], *b = bf[kk & 1];
-#pragma unroll
-            for (int j = 0; j < kTN; ++j) {
-                const float2 bb = make_float2(b[j], b[j]);
-#pragma unroll
-                for (int p = 0; p < kTM / 2; ++p)
-                    acc2[p][j] = __ffma2_rn(make_float2(a[2 * p], a[2 * p + 1]), bb, acc2[p][j]);
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (loader && kt >= 1) {
-            const int64_t done = kt - 1, next = done + S;
-            if (next < ktiles) {
-                const int ds = static_cast<int>(done % S);
-                const uint32_t dph = static_cast<uint32_t>((done / S) & 1);
-                if (!mbar_wait(&empty[ds], dph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x33, args.wait_ns)) {
+                    for (int r = 0; r < 1024 / Cf::THREADS; ++r) {
+                        const int q = r * Cf::THREADS + tid;
+                        const int m = q & 127, c = q >> 7;
+                        const float4 v = *reinterpret_cast<const float4 *>(src + m * 32 + ((c ^ (m & 7)) << 2));
+                        at[(4 * c + 0) * kBM + m] = v.x;
+                        at[(4 * c + 1) * kBM + m] = v.y;
+                        at[(4 * c + 2) * kBM + m] = v.z;
+                        at[(4 * c + 3) * kBM + m] = v.w;
+                    }
+                }
+                // Every warp's transpose is done (and every warp's wait held)
+                // before any warp reads it; a warp arriving here has also finished
+                // reading the buffer it overwrote, from two k-blocks ago.
+                if (!bar1_and(w, Cf::THREADS)) {
                     ok = false;
-                } else {
-                    issue(next);
+                    break;
+                }
+                as = at;
+            } else {
+                if (!w) {
+                    ok = false;
+                    break;
+                }
+                as = As + s * kAStageF;
+            }
+            const float *bs = Bs + s * Cf::B_STAGE_F;
+            float af[2][kTM], bf[2][kTN];
+            load_frags(as, bs, 0, af[0], bf[0]);
+#pragma unroll
+            for (int kk = 0; kk < kBK; ++kk) {
+                if (kk + 1 < kBK) load_frags(as, bs, kk + 1, af[(kk + 1) & 1], bf[(kk + 1) & 1]);
+                const float *a = af[kk & 1], *b = bf[kk & 1];
+#pragma unroll
+                for (int j = 0; j < kTN; ++j) {
+                    const float2 bb = make_float2(b[j], b[j]);
+#pragma unroll
+                    for (int p = 0; p < kTM / 2; ++p)
+                        acc2[p][j] = __ffma2_rn(make_float2(a[2 * p], a[2 * p + 1]), bb, acc2[p][j]);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (loader && gk >= 1) {
+                const int64_t done = gk - 1, next = done + S;
+                if (next < total) {
+                    const int ds = static_cast<int>(done % S);
+                    const uint32_t dph = static_cast<uint32_t>((done / S) & 1);
+                    if (!mbar_wait(&empty[ds], dph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x33, args.wait_ns)) {
+                        ok = false;
+                    } else {
+                        issue();
+                    }
+                }
+            }
+            if constexpr (XP) {
+                // a failed refill reaches the other warps at the next barrier
+                ok = __all_sync(0xffffffffu, ok);
+            } else if (!__all_sync(0xffffffffu, ok)) {
+                ok = false;
+                break;
+            }
         }
-        if (!__all_sync(0xffffffffu, ok)) {
-            ok = false;
-            break;
-        }
-    }
-    if (!ok) {
-        if (loader && issued) {
-            const int64_t first_pending = issued > S ? issued - S : 0;
-            for (int64_t kt = first_pending; kt < issued; ++kt)
-                mbar_wait_drain(&full[kt % S], static_cast<uint32_t>((kt / S) & 1), 1000000000ull);
-        }
-        return;
-    }
+        if (!ok) break;
 
-    float *Cb = args.C + batch * args.sC;
-    const bool read_c = args.beta != 0.0f;
+        if (MULTI && ti > 0) rowa_tile(args, blockIdx.x + ti * gridDim.x, Cf::BN, batch, m0, n0);
+        float *Cb = args.C + batch * args.sC;
+        const bool read_c = args.beta != 0.0f;
 #pragma unroll
-    for (int i = 0; i < kTM; ++i) {
-        const int64_t row = m0 + row0 + 4 * i;
-        if (row >= args.M) continue;
-        float *crow = Cb + row * args.N;
+        for (int i = 0; i < kTM; ++i) {
+            const int64_t row = m0 + (XP ? row_base + (i >> 2) * 16 + (i & 3) : row0 + 4 * i);
+            if (row >= args.M) continue;
+            float *crow = Cb + row * args.N;
 #pragma unroll
-        for (int gj = 0; gj < kTN / 4; ++gj) {
-            const int64_t col = n0 + col_base + gj * 32;
-            if (col >= args.N) continue;  // N % 4 == 0: the 4-vector is all in or all out
-            float o[4];
+            for (int gj = 0; gj < kTN / 4; ++gj) {
+                const int64_t col = n0 + col_base + gj * 32;
+                if (col >= args.N) continue;  // N % 4 == 0: the 4-vector is all in or all out
+                float o[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) o[e] = args.alpha * acc_at(i, gj * 4 + e);
-            if (read_c) {
-                const float4 old = *reinterpret_cast<const float4 *>(crow + col);
-                o[0] = fmaf(args.beta, old.x, o[0]);
-                o[1] = fmaf(args.beta, old.y, o[1]);
-                o[2] = fmaf(args.beta, old.z, o[2]);
-                o[3] = fmaf(args.beta, old.w, o[3]);
-            }
-            if (args.bias || args.relu) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    if (args.bias) o[e] += args.bias[col + e];
-                    if (args.relu) o[e] = o[e] > 0.0f ? o[e] : 0.0f;
+                for (int e = 0; e < 4; ++e) o[e] = args.alpha * acc_at(i, gj * 4 + e);
+                if (read_c) {
+                    const float4 old = *reinterpret_cast<const float4 *>(crow + col);
+                    o[0] = fmaf(args.beta, old.x, o[0]);
+                    o[1] = fmaf(args.beta, old.y, o[1]);
+                    o[2] = fmaf(args.beta, old.z, o[2]);
+                    o[3] = fmaf(args.beta, old.w, o[3]);
                 }
+                if (args.bias || args.relu) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (args.bias) o[e] += args.bias[col + e];
+                        if (args.relu) o[e] = o[e] > 0.0f ? o[e] : 0.0f;
+                    }
+                }
+                *reinterpret_cast<float4 *>(crow + col) = make_float4(o[0], o[1], o[2], o[3]);
             }
-            *reinterpret_cast<float4 *>(crow + col) = make_float4(o[0], o[1], o[2], o[3]);
         }
+    }  // tiles
+    if (!ok && loader && issued) {
+        const int64_t first_pending = issued > S ? issued - S : 0;
+        for (int64_t q = first_pending; q < issued; ++q)
+            mbar_wait_drain(&full[q % S], static_cast<uint32_t>((q / S) & 1), 1000000000ull);
     }
 }
 
@@ -707,16 +831,17 @@ bool sgemm_tma_rowa_eligible(int64_t M, int64_t N, int64_t K, int64_t sA, int64_
 
 namespace {
 
-template <int WN>
+template <int WN, bool XP, bool MULTI>
 int launch_rowa(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, RArgs args, int64_t batch) {
-    using Cf = RowaCfg<WN>;
+    using Cf = RowaCfg<WN, XP>;
     {
         static std::mutex mu;
         static bool attr_set[64] = {};
         std::lock_guard<std::mutex> lk(mu);
         if (!attr_set[h->device & 63]) {
             cudaError_t e =
-                cudaFuncSetAttribute(sgemm_tma_rowa_kernel<WN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+                cudaFuncSetAttribute(sgemm_tma_rowa_kernel<WN, XP, MULTI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cf::SMEM);
             if (e != cudaSuccess) return fail_cuda(e, "sgemm (row-major A) smem attribute");
             attr_set[h->device & 63] = true;
         }
@@ -724,7 +849,11 @@ int launch_rowa(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, R
     args.tiles_n = (args.N + Cf::BN - 1) / Cf::BN;
     const int64_t blocks = args.tiles_m * args.tiles_n * batch;
     if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
-    sgemm_tma_rowa_kernel<WN><<<static_cast<unsigned>(blocks), Cf::THREADS, Cf::SMEM, h->stream>>>(tmA, tmB, args);
+    args.tiles = blocks;
+    // persistent: one CTA per SM (its shared memory allows no second one)
+    const int64_t grid = MULTI ? (blocks < h->sm_count ? blocks : h->sm_count) : blocks;
+    sgemm_tma_rowa_kernel<WN, XP, MULTI>
+        <<<static_cast<unsigned>(grid), Cf::THREADS, Cf::SMEM, h->stream>>>(tmA, tmB, args);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm (row-major A) TMA launch");
 }
@@ -745,7 +874,9 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
     // B tile per CTA costs more L2 -> SM traffic per flop than overlapping two
     // CTAs' prologues and epilogues saves.
     const bool narrow = h->sgemm_variant == 25;
-    const int bn = narrow ? RowaCfg<2>::BN : RowaCfg<4>::BN;
+    const bool xpose = h->sgemm_variant == 26 || h->sgemm_variant == 27;
+    const bool multi = h->sgemm_variant == 27;
+    const int bn = narrow ? RowaCfg<2, false>::BN : RowaCfg<4, false>::BN;
     CUtensorMap tmA, tmB;
     int rc = encode_tma_3d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, A, static_cast<uint64_t>(K),
                            static_cast<uint64_t>(M), static_cast<uint64_t>(batch), static_cast<uint64_t>(K) * 4,
@@ -756,7 +887,10 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
                        kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     RArgs args{C, M, N, K, sC, tiles_m, 0, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns};
-    return narrow ? launch_rowa<2>(h, tmA, tmB, args, batch) : launch_rowa<4>(h, tmA, tmB, args, batch);
+    if (narrow) return launch_rowa<2, false, false>(h, tmA, tmB, args, batch);
+    if (multi) return launch_rowa<4, true, true>(h, tmA, tmB, args, batch);
+    return xpose ? launch_rowa<4, true, false>(h, tmA, tmB, args, batch)
+                 : launch_rowa<4, false, false>(h, tmA, tmB, args, batch);
 }
 
 }  // namespace b2b

@@ -344,24 +344,7 @@ struct RArgs {
     int relu;
     int *status;
     uint64_t wait_ns;
-    int64_t tiles;  // tiles of the whole call (persistent form)
 };
-
-// (batch, first row, first column) of tile t: batches in order, each
-// batch's tiles raster-grouped by kGroupM tile rows.
-__device__ __forceinline__ void rowa_tile(const RArgs &args, int64_t t, int bn, int64_t &batch, int64_t &m0,
-                                          int64_t &n0) {
-    const int64_t per_batch = args.tiles_m * args.tiles_n;
-    batch = t / per_batch;
-    const int64_t tb = t - batch * per_batch;
-    const int64_t span = kGroupM * args.tiles_n;
-    const int64_t g = tb / span;
-    const int64_t first = g * kGroupM;
-    const int64_t gm = args.tiles_m - first < kGroupM ? args.tiles_m - first : kGroupM;
-    const int64_t r = tb - g * span;
-    m0 = (first + r % gm) * kBM;
-    n0 = (r / gm) * bn;
-}
 
 template <int WN, bool XP>
 struct RowaCfg {
@@ -391,16 +374,13 @@ __device__ __forceinline__ bool bar1_and(bool pred, int threads) {
     return out != 0;
 }
 
-// XP = true: the warps transpose each landed A tile into At_s[k][m] (two
-// buffers, alternating by k-block) before the FFMA loop reads it, so A
-// fragments are 16-byte loads of four rows as in sgemm_tma_kernel instead of
-// four 4-byte loads; one barrier per k-block separates the transpose from
-// the reads.  MULTI = true (with XP): persistent, CTA b takes tiles b,
-// b + gridDim.x, ...; the k-blocks of all its tiles form one load stream
-// through the stage ring, so the next tile's first loads are in flight while
-// the warps finish and store the current one; the loader's position lives in
-// shared memory.  Same per-element arithmetic (and bits) in every form.
-template <int WN, bool XP, bool MULTI>
+// XP = true (the default for batched calls): the warps transpose each landed
+// A tile into At_s[k][m] (two buffers, alternating by k-block) before the
+// FFMA loop reads it, so A fragments are 16-byte loads of four rows as in
+// sgemm_tma_kernel instead of four 4-byte loads; one barrier per k-block
+// separates the transpose from the reads.  Same per-element arithmetic (and
+// bits) as XP = false.
+template <int WN, bool XP>
 __global__ void __launch_bounds__(RowaCfg<WN, XP>::THREADS, RowaCfg<WN, XP>::MIN_BLOCKS)
     sgemm_tma_rowa_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           RArgs args) {
@@ -417,17 +397,19 @@ __global__ void __launch_bounds__(RowaCfg<WN, XP>::THREADS, RowaCfg<WN, XP>::MIN
     uint64_t *full = bars;
     uint64_t *empty = bars + S;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * S);
-    // loader position (MULTI): tile of this CTA, k-block, batch, m0, n0
-    int *ld = reinterpret_cast<int *>(bars + 2 * S + 1);
-    static_assert(!MULTI || XP, "the persistent form is built on the transposing one");
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    int64_t batch, m0, n0;
-    rowa_tile(args, blockIdx.x, Cf::BN, batch, m0, n0);
+    const int64_t per_batch = args.tiles_m * args.tiles_n;
+    const int64_t t = blockIdx.x;
+    const int64_t batch = t / per_batch;
+    const int64_t tb = t - batch * per_batch;
+    const int64_t span = kGroupM * args.tiles_n;
+    const int64_t g = tb / span;
+    const int64_t first = g * kGroupM;
+    const int64_t gm = args.tiles_m - first < kGroupM ? args.tiles_m - first : kGroupM;
+    const int64_t r = tb - g * span;
+    const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * Cf::BN;
     const int64_t ktiles = (args.K + kBK - 1) / kBK;
-    // this CTA's tiles and its whole k-block stream
-    const int64_t ntiles = MULTI ? (args.tiles - static_cast<int64_t>(blockIdx.x) + gridDim.x - 1) / gridDim.x : 1;
-    const int64_t total = ntiles * ktiles;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -438,50 +420,22 @@ __global__ void __launch_bounds__(RowaCfg<WN, XP>::THREADS, RowaCfg<WN, XP>::MIN
         fence_barrier_init();
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
-        ld[0] = 0;
-        ld[1] = 0;
-        ld[2] = static_cast<int>(batch);
-        ld[3] = static_cast<int>(m0);
-        ld[4] = static_cast<int>(n0);
     }
     __syncthreads();
 
     const bool loader = tid == 0;
     int64_t issued = 0;
-    // Loads k-block `issued` of the stream (MULTI: the loader's position in
-    // shared memory names its tile) into stage issued % S.
-    auto issue = [&]() {
-        const int s = static_cast<int>(issued % S);
+    auto issue = [&](int64_t kt) {
+        const int s = static_cast<int>(kt % S);
         mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
-        if constexpr (MULTI) {
-            const int kt = ld[1];
-            tma_load_3d(As + s * kAStageF, &tmA, &full[s], kt * kBK, ld[3], ld[2]);
-            tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], ld[4], kt * kBK, ld[2]);
-            if (kt + 1 == ktiles) {
-                const int i = ld[0] + 1;
-                if (i < ntiles) {
-                    int64_t b1, mm, nn;
-                    rowa_tile(args, blockIdx.x + static_cast<int64_t>(i) * gridDim.x, Cf::BN, b1, mm, nn);
-                    ld[2] = static_cast<int>(b1);
-                    ld[3] = static_cast<int>(mm);
-                    ld[4] = static_cast<int>(nn);
-                }
-                ld[0] = i;
-                ld[1] = 0;
-            } else {
-                ld[1] = kt + 1;
-            }
-        } else {
-            const int64_t kt = issued;
-            tma_load_3d(As + s * kAStageF, &tmA, &full[s], static_cast<int32_t>(kt * kBK), static_cast<int32_t>(m0),
-                        static_cast<int32_t>(batch));
-            tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], static_cast<int32_t>(n0),
-                        static_cast<int32_t>(kt * kBK), static_cast<int32_t>(batch));
-        }
+        tma_load_3d(As + s * kAStageF, &tmA, &full[s], static_cast<int32_t>(kt * kBK), static_cast<int32_t>(m0),
+                    static_cast<int32_t>(batch));
+        tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], static_cast<int32_t>(n0), static_cast<int32_t>(kt * kBK),
+                    static_cast<int32_t>(batch));
         ++issued;
     };
     if (loader)
-        for (int64_t q = 0; q < S && q < total; ++q) issue();
+        for (int64_t kt = 0; kt < S && kt < ktiles; ++kt) issue(kt);
 
     const int wm = warp / WN, wn = warp % WN;
     const int ty = lane >> 3, tx = lane & 7;
@@ -526,131 +480,122 @@ __global__ void __launch_bounds__(RowaCfg<WN, XP>::THREADS, RowaCfg<WN, XP>::MIN
     };
 
     bool ok = true;
-    int64_t gk = 0;  // position in this CTA's k-block stream
-#pragma unroll 1
-    for (int64_t ti = 0; ti < ntiles && ok; ++ti) {
-        if (MULTI && ti > 0) {
+    for (int64_t kt = 0; kt < ktiles; ++kt) {
+        const int s = static_cast<int>(kt % S);
+        const uint32_t ph = static_cast<uint32_t>((kt / S) & 1);
+        bool w = ok && mbar_wait(&full[s], ph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x34, args.wait_ns);
+        w = __all_sync(0xffffffffu, w);
+        const float *as;
+        if constexpr (XP) {
+            // A tile -> At_s[kt & 1] as [k][m]: thread q of 1024 moves the
+            // 16-byte chunk c = q / 128 (k = 4c..4c+3) of row m = q % 128, so a
+            // warp reads 32 rows (4 wavefronts, the swizzle spreads the chunks)
+            // and writes 32 consecutive m of each k (conflict-free).
+            float *at = At_s + (kt & 1) * kAStageF;
+            if (w) {
+                const float *src = As + s * kAStageF;
 #pragma unroll
-            for (int i = 0; i < kTM / 2; ++i)
-#pragma unroll
-                for (int j = 0; j < kTN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
-        }
-        for (int64_t kt = 0; kt < ktiles; ++kt, ++gk) {
-            const int s = static_cast<int>(gk % S);
-            const uint32_t ph = static_cast<uint32_t>((gk / S) & 1);
-            bool w = ok && mbar_wait(&full[s], ph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x34, args.wait_ns);
-            w = __all_sync(0xffffffffu, w);
-            const float *as;
-            if constexpr (XP) {
-                // A tile -> At_s[kt & 1] as [k][m]: thread q of 1024 moves the
-                // 16-byte chunk c = q / 128 (k = 4c..4c+3) of row m = q % 128, so a
-                // warp reads 32 rows (4 wavefronts, the swizzle spreads the chunks)
-                // and writes 32 consecutive m of each k (conflict-free).
-                float *at = At_s + (gk & 1) * kAStageF;
-                if (w) {
-                    const float *src = As + s * kAStageF;
-#pragma unroll
-                    for (int r = 0; r < 1024 / Cf::THREADS; ++r) {
-                        const int q = r * Cf::THREADS + tid;
-                        const int m = q & 127, c = q >> 7;
-                        const float4 v = *reinterpret_cast<const float4 *>(src + m * 32 + ((c ^ (m & 7)) << 2));
-                        at[(4 * c + 0) * kBM + m] = v.x;
-                        at[(4 * c + 1) * kBM + m] = v.y;
-                        at[(4 * c + 2) * kBM + m] = v.z;
-                        at[(4 * c + 3) * kBM + m] = v.w;
-                    }
-                }
-                // Every warp's transpose is done (and every warp's wait held)
-                // before any warp reads it; a warp arriving here has also finished
-                // reading the buffer it overwrote, from two k-blocks ago.
-                if (!bar1_and(w, Cf::THREADS)) {
-                    ok = false;
-                    break;
-                }
-                as = at;
-            } else {
-                if (!w) {
-                    ok = false;
-                    break;
-                }
-                as = As + s * kAStageF;
-            }
-            const float *bs = Bs + s * Cf::B_STAGE_F;
-            float af[2][kTM], bf[2][kTN];
-            load_frags(as, bs, 0, af[0], bf[0]);
-#pragma unroll
-            for (int kk = 0; kk < kBK; ++kk) {
-                if (kk + 1 < kBK) load_frags(as, bs, kk + 1, af[(kk + 1) & 1], bf[(kk + 1) & 1]);
-                const float *a = af[kk & 1], *b = bf[kk & 1];
-#pragma unroll
-                for (int j = 0; j < kTN; ++j) {
-                    const float2 bb = make_float2(b[j], b[j]);
-#pragma unroll
-                    for (int p = 0; p < kTM / 2; ++p)
-                        acc2[p][j] = __ffma2_rn(make_float2(a[2 * p], a[2 * p + 1]), bb, acc2[p][j]);
+                for (int r = 0; r < 1024 / Cf::THREADS; ++r) {
+                    const int q = r * Cf::THREADS + tid;
+                    const int m = q & 127, c = q >> 7;
+                    const float4 v = *reinterpret_cast<const float4 *>(src + m * 32 + ((c ^ (m & 7)) << 2));
+                    at[(4 * c + 0) * kBM + m] = v.x;
+                    at[(4 * c + 1) * kBM + m] = v.y;
+                    at[(4 * c + 2) * kBM + m] = v.z;
+                    at[(4 * c + 3) * kBM + m] = v.w;
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (loader && gk >= 1) {
-                const int64_t done = gk - 1, next = done + S;
-                if (next < total) {
-                    const int ds = static_cast<int>(done % S);
-                    const uint32_t dph = static_cast<uint32_t>((done / S) & 1);
-                    if (!mbar_wait(&empty[ds], dph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x33, args.wait_ns)) {
-                        ok = false;
-                    } else {
-                        issue();
-                    }
-                }
-            }
-            if constexpr (XP) {
-                // a failed refill reaches the other warps at the next barrier
-                ok = __all_sync(0xffffffffu, ok);
-            } else if (!__all_sync(0xffffffffu, ok)) {
+            // Every warp's transpose is done (and every warp's wait held)
+            // before any warp reads it; a warp arriving here has also finished
+            // reading the buffer it overwrote, from two k-blocks ago.
+            if (!bar1_and(w, Cf::THREADS)) {
                 ok = false;
                 break;
             }
+            as = at;
+        } else {
+            if (!w) {
+                ok = false;
+                break;
+            }
+            as = As + s * kAStageF;
         }
-        if (!ok) break;
-
-        if (MULTI && ti > 0) rowa_tile(args, blockIdx.x + ti * gridDim.x, Cf::BN, batch, m0, n0);
-        float *Cb = args.C + batch * args.sC;
-        const bool read_c = args.beta != 0.0f;
+        const float *bs = Bs + s * Cf::B_STAGE_F;
+        float af[2][kTM], bf[2][kTN];
+        load_frags(as, bs, 0, af[0], bf[0]);
 #pragma unroll
-        for (int i = 0; i < kTM; ++i) {
-            const int64_t row = m0 + (XP ? row_base + (i >> 2) * 16 + (i & 3) : row0 + 4 * i);
-            if (row >= args.M) continue;
-            float *crow = Cb + row * args.N;
+        for (int kk = 0; kk < kBK; ++kk) {
+            if (kk + 1 < kBK) load_frags(as, bs, kk + 1, af[(kk + 1) & 1], bf[(kk + 1) & 1]);
+            const float *a = af[kk & 1], *b = bf[kk & 1];
 #pragma unroll
-            for (int gj = 0; gj < kTN / 4; ++gj) {
-                const int64_t col = n0 + col_base + gj * 32;
-                if (col >= args.N) continue;  // N % 4 == 0: the 4-vector is all in or all out
-                float o[4];
+            for (int j = 0; j < kTN; ++j) {
+                const float2 bb = make_float2(b[j], b[j]);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) o[e] = args.alpha * acc_at(i, gj * 4 + e);
-                if (read_c) {
-                    const float4 old = *reinterpret_cast<const float4 *>(crow + col);
-                    o[0] = fmaf(args.beta, old.x, o[0]);
-                    o[1] = fmaf(args.beta, old.y, o[1]);
-                    o[2] = fmaf(args.beta, old.z, o[2]);
-                    o[3] = fmaf(args.beta, old.w, o[3]);
-                }
-                if (args.bias || args.relu) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        if (args.bias) o[e] += args.bias[col + e];
-                        if (args.relu) o[e] = o[e] > 0.0f ? o[e] : 0.0f;
-                    }
-                }
-                *reinterpret_cast<float4 *>(crow + col) = make_float4(o[0], o[1], o[2], o[3]);
+                for (int p = 0; p < kTM / 2; ++p)
+                    acc2[p][j] = __ffma2_rn(make_float2(a[2 * p], a[2 * p + 1]), bb, acc2[p][j]);
             }
         }
-    }  // tiles
-    if (!ok && loader && issued) {
-        const int64_t first_pending = issued > S ? issued - S : 0;
-        for (int64_t q = first_pending; q < issued; ++q)
-            mbar_wait_drain(&full[q % S], static_cast<uint32_t>((q / S) & 1), 1000000000ull);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (loader && kt >= 1) {
+            const int64_t done = kt - 1, next = done + S;
+            if (next < ktiles) {
+                const int ds = static_cast<int>(done % S);
+                const uint32_t dph = static_cast<uint32_t>((done / S) & 1);
+                if (!mbar_wait(&empty[ds], dph, abort_flag, args.status, B2B_DEVSTAT_TIMEOUT | 0x33, args.wait_ns)) {
+                    ok = false;
+                } else {
+                    issue(next);
+                }
+            }
+        }
+        if constexpr (XP) {
+            // a failed refill reaches the other warps at the next barrier
+            ok = __all_sync(0xffffffffu, ok);
+        } else if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+        }
+    }
+    if (!ok) {
+        if (loader && issued) {
+            const int64_t first_pending = issued > S ? issued - S : 0;
+            for (int64_t kt = first_pending; kt < issued; ++kt)
+                mbar_wait_drain(&full[kt % S], static_cast<uint32_t>((kt / S) & 1), 1000000000ull);
+        }
+        return;
+    }
+
+    float *Cb = args.C + batch * args.sC;
+    const bool read_c = args.beta != 0.0f;
+#pragma unroll
+    for (int i = 0; i < kTM; ++i) {
+        const int64_t row = m0 + (XP ? row_base + (i >> 2) * 16 + (i & 3) : row0 + 4 * i);
+        if (row >= args.M) continue;
+        float *crow = Cb + row * args.N;
+#pragma unroll
+        for (int gj = 0; gj < kTN / 4; ++gj) {
+            const int64_t col = n0 + col_base + gj * 32;
+            if (col >= args.N) continue;  // N % 4 == 0: the 4-vector is all in or all out
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[e] = args.alpha * acc_at(i, gj * 4 + e);
+            if (read_c) {
+                const float4 old = *reinterpret_cast<const float4 *>(crow + col);
+                o[0] = fmaf(args.beta, old.x, o[0]);
+                o[1] = fmaf(args.beta, old.y, o[1]);
+                o[2] = fmaf(args.beta, old.z, o[2]);
+                o[3] = fmaf(args.beta, old.w, o[3]);
+            }
+            if (args.bias || args.relu) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    if (args.bias) o[e] += args.bias[col + e];
+                    if (args.relu) o[e] = o[e] > 0.0f ? o[e] : 0.0f;
+                }
+            }
+            *reinterpret_cast<float4 *>(crow + col) = make_float4(o[0], o[1], o[2], o[3]);
+        }
     }
 }
 
@@ -831,7 +776,7 @@ bool sgemm_tma_rowa_eligible(int64_t M, int64_t N, int64_t K, int64_t sA, int64_
 
 namespace {
 
-template <int WN, bool XP, bool MULTI>
+template <int WN, bool XP>
 int launch_rowa(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, RArgs args, int64_t batch) {
     using Cf = RowaCfg<WN, XP>;
     {
@@ -840,8 +785,7 @@ int launch_rowa(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, R
         std::lock_guard<std::mutex> lk(mu);
         if (!attr_set[h->device & 63]) {
             cudaError_t e =
-                cudaFuncSetAttribute(sgemm_tma_rowa_kernel<WN, XP, MULTI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cf::SMEM);
+                cudaFuncSetAttribute(sgemm_tma_rowa_kernel<WN, XP>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
             if (e != cudaSuccess) return fail_cuda(e, "sgemm (row-major A) smem attribute");
             attr_set[h->device & 63] = true;
         }
@@ -849,11 +793,7 @@ int launch_rowa(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, R
     args.tiles_n = (args.N + Cf::BN - 1) / Cf::BN;
     const int64_t blocks = args.tiles_m * args.tiles_n * batch;
     if (blocks > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
-    args.tiles = blocks;
-    // persistent: one CTA per SM (its shared memory allows no second one)
-    const int64_t grid = MULTI ? (blocks < h->sm_count ? blocks : h->sm_count) : blocks;
-    sgemm_tma_rowa_kernel<WN, XP, MULTI>
-        <<<static_cast<unsigned>(grid), Cf::THREADS, Cf::SMEM, h->stream>>>(tmA, tmB, args);
+    sgemm_tma_rowa_kernel<WN, XP><<<static_cast<unsigned>(blocks), Cf::THREADS, Cf::SMEM, h->stream>>>(tmA, tmB, args);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm (row-major A) TMA launch");
 }
@@ -869,14 +809,15 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
         sC = M * N;
     }
     const int64_t tiles_m = (M + kBM - 1) / kBM;
-    // 128 x 256 tiles; variant 25 takes the 128 x 128 form (two CTAs per SM),
-    // which measured slower on 4096 x 256^3 (51.5 vs 54.0 TFLOP/s): half the
-    // B tile per CTA costs more L2 -> SM traffic per flop than overlapping two
-    // CTAs' prologues and epilogues saves.
+    // 128 x 256 tiles with A transposed in shared memory (54.5 TFLOP/s on
+    // 4096 x 256^3, against 50.9 for the 4-byte A fragments of variant 24 on
+    // the same box); variant 25 takes the 128 x 128 form (two CTAs per SM),
+    // which measured slower (51.5 vs 54.0): half the B tile per CTA costs more
+    // L2 -> SM traffic per flop than overlapping two CTAs' prologues and
+    // epilogues saves.
     const bool narrow = h->sgemm_variant == 25;
-    const bool xpose = h->sgemm_variant == 26 || h->sgemm_variant == 27;
-    const bool multi = h->sgemm_variant == 27;
-    const int bn = narrow ? RowaCfg<2, false>::BN : RowaCfg<4, false>::BN;
+    const bool plain = h->sgemm_variant == 24;
+    const int bn = narrow ? RowaCfg<2, false>::BN : RowaCfg<4, true>::BN;
     CUtensorMap tmA, tmB;
     int rc = encode_tma_3d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, A, static_cast<uint64_t>(K),
                            static_cast<uint64_t>(M), static_cast<uint64_t>(batch), static_cast<uint64_t>(K) * 4,
@@ -887,10 +828,8 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
                        kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     RArgs args{C, M, N, K, sC, tiles_m, 0, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns};
-    if (narrow) return launch_rowa<2, false, false>(h, tmA, tmB, args, batch);
-    if (multi) return launch_rowa<4, true, true>(h, tmA, tmB, args, batch);
-    return xpose ? launch_rowa<4, true, false>(h, tmA, tmB, args, batch)
-                 : launch_rowa<4, false, false>(h, tmA, tmB, args, batch);
+    if (narrow) return launch_rowa<2, false>(h, tmA, tmB, args, batch);
+    return plain ? launch_rowa<4, false>(h, tmA, tmB, args, batch) : launch_rowa<4, true>(h, tmA, tmB, args, batch);
 }
 
 }  // namespace b2b

@@ -662,7 +662,7 @@ class BatchedWorkload(Workload):
         self.b = b2blas.DeviceBuffer.from_ptr(h, self.B.data_ptr(), self.batch * mk, "float32", owner=self.B)
         self.c = b2blas.DeviceBuffer.from_ptr(h, self.C.data_ptr(), self.batch * mk, "float32", owner=self.C)
         self.cfg = b2blas.GemmConfig(m, m, m, 1.0, 0.0)
-        self.kernel = "sgemm_tma_rowa_kernel (batched)"
+        self.kernel = "sgemm_tma_rowa_ws_kernel (batched, persistent)"
         self.bound = "fma"
 
     def step(self):

@@ -673,7 +673,7 @@ int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float
     // Batched calls (and variant 23): the TMA-fed kernel on row-major A (no
     // transpose pass), batched through 3-D tensor maps; same bits, 2.5%
     // faster than the cp.async kernel on 4096 x 256^3.
-    if (((variant >= 23 && variant <= 26) || (variant == 0 && batch > 1)) &&
+    if (((variant >= 23 && variant <= 27) || (variant == 0 && batch > 1)) &&
         b2b::sgemm_tma_rowa_eligible(M, N, K, sA, sB, sC, batch, A, B, C))
         return b2b::launch_sgemm_tma_rowa(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi.bias, epi.relu);
     if (!vec_ok(K, N, sA, sB, sC, A, B, C) || variant == 1)

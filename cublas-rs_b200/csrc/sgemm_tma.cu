@@ -327,15 +327,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 // reads across a batch boundary and out-of-range rows/columns arrive as
 // zeros.
 //
-// Two CTA shapes, the same per-thread work (16 x 8 outputs, 248 registers):
-//   WN = 4: 8 warps, 128 x 256 tiles, 4 stages of 48 KiB -- one CTA per SM.
+// CTA shapes, the same per-thread work (16 x 8 outputs):
+//   WN = 4: 8 warps, 128 x 256 tiles, 4 stages of 48 KiB -- one CTA per SM;
+//     with A transposed in shared memory (XP, the default) or read as 4-byte
+//     fragments (variant 24).
 //   WN = 2: 4 warps, 128 x 128 tiles, 3 stages of 32 KiB -- two CTAs per SM,
 //     so one CTA's prologue (the first TMA round trip) and epilogue (the C
 //     stores) overlap the other's FFMA loop (variant 25; slower on the
 //     4096 x 256^3 batched workload, 51.5 vs 54.0 TFLOP/s).
-// (A persistent form of WN = 4 whose load stream ran across tile boundaries
-// measured 45.1 vs 53.7 TFLOP/s on 4096 x 256^3: the bookkeeping took it to
-// 255 registers and slowed the FFMA loop more than it hid.)
+//   sgemm_tma_rowa_ws_kernel: the XP form, persistent, with a producer warp.
+// (A persistent form of WN = 4 whose load stream ran across tile boundaries,
+// loaded by a compute warp, measured 45.1 vs 53.7 TFLOP/s on 4096 x 256^3:
+// the bookkeeping took it to 255 registers and slowed the FFMA loop more than
+// it hid.)
 struct RArgs {
     float *C;
     int64_t M, N, K, sC, tiles_m, tiles_n;
@@ -344,7 +348,24 @@ struct RArgs {
     int relu;
     int *status;
     uint64_t wait_ns;
+    int64_t tiles;  // tiles of the whole call (the persistent form)
 };
+
+// (batch, first row, first column) of tile t: batches in order, each
+// batch's tiles raster-grouped by kGroupM tile rows.
+__device__ __forceinline__ void rowa_tile(const RArgs &args, int64_t t, int bn, int64_t &batch, int64_t &m0,
+                                          int64_t &n0) {
+    const int64_t per_batch = args.tiles_m * args.tiles_n;
+    batch = t / per_batch;
+    const int64_t tb = t - batch * per_batch;
+    const int64_t span = kGroupM * args.tiles_n;
+    const int64_t g = tb / span;
+    const int64_t first = g * kGroupM;
+    const int64_t gm = args.tiles_m - first < kGroupM ? args.tiles_m - first : kGroupM;
+    const int64_t r = tb - g * span;
+    m0 = (first + r % gm) * kBM;
+    n0 = (r / gm) * bn;
+}
 
 template <int WN, bool XP>
 struct RowaCfg {
@@ -374,7 +395,7 @@ __device__ __forceinline__ bool bar1_and(bool pred, int threads) {
     return out != 0;
 }
 
-// XP = true (the default for batched calls): the warps transpose each landed
+// XP = true: the warps transpose each landed
 // A tile into At_s[k][m] (two buffers, alternating by k-block) before the
 // FFMA loop reads it, so A fragments are 16-byte loads of four rows as in
 // sgemm_tma_kernel instead of four 4-byte loads; one barrier per k-block
@@ -636,6 +657,199 @@ __global__ void __launch_bounds__(256) sgemm_splitk_reduce_kernel(const float *_
     }
 }
 
+// Warp-specialised persistent form of the XP kernel: two FFMA warpgroups and a
+// producer warpgroup (384 threads launched at 168 registers each, 64512 in
+// all; the producer warpgroup gives up all but 56 per thread with
+// setmaxnreg.dec and the FFMA warpgroups take 224 with setmaxnreg.inc:
+// 128 x 56 + 256 x 224 = 64512, the launch's own total, so the increase never
+// waits).  CTA b takes tiles b, b + gridDim.x, ...; the producer's
+// lane 0 streams the k-blocks of all of them through the 4-stage ring,
+// waiting only on the "empty" barriers, so the next tile's first stages land
+// while the FFMA warps finish and store the current one, and none of the
+// loading bookkeeping sits in the FFMA warps.  The FFMA warps transpose each
+// A tile into At_s, meet at a 256-thread barrier (the producer never joins
+// it), run the FFMA loop and release the stage.  Same per-element arithmetic
+// (and bits) as the other forms.
+__global__ void __launch_bounds__(384, 1)
+    sgemm_tma_rowa_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             RArgs args) {
+    using namespace sm100;
+    using Cf = RowaCfg<4, true>;
+    constexpr int S = Cf::STAGES;
+    constexpr int NC = Cf::THREADS;  // FFMA threads (8 warps)
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    float *As = reinterpret_cast<float *>(smem);
+    float *Bs = As + S * kAStageF;
+    float *At_s = reinterpret_cast<float *>(smem + S * Cf::STAGE_BYTES);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cf::STAGE_BYTES + Cf::XPOSE_BYTES);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + S;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * S);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t ktiles = (args.K + kBK - 1) / kBK;
+    const int64_t ntiles = (args.tiles - static_cast<int64_t>(blockIdx.x) + gridDim.x - 1) / gridDim.x;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], Cf::WARPS);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    __syncthreads();
+
+    if (warp >= Cf::WARPS) {
+        // ------------------------------------------------ producer warpgroup
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+        if (warp == Cf::WARPS && lane == 0) {
+            int64_t g = 0;
+            bool ok = true;
+            for (int64_t ti = 0; ti < ntiles && ok; ++ti) {
+                int64_t batch, m0, n0;
+                rowa_tile(args, blockIdx.x + ti * gridDim.x, Cf::BN, batch, m0, n0);
+                for (int64_t kt = 0; kt < ktiles; ++kt, ++g) {
+                    const int s = static_cast<int>(g % S);
+                    if (g >= S && !mbar_wait(&empty[s], static_cast<uint32_t>((g / S - 1) & 1), abort_flag,
+                                             args.status, B2B_DEVSTAT_TIMEOUT | 0x35, args.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
+                    tma_load_3d(As + s * kAStageF, &tmA, &full[s], static_cast<int32_t>(kt * kBK),
+                                static_cast<int32_t>(m0), static_cast<int32_t>(batch));
+                    tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], static_cast<int32_t>(n0),
+                                static_cast<int32_t>(kt * kBK), static_cast<int32_t>(batch));
+                }
+            }
+            if (!ok && g > 0) {
+                // loads in flight complete on their full barriers before the
+                // CTA's shared memory goes away
+                const int64_t first_pending = g > S ? g - S : 0;
+                for (int64_t q = first_pending; q < g; ++q)
+                    mbar_wait_drain(&full[q % S], static_cast<uint32_t>((q / S) & 1), 1000000000ull);
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------- FFMA warps
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
+    const int wm = warp / 4, wn = warp % 4;
+    const int ty = lane >> 3, tx = lane & 7;
+    const int row_base = wm * (kTM / 4) * 16 + ty * 4;
+    const int col_base = wn * (kTN / 4) * 32 + tx * 4;
+    float2 acc2[kTM / 2][kTN];
+    auto acc_at = [&](int i, int j) -> float & { return (i & 1) ? acc2[i >> 1][j].y : acc2[i >> 1][j].x; };
+    auto load_frags = [&](const float *as, const float *bs, int kk, float (&af)[kTM], float (&bf)[kTN]) {
+#pragma unroll
+        for (int q = 0; q < kTM / 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4 *>(as + kk * kBM + row_base + q * 16);
+            af[q * 4 + 0] = v.x;
+            af[q * 4 + 1] = v.y;
+            af[q * 4 + 2] = v.z;
+            af[q * 4 + 3] = v.w;
+        }
+#pragma unroll
+        for (int q = 0; q < kTN / 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4 *>(bs + kk * Cf::BN + col_base + q * 32);
+            bf[q * 4 + 0] = v.x;
+            bf[q * 4 + 1] = v.y;
+            bf[q * 4 + 2] = v.z;
+            bf[q * 4 + 3] = v.w;
+        }
+    };
+    int64_t g = 0;
+    bool ok = true;
+#pragma unroll 1
+    for (int64_t ti = 0; ti < ntiles && ok; ++ti) {
+#pragma unroll
+        for (int i = 0; i < kTM / 2; ++i)
+#pragma unroll
+            for (int j = 0; j < kTN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
+        for (int64_t kt = 0; kt < ktiles; ++kt, ++g) {
+            const int s = static_cast<int>(g % S);
+            bool w = mbar_wait(&full[s], static_cast<uint32_t>((g / S) & 1), abort_flag, args.status,
+                               B2B_DEVSTAT_TIMEOUT | 0x36, args.wait_ns);
+            w = __all_sync(0xffffffffu, w);
+            float *at = At_s + (g & 1) * kAStageF;
+            if (w) {
+                const float *src = As + s * kAStageF;
+#pragma unroll
+                for (int r = 0; r < 1024 / NC; ++r) {
+                    const int q = r * NC + tid;
+                    const int m = q & 127, c = q >> 7;
+                    const float4 v = *reinterpret_cast<const float4 *>(src + m * 32 + ((c ^ (m & 7)) << 2));
+                    at[(4 * c + 0) * kBM + m] = v.x;
+                    at[(4 * c + 1) * kBM + m] = v.y;
+                    at[(4 * c + 2) * kBM + m] = v.z;
+                    at[(4 * c + 3) * kBM + m] = v.w;
+                }
+            }
+            if (!bar1_and(w, NC)) {
+                ok = false;
+                break;
+            }
+            const float *bs = Bs + s * Cf::B_STAGE_F;
+            float af[2][kTM], bf[2][kTN];
+            load_frags(at, bs, 0, af[0], bf[0]);
+#pragma unroll
+            for (int kk = 0; kk < kBK; ++kk) {
+                if (kk + 1 < kBK) load_frags(at, bs, kk + 1, af[(kk + 1) & 1], bf[(kk + 1) & 1]);
+                const float *a = af[kk & 1], *b = bf[kk & 1];
+#pragma unroll
+                for (int j = 0; j < kTN; ++j) {
+                    const float2 bb = make_float2(b[j], b[j]);
+#pragma unroll
+                    for (int p = 0; p < kTM / 2; ++p)
+                        acc2[p][j] = __ffma2_rn(make_float2(a[2 * p], a[2 * p + 1]), bb, acc2[p][j]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (!ok) break;
+        int64_t batch, m0, n0;
+        rowa_tile(args, blockIdx.x + ti * gridDim.x, Cf::BN, batch, m0, n0);
+        float *Cb = args.C + batch * args.sC;
+        const bool read_c = args.beta != 0.0f;
+#pragma unroll
+        for (int i = 0; i < kTM; ++i) {
+            const int64_t row = m0 + row_base + (i >> 2) * 16 + (i & 3);
+            if (row >= args.M) continue;
+            float *crow = Cb + row * args.N;
+#pragma unroll
+            for (int gj = 0; gj < kTN / 4; ++gj) {
+                const int64_t col = n0 + col_base + gj * 32;
+                if (col >= args.N) continue;  // N % 4 == 0: the 4-vector is all in or all out
+                float o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[e] = args.alpha * acc_at(i, gj * 4 + e);
+                if (read_c) {
+                    const float4 old = *reinterpret_cast<const float4 *>(crow + col);
+                    o[0] = fmaf(args.beta, old.x, o[0]);
+                    o[1] = fmaf(args.beta, old.y, o[1]);
+                    o[2] = fmaf(args.beta, old.z, o[2]);
+                    o[3] = fmaf(args.beta, old.w, o[3]);
+                }
+                if (args.bias || args.relu) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (args.bias) o[e] += args.bias[col + e];
+                        if (args.relu) o[e] = o[e] > 0.0f ? o[e] : 0.0f;
+                    }
+                }
+                *reinterpret_cast<float4 *>(crow + col) = make_float4(o[0], o[1], o[2], o[3]);
+            }
+        }
+    }
+}
+
 // At[k][m] = A[m][k]: 32 x 32 tiles through shared memory (padded row).
 __global__ void __launch_bounds__(256) transpose_f32_kernel(const float *__restrict__ A, float *__restrict__ At,
                                                             int64_t M, int64_t K) {
@@ -798,6 +1012,29 @@ int launch_rowa(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, R
     return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm (row-major A) TMA launch");
 }
 
+int launch_rowa_ws(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, RArgs args, int64_t batch) {
+    using Cf = RowaCfg<4, true>;
+    {
+        static std::mutex mu;
+        static bool attr_set[64] = {};
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set[h->device & 63]) {
+            cudaError_t e =
+                cudaFuncSetAttribute(sgemm_tma_rowa_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+            if (e != cudaSuccess) return fail_cuda(e, "sgemm (row-major A, persistent) smem attribute");
+            attr_set[h->device & 63] = true;
+        }
+    }
+    args.tiles_n = (args.N + Cf::BN - 1) / Cf::BN;
+    args.tiles = args.tiles_m * args.tiles_n * batch;
+    if (args.tiles > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
+    // one CTA per SM: its shared memory allows no second one
+    const int64_t grid = args.tiles < h->sm_count ? args.tiles : h->sm_count;
+    sgemm_tma_rowa_ws_kernel<<<static_cast<unsigned>(grid), 384, Cf::SMEM, h->stream>>>(tmA, tmB, args);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm (row-major A, persistent) TMA launch");
+}
+
 }  // namespace
 
 int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
@@ -809,14 +1046,16 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
         sC = M * N;
     }
     const int64_t tiles_m = (M + kBM - 1) / kBM;
-    // 128 x 256 tiles with A transposed in shared memory (54.5 TFLOP/s on
-    // 4096 x 256^3, against 50.9 for the 4-byte A fragments of variant 24 on
-    // the same box); variant 25 takes the 128 x 128 form (two CTAs per SM),
-    // which measured slower (51.5 vs 54.0): half the B tile per CTA costs more
-    // L2 -> SM traffic per flop than overlapping two CTAs' prologues and
-    // epilogues saves.
+    // The persistent warp-specialised kernel, 128 x 256 tiles with A
+    // transposed in shared memory (4096 x 256^3: 56.4 TFLOP/s, against 54.3
+    // for the one-CTA-per-tile form of variant 26 and 54.1 for the 4-byte A
+    // fragments of variant 24, same box); variant 25 takes the 128 x 128 form
+    // (two CTAs per SM), which measured slower (51.5 vs 54.0): half the B tile
+    // per CTA costs more L2 -> SM traffic per flop than overlapping two CTAs'
+    // prologues and epilogues saves.
     const bool narrow = h->sgemm_variant == 25;
     const bool plain = h->sgemm_variant == 24;
+    const bool per_tile = h->sgemm_variant == 26;
     const int bn = narrow ? RowaCfg<2, false>::BN : RowaCfg<4, true>::BN;
     CUtensorMap tmA, tmB;
     int rc = encode_tma_3d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, A, static_cast<uint64_t>(K),
@@ -827,9 +1066,11 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
                        static_cast<uint64_t>(batch), static_cast<uint64_t>(N) * 4, static_cast<uint64_t>(sB) * 4, bn,
                        kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    RArgs args{C, M, N, K, sC, tiles_m, 0, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns};
+    RArgs args{C, M, N, K, sC, tiles_m, 0, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns, 0};
     if (narrow) return launch_rowa<2, false>(h, tmA, tmB, args, batch);
-    return plain ? launch_rowa<4, false>(h, tmA, tmB, args, batch) : launch_rowa<4, true>(h, tmA, tmB, args, batch);
+    if (plain) return launch_rowa<4, false>(h, tmA, tmB, args, batch);
+    if (per_tile) return launch_rowa<4, true>(h, tmA, tmB, args, batch);
+    return launch_rowa_ws(h, tmA, tmB, args, batch);
 }
 
 }  // namespace b2b

@@ -353,13 +353,14 @@ def workload_config(name, args, world):
                 "scaling": ("weak" if weak else "strong") if world > 1 else "weak",
                 "l2": "inputs larger than L2 (126 MB): no flush needed"}
     if name == "batched":
-        b0, b1 = split_range(4096, world, 0)
-        return {"workload": "strided-batched sgemm 4096 x 256^3"
+        nb = getattr(args, "batch", None) or 4096
+        b0, b1 = split_range(nb, world, 0)
+        return {"workload": f"strided-batched sgemm {nb} x 256^3"
                             + (f", {b1 - b0} batches per GPU" if world > 1 else ""),
-                "batch": 4096, "batch_per_gpu": b1 - b0, "m": 256, "n": 256, "k": 256,
+                "batch": nb, "batch_per_gpu": b1 - b0, "m": 256, "n": 256, "k": 256,
                 "alpha": 1.0, "beta": 0.0, "parallelism": f"batch-shard x{world}",
                 "scaling": "strong" if world > 1 else "weak",
-                "l2": "inputs larger than L2 (3 GiB): no flush needed"}
+                "l2": f"inputs larger than L2 ({3 * nb * 256 * 256 * 4 / 2 ** 30:g} GiB): no flush needed"}
     if name in ("sgemv", "dgemv", "hgemv"):
         esz = {"s": 4, "d": 8, "h": 2}[name[0]]
         gib = 16384 * 16384 * esz / 2 ** 30
@@ -647,7 +648,7 @@ class BatchedWorkload(Workload):
 
         self.h = h
         self.name, self.args = "batched", args
-        self.total_batch, self.m = 4096, 256
+        self.total_batch, self.m = getattr(args, "batch", None) or 4096, 256
         b0, b1 = shard.batch_shard(self.total_batch, world, rank)
         self.batch = b1 - b0
         self.world = world
@@ -1418,7 +1419,7 @@ def run_secondary(names, h, stream, rank, world, dist, barrier, local, args, pea
         sa = copy.copy(args)
         sa.trans = sa.tf32x3 = sa.gather = sa.gather_nccl = sa.gather_multicast = False
         sa.no_gather, sa.weak = True, name == "hgemm-weak"
-        sa.m = sa.n = sa.k = None
+        sa.m = sa.n = sa.k = sa.batch = None
         wname = "hgemm" if name == "hgemm-weak" else name
         sa.workload = wname
         w = make_workload(wname, h, rank, world, sa)
@@ -1496,6 +1497,8 @@ def main():
     ap.add_argument("--m", type=int, default=None, help="GEMM size override (profiling small cases)")
     ap.add_argument("--n", type=int, default=None)
     ap.add_argument("--k", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="batched: batch count override (profiling small cases; default 4096)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-kernels", action="store_true",
                     help="skip timing the reference's GPU kernels (restated in CUDA C) beside the library")

@@ -70,7 +70,7 @@ int b2b_sgemm_splits(b2b_handle *h, size_t m, size_t n, size_t k, int *splits) {
 
 int b2b_set_sgemm_splits(b2b_handle *h, int splits) {
     if (!h) return fail(B2B_ERR_INVALID_ARG, "b2b_set_sgemm_splits: NULL handle");
-    if (splits < 0 || splits > 64) return fail(B2B_ERR_INVALID_ARG, "b2b_set_sgemm_splits: splits must be 0..64");
+    if (splits < 0 || splits > 16) return fail(B2B_ERR_INVALID_ARG, "b2b_set_sgemm_splits: splits must be 0..16");
     h->sgemm_ksplit_forced = splits;
     return B2B_OK;
 }

@@ -148,8 +148,9 @@ B2B_API int b2b_sgemm_bias(b2b_handle *h, int algo, size_t m, size_t n, size_t k
  * on S.  b2b_sgemm_splits returns the S that b2b_sgemm / b2b_sgemm_bias
  * (default algo, 16-byte aligned operands) choose for an m x n x k call;
  * b2b_set_sgemm_splits fixes S for the handle's later calls: 0 = choose per
- * call (the default), 1 = never split, S > 1 = always S where the TMA-fed
- * kernel takes the call.  A caller that computes one GEMM as several row or
+ * call (the default), 1 = never split, S in 2..16 = always S where the
+ * TMA-fed kernel takes the call (S partial sums of m x n floats live in the
+ * handle's workspace).  A caller that computes one GEMM as several row or
  * column pieces gets the whole GEMM's bits by fixing the whole GEMM's S for
  * the pieces (the host-slice calls do this themselves). */
 B2B_API int b2b_sgemm_splits(b2b_handle *h, size_t m, size_t n, size_t k, int *splits);

@@ -185,7 +185,10 @@ int b2b_create(int device, b2b_handle **out) {
     h->force_single_cta = single && single[0] == '1';
     if (const char *v = getenv("B2B_SGEMM_VARIANT")) h->sgemm_variant = atoi(v);
     if (const char *v = getenv("B2B_SGEMM_GROUP_M")) h->sgemm_group_m = atoi(v);
-    if (const char *v = getenv("B2B_SGEMM_KSPLIT")) h->sgemm_ksplit_forced = atoi(v);
+    if (const char *v = getenv("B2B_SGEMM_KSPLIT")) {
+        const int ks = atoi(v);
+        if (ks >= 0 && ks <= 16) h->sgemm_ksplit_forced = ks;
+    }
     if (const char *v = getenv("B2B_HGEMM_VARIANT")) h->hgemm_variant = atoi(v);
     if (const char *v = getenv("B2B_HGEMM_GROUP_M")) h->hgemm_group_m = atoi(v);
     if (const char *v = getenv("B2B_GEMV_SEG_KB")) {

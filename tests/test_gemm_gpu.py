@@ -616,3 +616,22 @@ def test_sgemm_splits_query_and_row_pieces_reproduce_whole(oracle):
             h.set_sgemm_splits(-1)
     finally:
         h.close()
+
+
+def test_sgemm_split_k_beta_zero_does_not_read_c(oracle):
+    # The split-K reduce keeps the rule that beta == 0 leaves C unread: NaN in
+    # C does not reach the result, which equals the call on a zeroed C.
+    import b2blas
+
+    m = n = k = 1024  # 32 tiles: split in 4
+    A = oracle.uniform_f32(m * k, 34, 1)
+    B = oracle.uniform_f32(k * n, 34, 2)
+    h = b2blas.Handle(0)
+    try:
+        assert h.sgemm_splits(m, n, k) > 1
+        cfg = b2blas.GemmConfig(m, n, k, 0.5, 0.0)
+        got = _gemm_dev(h, "sgemm", None, cfg, A, B, np.full(m * n, np.nan, np.float32))
+        ref = _gemm_dev(h, "sgemm", None, cfg, A, B, np.zeros(m * n, np.float32))
+        assert np.all(np.isfinite(got)) and np.array_equal(got, ref)
+    finally:
+        h.close()

@@ -1403,7 +1403,9 @@ def secondary_names(args, world):
         return []
     if world == 1:
         return ["sgemm", "sgemv", "batched", "dgemm"]
-    return ["batched", "hgemm-weak"]
+    # the column-sharded FP32/FP64 problems (fixed 8192^3 / 4096^3, A
+    # replicated), without and with the gathered C
+    return ["batched", "hgemm-weak", "sgemm", "sgemm-gather", "dgemm"]
 
 
 def run_secondary(names, h, stream, rank, world, dist, barrier, local, args, peaks, info):
@@ -1419,8 +1421,10 @@ def run_secondary(names, h, stream, rank, world, dist, barrier, local, args, pea
         sa = copy.copy(args)
         sa.trans = sa.tf32x3 = sa.gather = sa.gather_nccl = sa.gather_multicast = False
         sa.no_gather, sa.weak = True, name == "hgemm-weak"
+        if name.endswith("-gather"):
+            sa.gather, sa.no_gather = True, False
         sa.m = sa.n = sa.k = sa.batch = None
-        wname = "hgemm" if name == "hgemm-weak" else name
+        wname = name.split("-")[0]
         sa.workload = wname
         w = make_workload(wname, h, rank, world, sa)
         torch.cuda.synchronize()

@@ -736,8 +736,8 @@ int launch_sgemm_strided_batched(b2b_handle *h, size_t m, size_t n, size_t k, fl
                      (int64_t)sb, C, (int64_t)sc, (int64_t)batch);
 }
 
-// DGEMM: 64x64 CTA tile, 4x4 per thread, BK=16; the FP64 pipe issues at half
-// the FP32 rate, so a smaller register block keeps three CTAs resident.
+// DGEMM: the FP64 tensor path (dgemm_dmma.cu) where its alignment rules hold,
+// else the CUDA-core DFMA kernels above.
 int launch_dgemm(b2b_handle *h, size_t m, size_t n, size_t k, double alpha, const double *A, const double *B,
                  double beta, double *C) {
     return run_dgemm(h, h->dgemm_variant, (int64_t)m, (int64_t)n, (int64_t)k, alpha, beta, A, B, C);

@@ -123,7 +123,7 @@ def test_hgemm_config_at_n_gpus():
 def test_secondary_configurations():
     bench, ns = _bench_args([])
     assert bench.secondary_names(ns, 1) == ["sgemm", "sgemv", "batched", "dgemm"]
-    assert bench.secondary_names(ns, 8) == ["batched", "hgemm-weak"]
+    assert bench.secondary_names(ns, 8) == ["batched", "hgemm-weak", "sgemm", "sgemm-gather", "dgemm"]
     _, ns2 = _bench_args(["no_secondary"])
     assert bench.secondary_names(ns2, 1) == []
     _, ns3 = _bench_args(["workload=sgemm"])

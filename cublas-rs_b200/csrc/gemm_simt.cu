@@ -670,11 +670,11 @@ int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float
         b2b::sgemm_tma_eligible(M, N, K, A, B, C, h->sgemm_ksplit_forced > 1))
         return b2b::launch_sgemm_tma(h, M, N, K, alpha, beta, A, B, C, epi.bias, epi.relu,
                                      variant == 0 ? 1 : variant - 20);
-    // Batched calls (and variants 23-27): the TMA-fed kernels on row-major A
+    // Batched calls (and variants 23-28): the TMA-fed kernels on row-major A
     // (no transpose pass through global memory), batched through 3-D tensor
     // maps; by default the persistent warp-specialised one (sgemm_tma.cu),
-    // 56.4 vs 52.6 TFLOP/s for the cp.async kernel on 4096 x 256^3, same bits.
-    if (((variant >= 23 && variant <= 27) || (variant == 0 && batch > 1)) &&
+    // 58.8 vs 52.6 TFLOP/s for the cp.async kernel on 4096 x 256^3, same bits.
+    if (((variant >= 23 && variant <= 28) || (variant == 0 && batch > 1)) &&
         b2b::sgemm_tma_rowa_eligible(M, N, K, sA, sB, sC, batch, A, B, C))
         return b2b::launch_sgemm_tma_rowa(h, M, N, K, alpha, beta, A, sA, B, sB, C, sC, batch, epi.bias, epi.relu);
     if (!vec_ok(K, N, sA, sB, sC, A, B, C) || variant == 1)

@@ -335,7 +335,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //     so one CTA's prologue (the first TMA round trip) and epilogue (the C
 //     stores) overlap the other's FFMA loop (variant 25; slower on the
 //     4096 x 256^3 batched workload, 51.5 vs 54.0 TFLOP/s).
-//   sgemm_tma_rowa_ws_kernel: the XP form, persistent, with a producer warp.
+//   sgemm_tma_rowa_ws_kernel: the XP form, persistent, with a producer
+//     warpgroup that also transposes A (the default).
 // (A persistent form of WN = 4 whose load stream ran across tile boundaries,
 // loaded by a compute warp, measured 45.1 vs 53.7 TFLOP/s on 4096 x 256^3:
 // the bookkeeping took it to 255 registers and slowed the FFMA loop more than
@@ -666,10 +667,18 @@ __global__ void __launch_bounds__(256) sgemm_splitk_reduce_kernel(const float *_
 // lane 0 streams the k-blocks of all of them through the 4-stage ring,
 // waiting only on the "empty" barriers, so the next tile's first stages land
 // while the FFMA warps finish and store the current one, and none of the
-// loading bookkeeping sits in the FFMA warps.  The FFMA warps transpose each
-// A tile into At_s, meet at a 256-thread barrier (the producer never joins
-// it), run the FFMA loop and release the stage.  Same per-element arithmetic
+// loading bookkeeping sits in the FFMA warps.  Same per-element arithmetic
 // (and bits) as the other forms.
+//   PX = false: the FFMA warps transpose each A tile into At_s, meet at a
+//     256-thread barrier (the producer never joins it), run the FFMA loop and
+//     release the stage.
+//   PX = true: the producer warpgroup's other three warps transpose each
+//     landed A tile into At_s (two buffers, k-block g into buffer g & 1) and
+//     arrive on that buffer's "xfull" barrier; the FFMA warps wait on it (and
+//     on the stage's "full" barrier, for B), run the FFMA loop and arrive on
+//     "empty" (the stage) and "xempty" (the buffer).  The FFMA warps then meet
+//     no CTA-wide barrier, as in sgemm_tma_kernel.
+template <bool PX>
 __global__ void __launch_bounds__(384, 1)
     sgemm_tma_rowa_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              RArgs args) {
@@ -677,6 +686,7 @@ __global__ void __launch_bounds__(384, 1)
     using Cf = RowaCfg<4, true>;
     constexpr int S = Cf::STAGES;
     constexpr int NC = Cf::THREADS;  // FFMA threads (8 warps)
+    constexpr int NX = 96;           // PX: transposing threads (producer warps 1-3)
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -686,7 +696,9 @@ __global__ void __launch_bounds__(384, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cf::STAGE_BYTES + Cf::XPOSE_BYTES);
     uint64_t *full = bars;
     uint64_t *empty = bars + S;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * S);
+    uint64_t *xfull = bars + 2 * S;      // PX: At_s buffer b transposed
+    uint64_t *xempty = bars + 2 * S + 2; // PX: At_s buffer b read by all FFMA warps
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * S + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t ktiles = (args.K + kBK - 1) / kBK;
@@ -696,6 +708,10 @@ __global__ void __launch_bounds__(384, 1)
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], Cf::WARPS);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&xfull[b], NX / 32);
+            mbar_init(&xempty[b], Cf::WARPS);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -707,6 +723,40 @@ __global__ void __launch_bounds__(384, 1)
     if (warp >= Cf::WARPS) {
         // ------------------------------------------------ producer warpgroup
         asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+        if (PX && warp > Cf::WARPS) {
+            // A transposer: k-block g's landed A tile ([128 m][32 k], 128-byte
+            // swizzle) into At_s buffer g & 1 as [32 k][128 m].
+            const int xt = tid - NC - 32;
+            int64_t g = 0;
+            for (int64_t ti = 0; ti < ntiles; ++ti) {
+                bool w = true;
+                for (int64_t kt = 0; kt < ktiles && w; ++kt, ++g) {
+                    const int s = static_cast<int>(g % S), b = static_cast<int>(g & 1);
+                    w = mbar_wait(&full[s], static_cast<uint32_t>((g / S) & 1), abort_flag, args.status,
+                                  B2B_DEVSTAT_TIMEOUT | 0x37, args.wait_ns);
+                    if (w && g >= 2)
+                        w = mbar_wait(&xempty[b], static_cast<uint32_t>(((g >> 1) - 1) & 1), abort_flag, args.status,
+                                      B2B_DEVSTAT_TIMEOUT | 0x38, args.wait_ns);
+                    w = __all_sync(0xffffffffu, w);
+                    if (!w) break;
+                    const float *src = As + s * kAStageF;
+                    float *at = At_s + b * kAStageF;
+#pragma unroll 1
+                    for (int q = xt; q < 1024; q += NX) {
+                        const int m = q & 127, c = q >> 7;
+                        const float4 v = *reinterpret_cast<const float4 *>(src + m * 32 + ((c ^ (m & 7)) << 2));
+                        at[(4 * c + 0) * kBM + m] = v.x;
+                        at[(4 * c + 1) * kBM + m] = v.y;
+                        at[(4 * c + 2) * kBM + m] = v.z;
+                        at[(4 * c + 3) * kBM + m] = v.w;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&xfull[b]);
+                }
+                if (!w) break;
+            }
+            return;
+        }
         if (warp == Cf::WARPS && lane == 0) {
             int64_t g = 0;
             bool ok = true;
@@ -774,10 +824,21 @@ __global__ void __launch_bounds__(384, 1)
             for (int j = 0; j < kTN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
         for (int64_t kt = 0; kt < ktiles; ++kt, ++g) {
             const int s = static_cast<int>(g % S);
+            float *at = At_s + (g & 1) * kAStageF;
+            if constexpr (PX) {
+                bool w = mbar_wait(&xfull[g & 1], static_cast<uint32_t>((g >> 1) & 1), abort_flag, args.status,
+                                   B2B_DEVSTAT_TIMEOUT | 0x39, args.wait_ns);
+                if (w)
+                    w = mbar_wait(&full[s], static_cast<uint32_t>((g / S) & 1), abort_flag, args.status,
+                                  B2B_DEVSTAT_TIMEOUT | 0x36, args.wait_ns);
+                if (!__all_sync(0xffffffffu, w)) {
+                    ok = false;
+                    break;
+                }
+            } else {
             bool w = mbar_wait(&full[s], static_cast<uint32_t>((g / S) & 1), abort_flag, args.status,
                                B2B_DEVSTAT_TIMEOUT | 0x36, args.wait_ns);
             w = __all_sync(0xffffffffu, w);
-            float *at = At_s + (g & 1) * kAStageF;
             if (w) {
                 const float *src = As + s * kAStageF;
 #pragma unroll
@@ -795,6 +856,7 @@ __global__ void __launch_bounds__(384, 1)
                 ok = false;
                 break;
             }
+            }
             const float *bs = Bs + s * Cf::B_STAGE_F;
             float af[2][kTM], bf[2][kTN];
             load_frags(at, bs, 0, af[0], bf[0]);
@@ -811,7 +873,10 @@ __global__ void __launch_bounds__(384, 1)
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+            if (lane == 0) {
+                mbar_arrive(&empty[s]);
+                if (PX) mbar_arrive(&xempty[g & 1]);
+            }
         }
         if (!ok) break;
         int64_t batch, m0, n0;
@@ -1012,6 +1077,7 @@ int launch_rowa(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, R
     return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm (row-major A) TMA launch");
 }
 
+template <bool PX>
 int launch_rowa_ws(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB, RArgs args, int64_t batch) {
     using Cf = RowaCfg<4, true>;
     {
@@ -1019,8 +1085,8 @@ int launch_rowa_ws(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB
         static bool attr_set[64] = {};
         std::lock_guard<std::mutex> lk(mu);
         if (!attr_set[h->device & 63]) {
-            cudaError_t e =
-                cudaFuncSetAttribute(sgemm_tma_rowa_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+            cudaError_t e = cudaFuncSetAttribute(sgemm_tma_rowa_ws_kernel<PX>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
             if (e != cudaSuccess) return fail_cuda(e, "sgemm (row-major A, persistent) smem attribute");
             attr_set[h->device & 63] = true;
         }
@@ -1030,7 +1096,7 @@ int launch_rowa_ws(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB
     if (args.tiles > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
     // one CTA per SM: its shared memory allows no second one
     const int64_t grid = args.tiles < h->sm_count ? args.tiles : h->sm_count;
-    sgemm_tma_rowa_ws_kernel<<<static_cast<unsigned>(grid), 384, Cf::SMEM, h->stream>>>(tmA, tmB, args);
+    sgemm_tma_rowa_ws_kernel<PX><<<static_cast<unsigned>(grid), 384, Cf::SMEM, h->stream>>>(tmA, tmB, args);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm (row-major A, persistent) TMA launch");
 }
@@ -1047,9 +1113,11 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
     }
     const int64_t tiles_m = (M + kBM - 1) / kBM;
     // The persistent warp-specialised kernel, 128 x 256 tiles with A
-    // transposed in shared memory (4096 x 256^3: 56.4 TFLOP/s, against 54.3
-    // for the one-CTA-per-tile form of variant 26 and 54.1 for the 4-byte A
-    // fragments of variant 24, same box); variant 25 takes the 128 x 128 form
+    // transposed in shared memory by the producer warpgroup (4096 x 256^3:
+    // 58.8 TFLOP/s, against 56.5 when the FFMA warps transpose it behind a
+    // CTA-wide barrier per k-block, variant 27; 54.3 for the one-CTA-per-tile
+    // form of variant 26 and 54.1 for the 4-byte A fragments of variant 24);
+    // variant 25 takes the 128 x 128 form
     // (two CTAs per SM), which measured slower (51.5 vs 54.0): half the B tile
     // per CTA costs more L2 -> SM traffic per flop than overlapping two CTAs'
     // prologues and epilogues saves.
@@ -1070,7 +1138,8 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
     if (narrow) return launch_rowa<2, false>(h, tmA, tmB, args, batch);
     if (plain) return launch_rowa<4, false>(h, tmA, tmB, args, batch);
     if (per_tile) return launch_rowa<4, true>(h, tmA, tmB, args, batch);
-    return launch_rowa_ws(h, tmA, tmB, args, batch);
+    if (h->sgemm_variant == 27) return launch_rowa_ws<false>(h, tmA, tmB, args, batch);
+    return launch_rowa_ws<true>(h, tmA, tmB, args, batch);
 }
 
 }  // namespace b2b

@@ -404,9 +404,9 @@ def test_strided_batched_tma_kernel_bit_identical(monkeypatch, oracle, batch):
     # the cp.async kernel (variant 11) and the TMA kernel's 128 x 256 and
     # 128 x 128 (two CTAs per SM) forms (variants 24, 25) and the form that
     # transposes A in shared memory (26), and its persistent warp-specialised
-    # form (27, the default; 300 batches give each CTA several tiles), with
-    # gaps between
-    # batches and ragged M/N edges.
+    # forms (27: the FFMA warps transpose A; 28 and the default: the producer
+    # warpgroup does; 300 batches give each CTA several tiles), with gaps between batches and
+    # ragged M/N edges.
     import b2blas
 
     m, n, k = 200, 136, 100
@@ -416,7 +416,7 @@ def test_strided_batched_tma_kernel_bit_identical(monkeypatch, oracle, batch):
     C = oracle.uniform_f32(batch * sc, 22, 3)
     cfg = b2blas.GemmConfig(m, n, k, 1.5, 0.5)
     outs = {}
-    for v in ("0", "11", "24", "25", "26", "27"):
+    for v in ("0", "11", "24", "25", "26", "27", "28"):
         monkeypatch.setenv("B2B_SGEMM_VARIANT", v)
         h = b2blas.Handle(0)
         try:
@@ -431,6 +431,7 @@ def test_strided_batched_tma_kernel_bit_identical(monkeypatch, oracle, batch):
     assert np.array_equal(outs["0"], outs["25"])
     assert np.array_equal(outs["0"], outs["26"])
     assert np.array_equal(outs["0"], outs["27"])
+    assert np.array_equal(outs["0"], outs["28"])
     ref = oracle.sgemm_strided_batched_f64(m, n, k, 1.5, A, sa, B, sb, 0.5, C, sc, batch)
     got = np.concatenate([outs["0"][i * sc:i * sc + m * n] for i in range(batch)])
     assert oracle.rel_err(got, ref) <= oracle.tol_normwise(k, "f32")

@@ -215,10 +215,12 @@ def sgemm_ksplit(sm_count, m, n, k):
 
 
 def sgemm_kernels_per_call(m, n, k, tf32x3=False, sm_count=148):
-    """Kernels one single SGEMM call launches: on the TMA-fed FFMA path the
-    transpose of A, the GEMM and, when split-K applies, the reduce; else 1.
-    Mirrors the library's dispatch (run_sgemm in gemm_simt.cu,
-    sgemm_tma_eligible and sgemm_ksplit in sgemm_tma.cu) for 16-byte aligned
+    """Kernels one single SGEMM call launches on the TMA-fed FFMA path: one
+    when unsplit (the persistent row-major-A kernel, which transposes A in
+    shared memory; variant 0 with K % 4 == 0), else the transpose of A, the
+    GEMM and, when split-K applies, the reduce; 1 off that path.  Mirrors
+    the library's dispatch (run_sgemm in gemm_simt.cu, sgemm_tma_eligible,
+    sgemm_ksplit and launch_sgemm_tma in sgemm_tma.cu) for 16-byte aligned
     operands."""
     variant = int(os.environ.get("B2B_SGEMM_VARIANT", "0") or 0)
     if tf32x3 or variant not in (0, 20, 21, 22):
@@ -228,7 +230,17 @@ def sgemm_kernels_per_call(m, n, k, tf32x3=False, sm_count=148):
         return 1
     forced = int(os.environ.get("B2B_SGEMM_KSPLIT", "0") or 0)
     S = forced if forced > 0 else sgemm_ksplit(sm_count, m, n, k)
-    return 3 if S > 1 else 2
+    if S > 1:
+        return 3
+    return 1 if variant == 0 and k % 4 == 0 else 2
+
+
+def sgemm_kernel_name(m, n, k):
+    """The dominant kernel of one single SGEMM call (FFMA path)."""
+    if sgemm_kernels_per_call(m, n, k) == 1 and int(os.environ.get("B2B_SGEMM_VARIANT", "0") or 0) == 0 \
+            and m % 4 == 0 and n % 4 == 0 and m >= 128 and n >= 1024:
+        return "sgemm_tma_rowa_ws_kernel<true> (persistent; A transposed in shared memory)"
+    return "sgemm_tma_kernel"
 
 
 def _cur_stream():
@@ -471,7 +483,7 @@ class GemmWorkload(Workload):
         self.simple = {"hgemm": h.hgemm_simple, "dgemm": h.dgemm_simple,
                        "sgemm": h.sgemm_3xtf32_simple if args.tf32x3 else h.sgemm_simple}[kind]
         self.kernel = {"hgemm": "hgemm_tc2_kernel" if m > 128 else "hgemm_tc_kernel",
-                       "sgemm": "sgemm_tma_kernel", "dgemm": "dgemm_dmma_kernel<32,3>"}[kind]
+                       "sgemm": sgemm_kernel_name(m, self.n, k), "dgemm": "dgemm_dmma_kernel<32,3>"}[kind]
         self.bound = {"hgemm": "tensor", "sgemm": "fma", "dgemm": "fp64"}[kind]
         if kind == "sgemm" and args.tf32x3:
             self.kernel, self.bound = "sgemm_3xtf32_kernel", "tf32x3"
@@ -982,7 +994,9 @@ class MlpWorkload(Workload):
                      min(2, sgemm_kernels_per_call(rows, self.dims[i + 1], self.dims[i])))
                     for _, _, rows in self.lanes for i in range(4)]
         self.launches_per_step = sum(per_gemm) + (0 if self.fused else 4 * self.streams)  # + a saxpy per layer
-        self.kernel = "sgemm_tma_kernel"
+        names = sorted({sgemm_kernel_name(rows, self.dims[i + 1], self.dims[i]) if self.whole_splits[i] <= 1
+                        else "sgemm_tma_kernel" for _, _, rows in self.lanes for i in range(4)})
+        self.kernel = " + ".join(names)
         self.bound = "fma"
 
     def forward(self, xb):

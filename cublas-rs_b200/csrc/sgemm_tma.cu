@@ -54,11 +54,15 @@ constexpr int kAStageF = kBK * kBM;  // floats per stage
 constexpr int kBStageF = kBK * kBN;
 constexpr uint32_t kStageBytes = (kAStageF + kBStageF) * 4;  // 48 KiB
 constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
-constexpr int kGroupM = 8;  // raster group (M tiles sweeping the N tiles together), batched kernel
+constexpr int kGroupM = 8;  // raster group (M tiles sweeping the N tiles together), batched kernels
 // Raster group of the single-GEMM kernel: 64 tile rows (8192 rows) sweep the
 // N tiles together; at 8192^3 that measured 60.7 vs 59.7 TFLOP/s for 8 rows
 // (interleaved A/B, 3 rounds each, the same bits).
 constexpr int kGroupMSingle = 64;
+// Raster group of a single GEMM on the persistent row-major-A kernel: at
+// 8192^3 groups of 8-64 tile rows run at the same 62.0 TFLOP/s, and 16 moves
+// the fewest DRAM bytes (2.81 GB per launch; 8 rows: 3.44 GB).
+constexpr int kGroupMSingleWs = 16;
 
 struct SArgs {
     float *C;
@@ -349,20 +353,21 @@ struct RArgs {
     int relu;
     int *status;
     uint64_t wait_ns;
-    int64_t tiles;  // tiles of the whole call (the persistent form)
+    int64_t tiles;    // tiles of the whole call (the persistent form)
+    int64_t group_m;  // raster group in tile rows
 };
 
 // (batch, first row, first column) of tile t: batches in order, each
-// batch's tiles raster-grouped by kGroupM tile rows.
+// batch's tiles raster-grouped by group_m tile rows.
 __device__ __forceinline__ void rowa_tile(const RArgs &args, int64_t t, int bn, int64_t &batch, int64_t &m0,
                                           int64_t &n0) {
     const int64_t per_batch = args.tiles_m * args.tiles_n;
     batch = t / per_batch;
     const int64_t tb = t - batch * per_batch;
-    const int64_t span = kGroupM * args.tiles_n;
+    const int64_t span = args.group_m * args.tiles_n;
     const int64_t g = tb / span;
-    const int64_t first = g * kGroupM;
-    const int64_t gm = args.tiles_m - first < kGroupM ? args.tiles_m - first : kGroupM;
+    const int64_t first = g * args.group_m;
+    const int64_t gm = args.tiles_m - first < args.group_m ? args.tiles_m - first : args.group_m;
     const int64_t r = tb - g * span;
     m0 = (first + r % gm) * kBM;
     n0 = (r / gm) * bn;
@@ -421,16 +426,8 @@ __global__ void __launch_bounds__(RowaCfg<WN, XP>::THREADS, RowaCfg<WN, XP>::MIN
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * S);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t per_batch = args.tiles_m * args.tiles_n;
-    const int64_t t = blockIdx.x;
-    const int64_t batch = t / per_batch;
-    const int64_t tb = t - batch * per_batch;
-    const int64_t span = kGroupM * args.tiles_n;
-    const int64_t g = tb / span;
-    const int64_t first = g * kGroupM;
-    const int64_t gm = args.tiles_m - first < kGroupM ? args.tiles_m - first : kGroupM;
-    const int64_t r = tb - g * span;
-    const int64_t m0 = (first + r % gm) * kBM, n0 = (r / gm) * Cf::BN;
+    int64_t batch, m0, n0;
+    rowa_tile(args, blockIdx.x, Cf::BN, batch, m0, n0);
     const int64_t ktiles = (args.K + kBK - 1) / kBK;
 
     if (tid == 0) {
@@ -992,6 +989,12 @@ int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha
     if (S > ktiles) S = static_cast<int>(ktiles);
     if (S < 1) S = 1;
     const int64_t kbps = (ktiles + S - 1) / S;
+    // Unsplit: the persistent warp-specialised kernel on row-major A, whose
+    // producer warpgroup transposes A in shared memory -- no transpose pass
+    // through global memory and no workspace, the same bits.
+    if (S == 1 && pk == 1 && h->sgemm_variant == 0 &&
+        sgemm_tma_rowa_eligible(M, N, K, M * K, K * N, M * N, 1, A, B, C))
+        return launch_sgemm_tma_rowa(h, M, N, K, alpha, beta, A, M * K, B, K * N, C, M * N, 1, bias, relu);
     const size_t at_bytes = (static_cast<size_t>(M) * static_cast<size_t>(K) * 4 + 255) / 256 * 256;
     const size_t part_bytes = S > 1 ? static_cast<size_t>(S) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4 : 0;
     void *ws = nullptr;
@@ -1134,7 +1137,8 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
                        static_cast<uint64_t>(batch), static_cast<uint64_t>(N) * 4, static_cast<uint64_t>(sB) * 4, bn,
                        kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    RArgs args{C, M, N, K, sC, tiles_m, 0, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns, 0};
+    const int64_t group_m = batch > 1 ? kGroupM : (h->sgemm_group_m > 0 ? h->sgemm_group_m : kGroupMSingleWs);
+    RArgs args{C, M, N, K, sC, tiles_m, 0, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns, 0, group_m};
     if (narrow) return launch_rowa<2, false>(h, tmA, tmB, args, batch);
     if (plain) return launch_rowa<4, false>(h, tmA, tmB, args, batch);
     if (per_tile) return launch_rowa<4, true>(h, tmA, tmB, args, batch);

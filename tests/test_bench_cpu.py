@@ -43,15 +43,19 @@ def test_reference_arm_other_ranks_exit_quietly():
 
 
 def test_sgemm_kernels_per_call(monkeypatch):
-    # The TMA-fed SGEMM path is two launches (transpose of A, GEMM); the
-    # others are one.  Mirrors sgemm_tma_eligible.
+    # The TMA-fed SGEMM path is one launch unsplit (the persistent kernel on
+    # row-major A), two for the forced transposed-A forms (transpose of A,
+    # GEMM) and three with split-K; the others are one.  Mirrors
+    # sgemm_tma_eligible.
     sys.path.insert(0, ROOT)
     import bench
 
     monkeypatch.delenv("B2B_SGEMM_VARIANT", raising=False)
     monkeypatch.delenv("B2B_SGEMM_KSPLIT", raising=False)
-    assert bench.sgemm_kernels_per_call(8192, 8192, 8192) == 2
-    assert bench.sgemm_kernels_per_call(4096, 1024, 4096) == 2
+    assert bench.sgemm_kernels_per_call(8192, 8192, 8192) == 1
+    assert bench.sgemm_kernels_per_call(4096, 1024, 4096) == 1
+    assert bench.sgemm_kernels_per_call(4096, 1024, 4098) == 2  # K % 4 != 0: transposed-A kernel
+    assert bench.sgemm_kernel_name(8192, 8192, 8192).startswith("sgemm_tma_rowa_ws_kernel")
     # split-K adds the reduce: grids under one wave, or just past a whole one
     assert bench.sgemm_ksplit(148, 1024, 1024, 1024) == 4
     assert bench.sgemm_ksplit(148, 4096, 4096, 4096) == 2
@@ -59,7 +63,7 @@ def test_sgemm_kernels_per_call(monkeypatch):
     assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 3
     assert bench.sgemm_kernels_per_call(2048, 1024, 4096) == 3
     monkeypatch.setenv("B2B_SGEMM_KSPLIT", "1")
-    assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 2
+    assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 1
     monkeypatch.delenv("B2B_SGEMM_KSPLIT")
     assert bench.sgemm_kernels_per_call(512, 512, 512) == 1        # N < 1024
     assert bench.sgemm_kernels_per_call(100, 2048, 64) == 1        # M < 128

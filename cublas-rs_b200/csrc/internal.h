@@ -140,9 +140,13 @@ int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha
 // batched over 3-D tensor maps; batch 1 for a single GEMM.
 bool sgemm_tma_rowa_eligible(int64_t M, int64_t N, int64_t K, int64_t sA, int64_t sB, int64_t sC, int64_t batch,
                              const void *A, const void *B, const void *C);
+// ksplit > 1 (batch 1 only): split-K on the persistent kernel, raw partial
+// sums of split s to partial[s][M][N] (kb_per_split k-blocks each); the
+// caller runs the reduce.
 int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
                           int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch,
-                          const float *bias, int relu);
+                          const float *bias, int relu, int ksplit = 1, int64_t kb_per_split = 0,
+                          float *partial = nullptr);
 int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
                       const double *B, double *C);
 int launch_sgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A, const float *x,

@@ -353,8 +353,14 @@ struct RArgs {
     int relu;
     int *status;
     uint64_t wait_ns;
-    int64_t tiles;    // tiles of the whole call (the persistent form)
+    int64_t tiles;    // work units of the whole call (the persistent form): tiles x splits
     int64_t group_m;  // raster group in tile rows
+    // Split-K (the persistent form, batch 1): unit u is split u / tiles' k
+    // blocks [s * kb_per_split, ...) of tile u % tiles, whose raw sums go to
+    // partial[s][M][N]; sgemm_splitk_reduce_kernel finishes the outputs.
+    int ksplit;
+    int64_t kb_per_split;
+    float *partial;
 };
 
 // (batch, first row, first column) of tile t: batches in order, each
@@ -371,6 +377,25 @@ __device__ __forceinline__ void rowa_tile(const RArgs &args, int64_t t, int bn, 
     const int64_t r = tb - g * span;
     m0 = (first + r % gm) * kBM;
     n0 = (r / gm) * bn;
+}
+
+// Work unit u of the persistent form: its tile (rowa_tile), split and k
+// blocks [kb0, kb0 + nk).
+__device__ __forceinline__ void rowa_unit(const RArgs &args, int64_t u, int bn, int64_t ktiles_all,
+                                          int64_t &batch, int64_t &m0, int64_t &n0, int64_t &split, int64_t &kb0,
+                                          int64_t &nk) {
+    split = 0;
+    kb0 = 0;
+    nk = ktiles_all;
+    if (args.ksplit > 1) {
+        const int64_t per_split = args.tiles / args.ksplit;
+        split = u / per_split;
+        u -= split * per_split;
+        kb0 = split * args.kb_per_split;
+        nk = ktiles_all - kb0 < args.kb_per_split ? ktiles_all - kb0 : args.kb_per_split;
+        if (nk < 0) nk = 0;
+    }
+    rowa_tile(args, u, bn, batch, m0, n0);
 }
 
 template <int WN, bool XP>
@@ -726,8 +751,10 @@ __global__ void __launch_bounds__(384, 1)
             const int xt = tid - NC - 32;
             int64_t g = 0;
             for (int64_t ti = 0; ti < ntiles; ++ti) {
+                int64_t batch, m0, n0, split, kb0, nk;
+                rowa_unit(args, blockIdx.x + ti * gridDim.x, Cf::BN, ktiles, batch, m0, n0, split, kb0, nk);
                 bool w = true;
-                for (int64_t kt = 0; kt < ktiles && w; ++kt, ++g) {
+                for (int64_t kt = 0; kt < nk && w; ++kt, ++g) {
                     const int s = static_cast<int>(g % S), b = static_cast<int>(g & 1);
                     w = mbar_wait(&full[s], static_cast<uint32_t>((g / S) & 1), abort_flag, args.status,
                                   B2B_DEVSTAT_TIMEOUT | 0x37, args.wait_ns);
@@ -758,9 +785,9 @@ __global__ void __launch_bounds__(384, 1)
             int64_t g = 0;
             bool ok = true;
             for (int64_t ti = 0; ti < ntiles && ok; ++ti) {
-                int64_t batch, m0, n0;
-                rowa_tile(args, blockIdx.x + ti * gridDim.x, Cf::BN, batch, m0, n0);
-                for (int64_t kt = 0; kt < ktiles; ++kt, ++g) {
+                int64_t batch, m0, n0, split, kb0, nk;
+                rowa_unit(args, blockIdx.x + ti * gridDim.x, Cf::BN, ktiles, batch, m0, n0, split, kb0, nk);
+                for (int64_t kt = 0; kt < nk; ++kt, ++g) {
                     const int s = static_cast<int>(g % S);
                     if (g >= S && !mbar_wait(&empty[s], static_cast<uint32_t>((g / S - 1) & 1), abort_flag,
                                              args.status, B2B_DEVSTAT_TIMEOUT | 0x35, args.wait_ns)) {
@@ -768,10 +795,10 @@ __global__ void __launch_bounds__(384, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
-                    tma_load_3d(As + s * kAStageF, &tmA, &full[s], static_cast<int32_t>(kt * kBK),
+                    tma_load_3d(As + s * kAStageF, &tmA, &full[s], static_cast<int32_t>((kb0 + kt) * kBK),
                                 static_cast<int32_t>(m0), static_cast<int32_t>(batch));
                     tma_load_3d(Bs + s * Cf::B_STAGE_F, &tmB, &full[s], static_cast<int32_t>(n0),
-                                static_cast<int32_t>(kt * kBK), static_cast<int32_t>(batch));
+                                static_cast<int32_t>((kb0 + kt) * kBK), static_cast<int32_t>(batch));
                 }
             }
             if (!ok && g > 0) {
@@ -819,7 +846,12 @@ __global__ void __launch_bounds__(384, 1)
         for (int i = 0; i < kTM / 2; ++i)
 #pragma unroll
             for (int j = 0; j < kTN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
-        for (int64_t kt = 0; kt < ktiles; ++kt, ++g) {
+        int64_t nk;
+        {
+            int64_t b_, m_, n_, s_, k_;
+            rowa_unit(args, blockIdx.x + ti * gridDim.x, Cf::BN, ktiles, b_, m_, n_, s_, k_, nk);
+        }
+        for (int64_t kt = 0; kt < nk; ++kt, ++g) {
             const int s = static_cast<int>(g % S);
             float *at = At_s + (g & 1) * kAStageF;
             if constexpr (PX) {
@@ -876,8 +908,26 @@ __global__ void __launch_bounds__(384, 1)
             }
         }
         if (!ok) break;
-        int64_t batch, m0, n0;
-        rowa_tile(args, blockIdx.x + ti * gridDim.x, Cf::BN, batch, m0, n0);
+        int64_t batch, m0, n0, split, kb0, nk_;
+        rowa_unit(args, blockIdx.x + ti * gridDim.x, Cf::BN, ktiles, batch, m0, n0, split, kb0, nk_);
+        if (args.ksplit > 1) {
+            // raw sums of this k range; the reduce applies alpha, beta, bias, ReLU
+            float *P = args.partial + split * args.M * args.N;
+#pragma unroll
+            for (int i = 0; i < kTM; ++i) {
+                const int64_t row = m0 + row_base + (i >> 2) * 16 + (i & 3);
+                if (row >= args.M) continue;
+#pragma unroll
+                for (int gj = 0; gj < kTN / 4; ++gj) {
+                    const int64_t col = n0 + col_base + gj * 32;
+                    if (col >= args.N) continue;
+                    *reinterpret_cast<float4 *>(P + row * args.N + col) =
+                        make_float4(acc_at(i, gj * 4 + 0), acc_at(i, gj * 4 + 1), acc_at(i, gj * 4 + 2),
+                                    acc_at(i, gj * 4 + 3));
+                }
+            }
+            continue;
+        }
         float *Cb = args.C + batch * args.sC;
         const bool read_c = args.beta != 0.0f;
 #pragma unroll
@@ -989,14 +1039,34 @@ int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha
     if (S > ktiles) S = static_cast<int>(ktiles);
     if (S < 1) S = 1;
     const int64_t kbps = (ktiles + S - 1) / S;
-    // Unsplit: the persistent warp-specialised kernel on row-major A, whose
-    // producer warpgroup transposes A in shared memory -- no transpose pass
-    // through global memory and no workspace, the same bits.
-    if (S == 1 && pk == 1 && h->sgemm_variant == 0 &&
-        sgemm_tma_rowa_eligible(M, N, K, M * K, K * N, M * N, 1, A, B, C))
-        return launch_sgemm_tma_rowa(h, M, N, K, alpha, beta, A, M * K, B, K * N, C, M * N, 1, bias, relu);
-    const size_t at_bytes = (static_cast<size_t>(M) * static_cast<size_t>(K) * 4 + 255) / 256 * 256;
     const size_t part_bytes = S > 1 ? static_cast<size_t>(S) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4 : 0;
+    auto reduce = [&](const float *partial) -> int {
+        const int64_t quads = M * N / 4;
+        int64_t blocks = (quads + 255) / 256;
+        const int64_t cap = 8LL * h->sm_count;
+        if (blocks > cap) blocks = cap;
+        sgemm_splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, h->stream>>>(partial, S, M, N, C, alpha,
+                                                                                          beta, bias, relu);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? B2B_OK : fail_cuda(e, "sgemm split-K reduce launch");
+    };
+    // The persistent warp-specialised kernel on row-major A, whose producer
+    // warpgroup transposes A in shared memory: no transpose pass through
+    // global memory, workspace only for a split's partial sums, the same bits
+    // (each split sums its k range from zero, as below).
+    if (pk == 1 && h->sgemm_variant == 0 && sgemm_tma_rowa_eligible(M, N, K, M * K, K * N, M * N, 1, A, B, C)) {
+        float *partial = nullptr;
+        if (S > 1) {
+            void *pws = nullptr;
+            if (int rc = workspace(h, part_bytes, &pws)) return rc;
+            partial = static_cast<float *>(pws);
+        }
+        if (int rc = launch_sgemm_tma_rowa(h, M, N, K, alpha, beta, A, M * K, B, K * N, C, M * N, 1, bias, relu, S,
+                                           kbps, partial))
+            return rc;
+        return S > 1 ? reduce(partial) : B2B_OK;
+    }
+    const size_t at_bytes = (static_cast<size_t>(M) * static_cast<size_t>(K) * 4 + 255) / 256 * 256;
     void *ws = nullptr;
     if (int rc = workspace(h, at_bytes + part_bytes, &ws)) return rc;
     float *At = static_cast<float *>(ws);
@@ -1029,17 +1099,7 @@ int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha
     kern<<<static_cast<unsigned>(tiles * S), kThreads, kSmem, h->stream>>>(tmAt, tmB, args);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "sgemm TMA launch");
-    if (S > 1) {
-        const int64_t quads = M * N / 4;
-        int64_t blocks = (quads + 255) / 256;
-        const int64_t cap = 8LL * h->sm_count;
-        if (blocks > cap) blocks = cap;
-        sgemm_splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, h->stream>>>(partial, S, M, N, C, alpha,
-                                                                                          beta, bias, relu);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return fail_cuda(e, "sgemm split-K reduce launch");
-    }
-    return B2B_OK;
+    return S > 1 ? reduce(partial) : B2B_OK;
 }
 
 bool sgemm_tma_rowa_eligible(int64_t M, int64_t N, int64_t K, int64_t sA, int64_t sB, int64_t sC, int64_t batch,
@@ -1095,7 +1155,7 @@ int launch_rowa_ws(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB
         }
     }
     args.tiles_n = (args.N + Cf::BN - 1) / Cf::BN;
-    args.tiles = args.tiles_m * args.tiles_n * batch;
+    args.tiles = args.tiles_m * args.tiles_n * batch * (args.ksplit > 1 ? args.ksplit : 1);
     if (args.tiles > 0x7fffffffLL) return fail(B2B_ERR_INVALID_ARG, "sgemm: grid exceeds 2^31-1 tiles");
     // one CTA per SM: its shared memory allows no second one
     const int64_t grid = args.tiles < h->sm_count ? args.tiles : h->sm_count;
@@ -1108,7 +1168,9 @@ int launch_rowa_ws(b2b_handle *h, const CUtensorMap &tmA, const CUtensorMap &tmB
 
 int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
                           int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch,
-                          const float *bias, int relu) {
+                          const float *bias, int relu, int ksplit, int64_t kb_per_split, float *partial) {
+    if (ksplit > 1 && (batch != 1 || h->sgemm_variant != 0 || partial == nullptr || kb_per_split <= 0))
+        return fail(B2B_ERR_INVALID_ARG, "sgemm: split-K takes the persistent kernel on one GEMM only");
     if (batch == 1) {  // a single GEMM: the batch pitch is never used, keep it a legal multiple of 16
         sA = M * K;
         sB = K * N;
@@ -1138,7 +1200,9 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
                        kBK, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     const int64_t group_m = batch > 1 ? kGroupM : (h->sgemm_group_m > 0 ? h->sgemm_group_m : kGroupMSingleWs);
-    RArgs args{C, M, N, K, sC, tiles_m, 0, alpha, beta, bias, relu, h->d_status, h->wait_limit_ns, 0, group_m};
+    RArgs args{C,       M,          N,           K,    sC,      tiles_m, 0,      alpha,
+               beta,    bias,       relu,        h->d_status, h->wait_limit_ns, 0, group_m,
+               ksplit > 1 ? ksplit : 1, kb_per_split, partial};
     if (narrow) return launch_rowa<2, false>(h, tmA, tmB, args, batch);
     if (plain) return launch_rowa<4, false>(h, tmA, tmB, args, batch);
     if (per_tile) return launch_rowa<4, true>(h, tmA, tmB, args, batch);

@@ -43,9 +43,9 @@ def test_reference_arm_other_ranks_exit_quietly():
 
 
 def test_sgemm_kernels_per_call(monkeypatch):
-    # The TMA-fed SGEMM path is one launch unsplit (the persistent kernel on
-    # row-major A), two for the forced transposed-A forms (transpose of A,
-    # GEMM) and three with split-K; the others are one.  Mirrors
+    # The TMA-fed SGEMM path is the persistent kernel on row-major A (one
+    # launch), or for the forced transposed-A forms the transpose of A and
+    # the GEMM; split-K adds the reduce.  The others are one.  Mirrors
     # sgemm_tma_eligible.
     sys.path.insert(0, ROOT)
     import bench
@@ -60,8 +60,10 @@ def test_sgemm_kernels_per_call(monkeypatch):
     assert bench.sgemm_ksplit(148, 1024, 1024, 1024) == 4
     assert bench.sgemm_ksplit(148, 4096, 4096, 4096) == 2
     assert bench.sgemm_ksplit(148, 8192, 8192, 8192) == 1
-    assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 3
-    assert bench.sgemm_kernels_per_call(2048, 1024, 4096) == 3
+    assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 2   # persistent GEMM + reduce
+    assert bench.sgemm_kernels_per_call(2048, 1024, 4096) == 2
+    assert bench.sgemm_kernels_per_call(1024, 1024, 1022) == 3   # K % 4 != 0: transpose + GEMM + reduce
+    assert bench.sgemm_kernels_per_call(512, 4096, 4096, splits=2) == 2
     monkeypatch.setenv("B2B_SGEMM_KSPLIT", "1")
     assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 1
     monkeypatch.delenv("B2B_SGEMM_KSPLIT")

@@ -865,26 +865,26 @@ __global__ void __launch_bounds__(384, 1)
                     break;
                 }
             } else {
-            bool w = mbar_wait(&full[s], static_cast<uint32_t>((g / S) & 1), abort_flag, args.status,
-                               B2B_DEVSTAT_TIMEOUT | 0x36, args.wait_ns);
-            w = __all_sync(0xffffffffu, w);
-            if (w) {
-                const float *src = As + s * kAStageF;
+                bool w = mbar_wait(&full[s], static_cast<uint32_t>((g / S) & 1), abort_flag, args.status,
+                                   B2B_DEVSTAT_TIMEOUT | 0x36, args.wait_ns);
+                w = __all_sync(0xffffffffu, w);
+                if (w) {
+                    const float *src = As + s * kAStageF;
 #pragma unroll
-                for (int r = 0; r < 1024 / NC; ++r) {
-                    const int q = r * NC + tid;
-                    const int m = q & 127, c = q >> 7;
-                    const float4 v = *reinterpret_cast<const float4 *>(src + m * 32 + ((c ^ (m & 7)) << 2));
-                    at[(4 * c + 0) * kBM + m] = v.x;
-                    at[(4 * c + 1) * kBM + m] = v.y;
-                    at[(4 * c + 2) * kBM + m] = v.z;
-                    at[(4 * c + 3) * kBM + m] = v.w;
+                    for (int r = 0; r < 1024 / NC; ++r) {
+                        const int q = r * NC + tid;
+                        const int m = q & 127, c = q >> 7;
+                        const float4 v = *reinterpret_cast<const float4 *>(src + m * 32 + ((c ^ (m & 7)) << 2));
+                        at[(4 * c + 0) * kBM + m] = v.x;
+                        at[(4 * c + 1) * kBM + m] = v.y;
+                        at[(4 * c + 2) * kBM + m] = v.z;
+                        at[(4 * c + 3) * kBM + m] = v.w;
+                    }
                 }
-            }
-            if (!bar1_and(w, NC)) {
-                ok = false;
-                break;
-            }
+                if (!bar1_and(w, NC)) {
+                    ok = false;
+                    break;
+                }
             }
             const float *bs = Bs + s * Cf::B_STAGE_F;
             float af[2][kTM], bf[2][kTN];

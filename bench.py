@@ -485,7 +485,7 @@ class GemmWorkload(Workload):
         self.simple = {"hgemm": h.hgemm_simple, "dgemm": h.dgemm_simple,
                        "sgemm": h.sgemm_3xtf32_simple if args.tf32x3 else h.sgemm_simple}[kind]
         self.kernel = {"hgemm": "hgemm_tc2_kernel" if m > 128 else "hgemm_tc_kernel",
-                       "sgemm": sgemm_kernel_name(m, self.n, k), "dgemm": "dgemm_dmma_kernel<32,3>"}[kind]
+                       "sgemm": sgemm_kernel_name(m, self.n, k), "dgemm": "dgemm_dmma_ws_kernel<32,3> (persistent)"}[kind]
         self.bound = {"hgemm": "tensor", "sgemm": "fma", "dgemm": "fp64"}[kind]
         if kind == "sgemm" and args.tf32x3:
             self.kernel, self.bound = "sgemm_3xtf32_kernel", "tf32x3"

@@ -25,6 +25,7 @@
 #include <stdint.h>
 
 #include "internal.h"
+#include "sm100.cuh"
 
 namespace {
 
@@ -188,6 +189,188 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Persistent warp-specialised form: 8 DMMA warps (the same 2 x 4 warps of
+// 64 x 32 and fragment code as dgemm_dmma_kernel) and a producer warpgroup
+// that fills the cp.async ring.  Each producer thread copies its 32 chunks of
+// a stage, then cp.async.mbarrier.arrive.noinc makes the stage's "full"
+// barrier (count 128) complete once all of its copies have landed; the DMMA
+// warps wait on "full", run the stage's k steps and arrive on "empty"
+// (count 8), which the producer waits on before refilling the stage.  The
+// DMMA loop thus meets no CTA-wide barrier, and the producer loads the next
+// tile's first stages while the DMMA warps store the current one.  CTA b takes
+// tiles b, b + gridDim.x, ... in the grouped raster order.  Same per-element
+// arithmetic (and bits) as dgemm_dmma_kernel.  384 threads launched at 168
+// registers (64512 in all); the producer warpgroup keeps 56 and the DMMA
+// warps take 224 (128 x 56 + 256 x 224 = 64512).
+constexpr int kWsThreads = 384;
+constexpr int kWsProducers = 128;
+
+struct DWsArgs {
+    int64_t tiles;  // tiles of the call
+    int *status;
+    uint64_t wait_ns;
+};
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(sm100::smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void dtile_coords(const DTileMap &tmap, int64_t t, int64_t &m0, int64_t &n0) {
+    const int64_t span = 8 * tmap.tiles_n;
+    const int64_t g = t / span;
+    const int64_t first = g * 8;
+    const int64_t gm = tmap.tiles_m - first < 8 ? tmap.tiles_m - first : 8;
+    const int64_t r = t - g * span;
+    m0 = (first + r % gm) * kBM;
+    n0 = (r / gm) * kBN;
+}
+
+template <int BK_, int STAGES_>
+__global__ void __launch_bounds__(kWsThreads, 1)
+    dgemm_dmma_ws_kernel(const double *__restrict__ A, const double *__restrict__ B, double *__restrict__ C,
+                         int64_t M, int64_t N, int64_t K, double alpha, double beta, DTileMap tmap, DWsArgs args) {
+    using namespace sm100;
+    using Cf = DCfg<BK_, STAGES_>;
+    constexpr int kBK = Cf::kBK, kStages = Cf::kStages, kLdA = Cf::kLdA, kAStage = Cf::kAStage,
+                  kBStage = Cf::kBStage;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    double *As = reinterpret_cast<double *>(smem_raw);
+    double *Bs = As + kStages * kAStage;
+    uint64_t *full = reinterpret_cast<uint64_t *>(Bs + kStages * kBStage);
+    uint64_t *empty = full + kStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t ktiles = (K + kBK - 1) / kBK;
+    const int64_t ntiles = (args.tiles - static_cast<int64_t>(blockIdx.x) + gridDim.x - 1) / gridDim.x;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], kWsProducers);
+            mbar_init(&empty[s], kThreads / 32);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp >= kThreads / 32) {
+        // ------------------------------------------------ producer warpgroup
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+        const int pt = tid - kThreads;
+        // Chunk q (0..2047) of a stage: A row q / (kBK / 2), doubles 2 (q % (kBK / 2)) ..;
+        // B row q / (kBN / 2), columns 2 (q % (kBN / 2)) ..
+        const uint32_t as0 = static_cast<uint32_t>(__cvta_generic_to_shared(As));
+        const uint32_t bs0 = static_cast<uint32_t>(__cvta_generic_to_shared(Bs));
+        int64_t g = 0;
+        bool ok = true;
+        for (int64_t ti = 0; ti < ntiles && ok; ++ti) {
+            int64_t m0, n0;
+            dtile_coords(tmap, static_cast<int64_t>(blockIdx.x) + ti * gridDim.x, m0, n0);
+            for (int64_t kt = 0; kt < ktiles; ++kt, ++g) {
+                const int s = static_cast<int>(g % kStages);
+                if (g >= kStages) {
+                    bool w = mbar_wait(&empty[s], static_cast<uint32_t>((g / kStages - 1) & 1), abort_flag,
+                                       args.status, B2B_DEVSTAT_TIMEOUT | 0x41, args.wait_ns);
+                    if (!__all_sync(0xffffffffu, w)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                const int64_t k0 = kt * kBK;
+#pragma unroll 4
+                for (int q = pt; q < kBM * kBK / 2; q += kWsProducers) {
+                    const int r = q / (kBK / 2), c = (q % (kBK / 2)) * 2;
+                    const bool in = m0 + r < M && k0 + c < K;  // K even: the pair is all in or all out
+                    cp16(as0 + static_cast<uint32_t>((s * kAStage + r * kLdA + c) * 8),
+                         in ? A + (m0 + r) * K + k0 + c : A, in);
+                }
+#pragma unroll 4
+                for (int q = pt; q < kBK * kBN / 2; q += kWsProducers) {
+                    const int r = q / (kBN / 2), c = (q % (kBN / 2)) * 2;
+                    const bool in = k0 + r < K && n0 + c < N;  // N even
+                    cp16(bs0 + static_cast<uint32_t>((s * kBStage + r * kLdB + c) * 8),
+                         in ? B + (k0 + r) * N + n0 + c : B, in);
+                }
+                cp_async_arrive_noinc(&full[s]);
+            }
+        }
+        // Copies still in flight land before the CTA's shared memory goes away.
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        return;
+    }
+
+    // ---------------------------------------------------- DMMA warps
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
+    const int wm0 = (warp / kWarpsN) * kMT * 8, wn0 = (warp % kWarpsN) * kNT * 8;
+    const int fr = lane >> 2, fc = lane & 3;
+    int64_t g = 0;
+    bool ok = true;
+#pragma unroll 1
+    for (int64_t ti = 0; ti < ntiles && ok; ++ti) {
+        double acc[kMT][kNT][2];
+#pragma unroll
+        for (int i = 0; i < kMT; ++i)
+#pragma unroll
+            for (int j = 0; j < kNT; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+        for (int64_t kt = 0; kt < ktiles; ++kt, ++g) {
+            const int stage = static_cast<int>(g % kStages);
+            bool w = mbar_wait(&full[stage], static_cast<uint32_t>((g / kStages) & 1), abort_flag, args.status,
+                               B2B_DEVSTAT_TIMEOUT | 0x42, args.wait_ns);
+            if (!__all_sync(0xffffffffu, w)) {
+                ok = false;
+                break;
+            }
+            const double *as = As + stage * kAStage + (wm0 + fr) * kLdA + fc;
+            const double *bs = Bs + stage * kBStage + fc * kLdB + wn0 + fr;
+            double af[2][kMT], bf[2][kNT];
+#pragma unroll
+            for (int i = 0; i < kMT; ++i) af[0][i] = as[i * 8 * kLdA];
+#pragma unroll
+            for (int j = 0; j < kNT; ++j) bf[0][j] = bs[j * 8];
+#pragma unroll
+            for (int ks = 0; ks < kBK / 4; ++ks) {
+                const int cur = ks & 1;
+                if (ks + 1 < kBK / 4) {
+#pragma unroll
+                    for (int i = 0; i < kMT; ++i) af[cur ^ 1][i] = as[i * 8 * kLdA + (ks + 1) * 4];
+#pragma unroll
+                    for (int j = 0; j < kNT; ++j) bf[cur ^ 1][j] = bs[(ks + 1) * 4 * kLdB + j * 8];
+                }
+#pragma unroll
+                for (int i = 0; i < kMT; ++i)
+#pragma unroll
+                    for (int j = 0; j < kNT; ++j) dmma_8x8x4(acc[i][j], af[cur][i], bf[cur][j]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+        }
+        if (!ok) break;
+        int64_t m0, n0;
+        dtile_coords(tmap, static_cast<int64_t>(blockIdx.x) + ti * gridDim.x, m0, n0);
+        const bool read_c = beta != 0.0;
+#pragma unroll
+        for (int i = 0; i < kMT; ++i) {
+            const int64_t row = m0 + wm0 + i * 8 + fr;
+            if (row >= M) continue;
+            double *crow = C + row * N;
+#pragma unroll
+            for (int j = 0; j < kNT; ++j) {
+                const int64_t col = n0 + wn0 + j * 8 + 2 * fc;
+                if (col >= N) continue;  // N even: both columns in range
+                double2 o = make_double2(alpha * acc[i][j][0], alpha * acc[i][j][1]);
+                double2 *dst = reinterpret_cast<double2 *>(crow + col);
+                if (read_c) {
+                    const double2 old = *dst;
+                    o.x = fma(beta, old.x, o.x);
+                    o.y = fma(beta, old.y, o.y);
+                }
+                *dst = o;
+            }
+        }
+    }
+}
+
 }  // namespace
 
 namespace b2b {
@@ -213,14 +396,38 @@ int launch_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, do
     if (e != cudaSuccess) return fail_cuda(e, "dgemm launch");
     return B2B_OK;
 }
+template <int BK_, int STAGES_>
+int launch_dmma_ws(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
+                   const double *B, double *C) {
+    using Cf = DCfg<BK_, STAGES_>;
+    constexpr int smem = Cf::kSmem + 2 * Cf::kStages * 8 + 16;  // + full/empty barriers, abort flag
+    static_assert(smem <= 232448, "shared memory per CTA");
+    DTileMap tm{(M + kBM - 1) / kBM, (N + kBN - 1) / kBN};
+    const int64_t tiles = tm.tiles_m * tm.tiles_n;
+    auto kern = dgemm_dmma_ws_kernel<BK_, STAGES_>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) {
+        // one CTA per SM: its shared memory allows no second one
+        const int64_t grid = tiles < h->sm_count ? tiles : h->sm_count;
+        kern<<<static_cast<unsigned>(grid), kWsThreads, smem, h->stream>>>(A, B, C, M, N, K, alpha, beta, tm,
+                                                                           DWsArgs{tiles, h->d_status,
+                                                                                   h->wait_limit_ns});
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return fail_cuda(e, "dgemm (persistent) launch");
+    return B2B_OK;
+}
 }  // namespace
 
 int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
                       const double *B, double *C) {
-    // k-tile 32, 3 stages: 32.1 TF/s at 4096^3 (k-tile 16 with 3 or 4 stages:
-    // 31.4-31.6; k-tile 32 with 2 stages: 31.9).  Variant 7 keeps k-tile 16.
+    // The persistent warp-specialised form, k-tile 32, 3 stages: 32.8 TF/s at
+    // 4096^3 against 32.1 for dgemm_dmma_kernel<32, 3> (variant 8) and
+    // 32.2-32.4 for the persistent form with k-tile 16 and 4-5 stages, same
+    // bits.  dgemm_dmma_kernel with k-tile 16 (variant 7): 31.4-31.6.
     if (h->dgemm_variant == 7) return launch_dmma<16, 3>(h, M, N, K, alpha, beta, A, B, C);
-    return launch_dmma<32, 3>(h, M, N, K, alpha, beta, A, B, C);
+    if (h->dgemm_variant == 8) return launch_dmma<32, 3>(h, M, N, K, alpha, beta, A, B, C);
+    return launch_dmma_ws<32, 3>(h, M, N, K, alpha, beta, A, B, C);
 }
 
 }  // namespace b2b

@@ -222,6 +222,33 @@ def test_dgemm_4096_full_size_sampled(handle, oracle):
         assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= oracle.tol_normwise(k, "f64"), r
 
 
+@pytest.mark.parametrize("m,n,k,beta", [(1000, 1002, 998, 0.5), (2176, 2048, 512, 0.0), (130, 4096, 64, 0.5)])
+def test_dgemm_persistent_kernel_bit_identical(monkeypatch, oracle, m, n, k, beta):
+    # The persistent warp-specialised DMMA kernel (the default) against the
+    # one-CTA-per-tile kernel (variant 8): same per-element arithmetic, so the
+    # same bits.  2176 x 2048 is 272 tiles, so CTAs take two tiles each and the
+    # producer streams across a tile boundary; ragged edges in M, N and K.
+    import b2blas
+
+    A = oracle.uniform_f64(m * k, 31, 1)
+    B = oracle.uniform_f64(k * n, 31, 2)
+    C = oracle.uniform_f64(m * n, 31, 3)
+    cfg = b2blas.GemmConfig(m, n, k, 1.5, beta)
+    outs = {}
+    for v in ("0", "8"):
+        monkeypatch.setenv("B2B_DGEMM_VARIANT", v)
+        h = b2blas.Handle(0)
+        try:
+            outs[v] = _gemm_dev(h, "dgemm", None, cfg, A, B, C)
+        finally:
+            h.close()
+    assert np.array_equal(outs["0"], outs["8"])
+    got = outs["0"].reshape(m, n)
+    for r in (0, m // 2 + 1, m - 1):
+        ref = oracle.dgemm_f64(m, n, k, 1.5, A, B, beta, C, row0=r, nrows=1)
+        assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= oracle.tol_normwise(k, "f64"), r
+
+
 # ------------------------------------------------------- batched family
 
 @pytest.mark.parametrize("batch,m,n,k,gap", [(8, 64, 64, 64, 0), (33, 17, 29, 13, 3), (4, 256, 256, 256, 0),

@@ -17,6 +17,11 @@
 //     t/4, element t%4 of A; row t%4, column t/4 of B) hit 16 distinct 8-byte
 //     bank slots per half-warp -- no conflicts.
 //   * Fragments are double-buffered in registers across k steps.
+//   * Two kernels share that layout: dgemm_dmma_ws_kernel (the default) is
+//     persistent, with a producer warpgroup that fills the ring and signals
+//     mbarriers, so the DMMA warps never meet a CTA-wide barrier;
+//     dgemm_dmma_kernel (one CTA per tile, all warps copy and meet at a
+//     __syncthreads per k-tile) is kept for comparison.
 // Fragment layout of m8n8k4 .f64: A (8x4, row): thread t holds A[t/4][t%4];
 // B (4x8, col): B[t%4][t/4]; C/D (8x8): C[t/4][2(t%4)], C[t/4][2(t%4)+1].
 // Requires K and N even and 16-byte aligned operands (else the CUDA-core

@@ -401,9 +401,10 @@ def test_sgemm_ffma_kernels_bit_identical(monkeypatch, oracle, m, n, k, alpha, b
     # Every FP32 FFMA kernel sums each output over k in order with one fma per
     # step, so the forms must agree bit for bit: the cp.async kernel (variant
     # 11), the TMA-fed kernel on a transposed A with scalar FFMA (20), FFMA2
-    # on row pairs (21, the default), FFMA2 on column pairs (22), and the
-    # TMA-fed kernel on row-major A (23).  Split-K is off here (it sums k
-    # ranges separately, so a split call has other bits by design).
+    # on row pairs (21), FFMA2 on column pairs (22), and the persistent
+    # TMA-fed kernel on row-major A (23, which the default 0 takes for these
+    # shapes).  Split-K is off here (it sums k ranges separately, so a split
+    # call has other bits by design).
     import b2blas
 
     monkeypatch.setenv("B2B_SGEMM_KSPLIT", "1")
@@ -412,7 +413,7 @@ def test_sgemm_ffma_kernels_bit_identical(monkeypatch, oracle, m, n, k, alpha, b
     C = oracle.uniform_f32(m * n, 21, 3)
     cfg = b2blas.GemmConfig(m, n, k, alpha, beta)
     outs = {}
-    for v in ("11", "20", "21", "22", "23"):
+    for v in ("0", "11", "20", "21", "22", "23"):
         monkeypatch.setenv("B2B_SGEMM_VARIANT", v)
         h = b2blas.Handle(0)
         try:
@@ -421,8 +422,43 @@ def test_sgemm_ffma_kernels_bit_identical(monkeypatch, oracle, m, n, k, alpha, b
             h.close()
     ref = oracle.sgemm_f64(m, n, k, alpha, A, B, beta, C)
     assert oracle.rel_err(outs["11"], ref) <= oracle.tol_normwise(k, "f32")
-    for v in ("20", "21", "22", "23"):
+    for v in ("0", "20", "21", "22", "23"):
         assert np.array_equal(outs[v], outs["11"]), v
+
+
+@pytest.mark.parametrize("splits", [2, 3])
+@pytest.mark.parametrize("m,n,k,beta", [(1000, 1028, 1000, 0.5), (2048, 1024, 4096, 0.0)])
+def test_sgemm_split_k_persistent_matches_transposed_a_kernel(monkeypatch, oracle, splits, m, n, k, beta):
+    # A split GEMM on the persistent row-major-A kernel (the default) and on
+    # the transposed-A kernel (variant 21) sums the same k ranges in the same
+    # order and adds the partials in split order: the same bits, with and
+    # without the fused bias + ReLU epilogue.
+    import b2blas
+
+    monkeypatch.setenv("B2B_SGEMM_KSPLIT", str(splits))
+    A = oracle.uniform_f32(m * k, 23, 1)
+    B = oracle.uniform_f32(k * n, 23, 2)
+    C = oracle.uniform_f32(m * n, 23, 3)
+    bias = oracle.uniform_f32(n, 23, 5)
+    cfg = b2blas.GemmConfig(m, n, k, 1.5, beta)
+    outs = {}
+    for v in ("0", "21"):
+        monkeypatch.setenv("B2B_SGEMM_VARIANT", v)
+        h = b2blas.Handle(0)
+        try:
+            outs[v] = _gemm_dev(h, "sgemm", None, cfg, A, B, C)
+            a, b, c, bb = h.upload(A), h.upload(B), h.upload(C), h.upload(bias)
+            h.sgemm_bias(cfg, a, b, c, bb, relu=True)
+            h.synchronize()
+            outs[v + "b"] = h.download(c)
+        finally:
+            h.close()
+    assert np.array_equal(outs["0"], outs["21"])
+    assert np.array_equal(outs["0b"], outs["21b"])
+    got = outs["0"].reshape(m, n)
+    for r in (0, m // 2 + 3, m - 1):
+        ref = oracle.sgemm_f64(m, n, k, 1.5, A, B, beta, C, row0=r, nrows=1)
+        assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= oracle.tol_normwise(k, "f32"), r
 
 
 @pytest.mark.parametrize("batch", [12, 300])

@@ -25,8 +25,9 @@ page-locked host memory and C back.
 the same way in its own region with its own clock record and roofline: on
 one GPU SGEMM 8192^3 (alpha 1.5, beta 0.5), SGEMV 16384^2 N, strided-batched
 SGEMM 4096 x 256^3 and DGEMM 4096^3; on N GPUs the batch-sharded
-strided-batched SGEMM (strong) and the weak-scaled HGEMM without a gather
-(--no-secondary skips them).
+strided-batched SGEMM (strong), the weak-scaled HGEMM without a gather, and
+SGEMM 8192^3 (without and with the gathered C) and DGEMM 4096^3 with the
+columns of B and C sharded and A replicated (--no-secondary skips them).
 
 Other workloads (--workload): sgemm (8192^3, alpha 1.5, beta 0.5), dgemm
 (4096^3), batched (4096 x 256^3 strided, batch-sharded), sgemv / dgemv /

@@ -191,6 +191,7 @@ int b2b_create(int device, b2b_handle **out) {
     }
     if (const char *v = getenv("B2B_HGEMM_VARIANT")) h->hgemm_variant = atoi(v);
     if (const char *v = getenv("B2B_HGEMM_GROUP_M")) h->hgemm_group_m = atoi(v);
+    if (const char *v = getenv("B2B_GATHER_ROTATE")) h->gather_rotate = atoi(v) != 0;
     if (const char *v = getenv("B2B_GEMV_SEG_KB")) {
         const long kb = atol(v);
         if (kb > 0) h->gemv_seg_bytes = static_cast<int64_t>(kb) * 1024;

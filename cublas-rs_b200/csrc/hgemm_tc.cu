@@ -82,6 +82,7 @@ struct HgemmArgs {
     // With mc set, the gather goes through that NVLink multicast address
     // instead (one store reaches every rank's C); dst/ndst are then unused.
     uint16_t *mc;
+    int rotate;  // fused all-gather: rotate the destination order per CTA pair
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
@@ -734,7 +735,10 @@ __global__ void __launch_bounds__(hg2::THREADS, 1)
                             }
                         }
 #pragma unroll 1
-                        for (int d = 0; d < args.ndst; ++d) {
+                        for (int i = 0; i < args.ndst; ++i) {
+                            // rotate: each CTA pair starts on another rank, so the
+                            // ranks' stores spread over every receiving link
+                            const int d = args.rotate ? (i + pair) % args.ndst : i;
                             uint16_t *base = args.dst[d] + args.col_off;
 #pragma unroll
                             for (int t = 0; t < 8; ++t) {
@@ -995,7 +999,8 @@ int launch_hgemm_gather_fused(b2b_handle *h, size_t m, size_t n, size_t k, float
     rc = encode_2d_f16(&tmB, B, k, n, hg::B_BOX_N, hg::BK);
     if (rc) return rc;
     HgemmArgs args{cself, (int)m, (int)n, (int)k, alpha, 0.0f, h->d_status, h->wait_limit_ns, h->hgemm_group_m,
-                   ndst, static_cast<int64_t>(ldc), static_cast<int64_t>(col_off), {}, nullptr};
+                   ndst, static_cast<int64_t>(ldc), static_cast<int64_t>(col_off), {}, nullptr,
+                   h->gather_rotate};
     for (int d = 0; d < ndst; ++d) args.dst[d] = dst[d];
     rc = launch_pairs(h, tmA, tmB, args, m, n);
     if (rc == B2B_OK) *done = true;

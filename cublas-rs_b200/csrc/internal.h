@@ -70,6 +70,7 @@ struct b2b_handle {
     int sgemm_ksplit_forced = 0;
     int hgemm_variant = 0;              // 0 auto, 1 single CTA, 2 pair 256x256, 3 pair 256x512
     int hgemm_group_m = 0;              // pair kernels' raster group override (0 = default)
+    int gather_rotate = 1;              // fused gather: rotate destinations per CTA pair (B2B_GATHER_ROTATE=0: off)
     int64_t gemv_seg_bytes = 16384;     // GEMV-N row segment size (B2B_GEMV_SEG_KB)
     // DGEMM kernel configuration (B2B_DGEMM_VARIANT; 0 = the default).
     int dgemm_variant = 0;

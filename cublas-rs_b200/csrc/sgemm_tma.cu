@@ -31,6 +31,13 @@
 //   * Every wait is bounded; a wait that gives up records a status code,
 //     raises the abort flag, and warp 0 drains its in-flight loads before the
 //     CTA exits.
+// That transposed-A kernel (sgemm_tma_kernel) is the one the forced variants
+// 20-22 take.  By default single GEMMs with K % 4 == 0 (split or not) and
+// strided-batched GEMMs run sgemm_tma_rowa_ws_kernel below instead: the same
+// FFMA loop, persistent, with a producer warpgroup (setmaxnreg makes the
+// 384-thread CTA affordable) that loads row-major A and B with TMA and
+// transposes each A tile in shared memory, so no pass through global memory
+// and no workspace precede the GEMM.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

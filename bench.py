@@ -215,6 +215,44 @@ def sgemm_ksplit(sm_count, m, n, k):
     return best if tb <= 0.9 * t1 else 1
 
 
+def dgemm_ksplit(sm_count, m, n, k):
+    """The library's split-K choice for the persistent DMMA DGEMM (dgemm_ksplit
+    in dgemm_dmma.cu), restated to count launches: 128 x 128 tiles, k-tiles of
+    32 at ~4.7 us, a reduce of 8 (S + 1) M N bytes, taken when it saves 5%."""
+    import math
+
+    tiles = ((m + 127) // 128) * ((n + 127) // 128)
+    kt = (k + 31) // 32
+
+    def est(S):
+        t = math.ceil(tiles * S / sm_count) * ((kt + S - 1) // S) * 4.7
+        if S > 1:
+            t += 8.0 * (S + 1) * m * n / 6e12 * 1e6 + 4.0
+        return t
+
+    t1 = est(1)
+    best, tb = 1, t1
+    for S in (2, 3, 4, 6, 8):
+        if (kt + S - 1) // S < 8:
+            break
+        t = est(S)
+        if t < tb:
+            best, tb = S, t
+    return best if tb <= 0.95 * t1 else 1
+
+
+def dgemm_kernels_per_call(m, n, k, sm_count=148):
+    """Kernels one DGEMM call launches on the DMMA path (K and N even, 16-byte
+    aligned operands): the persistent kernel, plus the reduce when split-K
+    applies."""
+    variant = int(os.environ.get("B2B_DGEMM_VARIANT", "0") or 0)
+    if variant != 0 or k % 2 or n % 2:
+        return 1
+    forced = int(os.environ.get("B2B_DGEMM_KSPLIT", "0") or 0)
+    S = forced if forced > 0 else dgemm_ksplit(sm_count, m, n, k)
+    return 2 if min(S, (k + 31) // 32) > 1 else 1
+
+
 def sgemm_kernels_per_call(m, n, k, tf32x3=False, sm_count=148, splits=None):
     """Kernels one single SGEMM call launches on the TMA-fed FFMA path: the
     GEMM (the persistent row-major-A kernel, which transposes A in shared
@@ -500,7 +538,8 @@ class GemmWorkload(Workload):
         if self.gather == "fused-multicast":
             self.gather = "fused"  # becomes "fused-multicast" below once the multicast object exists
         self.mc = 0
-        gemm_kernels = sgemm_kernels_per_call(m, self.n, k, args.tf32x3) if kind == "sgemm" else 1
+        gemm_kernels = (sgemm_kernels_per_call(m, self.n, k, args.tf32x3) if kind == "sgemm" else
+                        dgemm_kernels_per_call(m, self.n, k) if kind == "dgemm" else 1)
         self.launches_per_step = gemm_kernels
         if self.gather == "nccl":
             self.panels = torch.empty(sum(self.widths) * m, device=dev, dtype=tdt)

@@ -197,6 +197,10 @@ int b2b_create(int device, b2b_handle **out) {
         if (kb > 0) h->gemv_seg_bytes = static_cast<int64_t>(kb) * 1024;
     }
     if (const char *v = getenv("B2B_DGEMM_VARIANT")) h->dgemm_variant = atoi(v);
+    if (const char *v = getenv("B2B_DGEMM_KSPLIT")) {
+        const int ks = atoi(v);
+        if (ks >= 0 && ks <= 16) h->dgemm_ksplit_forced = ks;
+    }
     if (const char *v = getenv("B2B_NOALLOC_SCRATCH_FLOATS")) h->noalloc_limit_floats = strtoull(v, nullptr, 10);
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
     *out = h;

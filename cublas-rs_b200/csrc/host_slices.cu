@@ -261,16 +261,18 @@ int gemm_simple(b2b_handle *h, const char *fn, size_t m, size_t n, size_t k, S a
     return finish(h);
 }
 
-// Sets the handle's forced SGEMM split-K factor for its lifetime (unless an
-// environment override already forces one), then restores it.
+// Sets one of the handle's forced split-K factors (SGEMM or DGEMM) for its
+// lifetime (unless an environment override already forces one), then
+// restores it.
 struct ForcedKsplit {
-    b2b_handle *h;
+    int *field;
     int saved;
-    ForcedKsplit(b2b_handle *hh, int S) : h(hh), saved(hh ? hh->sgemm_ksplit_forced : 0) {
-        if (h && saved == 0) h->sgemm_ksplit_forced = S;
+    ForcedKsplit(b2b_handle *hh, int b2b_handle::*member, int S)
+        : field(hh ? &(hh->*member) : nullptr), saved(field ? *field : 0) {
+        if (field && saved == 0) *field = S;
     }
     ~ForcedKsplit() {
-        if (h) h->sgemm_ksplit_forced = saved;
+        if (field) *field = saved;
     }
 };
 
@@ -298,7 +300,7 @@ int b2b_sgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t k, floa
     // the whole (16-byte aligned) GEMM would: its split-K factor, computed
     // once here, is forced on every tile, so the result has the device call's
     // bits however the output is tiled.
-    ForcedKsplit fk(h, h && algo != B2B_ALGO_3XTF32 && m && n && k &&
+    ForcedKsplit fk(h, &b2b_handle::sgemm_ksplit_forced, h && algo != B2B_ALGO_3XTF32 && m && n && k &&
                                sgemm_tma_eligible(static_cast<int64_t>(m), static_cast<int64_t>(n),
                                                   static_cast<int64_t>(k), nullptr, nullptr, nullptr)
                            ? sgemm_ksplit(h->sm_count, static_cast<int64_t>(m), static_cast<int64_t>(n),
@@ -317,6 +319,15 @@ int b2b_dgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t k, doub
                      size_t a_len, const double *B, size_t b_len, double beta, double *C, size_t c_len) {
     if (algo < B2B_ALGO_DEFAULT || algo > B2B_ALGO_DOUBLE_BUF)
         return fail(B2B_ERR_INVALID_ARG, "b2b_dgemm_simple: unknown algo " + std::to_string(algo));
+    // As for SGEMM: the whole GEMM's split-K factor on the DMMA path, forced on
+    // every tile, so a tiled call has the device call's bits.
+    ForcedKsplit fk(h, &b2b_handle::dgemm_ksplit_forced,
+                    h && m && n && k && h->dgemm_variant == 0 &&
+                            dgemm_dmma_eligible(static_cast<int64_t>(n), static_cast<int64_t>(k), nullptr, nullptr,
+                                                nullptr)
+                        ? dgemm_ksplit(h->sm_count, static_cast<int64_t>(m), static_cast<int64_t>(n),
+                                       static_cast<int64_t>(k))
+                        : 1);
     return gemm_simple<double, double>(h, "b2b_dgemm_simple", m, n, k, alpha, A, a_len, B, b_len, beta, C, c_len,
                                        launch_dgemm);
 }

@@ -74,6 +74,7 @@ struct b2b_handle {
     int64_t gemv_seg_bytes = 16384;     // GEMV-N row segment size (B2B_GEMV_SEG_KB)
     // DGEMM kernel configuration (B2B_DGEMM_VARIANT; 0 = the default).
     int dgemm_variant = 0;
+    int dgemm_ksplit_forced = 0;        // DGEMM split-K factor forced (B2B_DGEMM_KSPLIT, host-slice tiles); 0 = choose
     size_t noalloc_limit_floats = 0;    // b2b_sgemv_noalloc: lower scratch limit (0 = the whole array)
 };
 
@@ -148,6 +149,7 @@ int launch_sgemm_tma_rowa(b2b_handle *h, int64_t M, int64_t N, int64_t K, float 
                           int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch,
                           const float *bias, int relu, int ksplit = 1, int64_t kb_per_split = 0,
                           float *partial = nullptr);
+int dgemm_ksplit(int sm_count, int64_t M, int64_t N, int64_t K);
 int launch_dgemm_dmma(b2b_handle *h, int64_t M, int64_t N, int64_t K, double alpha, double beta, const double *A,
                       const double *B, double *C);
 int launch_sgemv(b2b_handle *h, int trans, size_t m, size_t n, float alpha, const float *A, const float *x,

@@ -76,6 +76,28 @@ def test_sgemm_kernels_per_call(monkeypatch):
     assert bench.sgemm_kernels_per_call(8192, 8192, 8192) == 2
 
 
+def test_dgemm_kernels_per_call(monkeypatch):
+    # The persistent DMMA DGEMM is one launch, plus the reduce when its
+    # split-K model picks a split (grids that fill the GPU badly).  Mirrors
+    # dgemm_ksplit in dgemm_dmma.cu.
+    sys.path.insert(0, ROOT)
+    import bench
+
+    monkeypatch.delenv("B2B_DGEMM_VARIANT", raising=False)
+    monkeypatch.delenv("B2B_DGEMM_KSPLIT", raising=False)
+    assert bench.dgemm_ksplit(148, 4096, 4096, 4096) == 1
+    assert bench.dgemm_ksplit(148, 1024, 1024, 1024) == 2
+    assert bench.dgemm_ksplit(148, 2048, 2048, 2048) == 4        # 1.73 waves
+    assert bench.dgemm_ksplit(148, 4096, 512, 4096) == 8         # a DGEMM 4096^3 column panel on 8 GPUs
+    assert bench.dgemm_kernels_per_call(4096, 4096, 4096) == 1
+    assert bench.dgemm_kernels_per_call(1024, 1024, 1024) == 2
+    assert bench.dgemm_kernels_per_call(1024, 1024, 1023) == 1   # K odd: the DFMA kernel
+    monkeypatch.setenv("B2B_DGEMM_KSPLIT", "4")
+    assert bench.dgemm_kernels_per_call(4096, 4096, 4096) == 2
+    monkeypatch.setenv("B2B_DGEMM_VARIANT", "8")
+    assert bench.dgemm_kernels_per_call(1024, 1024, 1024) == 1
+
+
 def _bench_args(argv):
     sys.path.insert(0, ROOT)
     import argparse

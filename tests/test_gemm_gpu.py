@@ -233,6 +233,7 @@ def test_dgemm_persistent_kernel_bit_identical(monkeypatch, oracle, m, n, k, bet
     A = oracle.uniform_f64(m * k, 31, 1)
     B = oracle.uniform_f64(k * n, 31, 2)
     C = oracle.uniform_f64(m * n, 31, 3)
+    monkeypatch.setenv("B2B_DGEMM_KSPLIT", "1")  # the one-CTA-per-tile kernel does not split
     cfg = b2blas.GemmConfig(m, n, k, 1.5, beta)
     outs = {}
     for v in ("0", "8"):
@@ -247,6 +248,70 @@ def test_dgemm_persistent_kernel_bit_identical(monkeypatch, oracle, m, n, k, bet
     for r in (0, m // 2 + 1, m - 1):
         ref = oracle.dgemm_f64(m, n, k, 1.5, A, B, beta, C, row0=r, nrows=1)
         assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= oracle.tol_normwise(k, "f64"), r
+
+
+@pytest.mark.parametrize("m,n,k,ks,beta", [(1024, 1024, 1024, None, 0.5), (2048, 2048, 2048, "4", 0.0),
+                                            (1000, 1002, 998, "3", 0.5), (130, 4096, 4096, "8", -1.0)])
+def test_dgemm_split_k(oracle, monkeypatch, m, n, k, ks, beta):
+    # Split-K on the persistent DMMA kernel (chosen for 1024^3: 64 tiles under
+    # one wave, S = 2; forced for the others, including K whose last range is
+    # short): raw sums per k range in workspace, then a fixed-order reduce
+    # applying alpha and beta.  Within the FP64 bound of the FP64 evaluation,
+    # and the same bits on a second call.
+    import b2blas
+
+    if ks is None:
+        monkeypatch.delenv("B2B_DGEMM_KSPLIT", raising=False)
+    else:
+        monkeypatch.setenv("B2B_DGEMM_KSPLIT", ks)
+    A = oracle.uniform_f64(m * k, 33, 1)
+    B = oracle.uniform_f64(k * n, 33, 2)
+    C = oracle.uniform_f64(m * n, 33, 3)
+    h = b2blas.Handle(0)
+    try:
+        cfg = b2blas.GemmConfig(m, n, k, 1.5, beta)
+        a, b = h.upload(A), h.upload(B)
+        outs = []
+        for _ in range(2):
+            c = h.upload(C)
+            h.dgemm(cfg, a, b, c)
+            h.synchronize()
+            outs.append(h.download(c))
+        assert np.array_equal(outs[0], outs[1])
+        got = outs[0].reshape(m, n)
+        for r in (0, m // 2 + 1, m - 1):
+            ref = oracle.dgemm_f64(m, n, k, 1.5, A, B, beta, C, row0=r, nrows=1)
+            assert oracle.rel_err(np.ascontiguousarray(got[r]), ref) <= oracle.tol_normwise(k, "f64"), r
+    finally:
+        h.close()
+
+
+def test_dgemm_split_k_simple_matches_device_bits(oracle):
+    # 1024 x 1024 x 8192 splits in two (64 tiles, under one wave).  Its
+    # 64 MiB operands make the host-slice call pipelined and tiled; the call
+    # forces the whole GEMM's split on every tile, so every output sums the
+    # same k ranges in the same order: the device call's bits.
+    import b2blas
+
+    m, n, k = 1024, 1024, 8192
+    A = oracle.uniform_f64(m * k, 34, 1)
+    B = oracle.uniform_f64(k * n, 34, 2)
+    C = oracle.uniform_f64(m * n, 34, 3)
+    h = b2blas.Handle(0)
+    try:
+        cfg = b2blas.GemmConfig(m, n, k, 1.25, -0.5)
+        host = C.copy()
+        h.dgemm_simple(cfg, A, B, host)
+        a, b, c = h.upload(A), h.upload(B), h.upload(C)
+        h.dgemm(cfg, a, b, c)
+        h.synchronize()
+        dev = h.download(c)
+        assert np.array_equal(dev, host)
+        for r in (0, 513, m - 1):
+            ref = oracle.dgemm_f64(m, n, k, 1.25, A, B, -0.5, C, row0=r, nrows=1)
+            assert oracle.rel_err(np.ascontiguousarray(host.reshape(m, n)[r]), ref) <= oracle.tol_normwise(k, "f64")
+    finally:
+        h.close()
 
 
 # ------------------------------------------------------- batched family

@@ -158,7 +158,11 @@ B2B_API int b2b_set_sgemm_splits(b2b_handle *h, int splits);
 
 /* ------------------------------------------------------ Level 3: DGEMM */
 
-/* Handle::dgemm_* (lib.rs:527-612) -> crates/cublas-l3/src/dgemm.rs:342-569. */
+/* Handle::dgemm_* (lib.rs:527-612) -> crates/cublas-l3/src/dgemm.rs:342-569.
+ * Grids that fill the GPU badly are split along K as for SGEMM (partial sums
+ * in handle workspace, added in a fixed order): the result is deterministic,
+ * and its bits depend on the split, which the host-slice call keeps equal to
+ * the device call's (B2B_DGEMM_KSPLIT forces one). */
 B2B_API int b2b_dgemm(b2b_handle *h, int algo, size_t m, size_t n, size_t k, double alpha, const double *A,
                       const double *B, double beta, double *C);
 B2B_API int b2b_dgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t k, double alpha,

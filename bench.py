@@ -265,19 +265,20 @@ def sgemm_kernels_per_call(m, n, k, tf32x3=False, sm_count=148, splits=None):
     variant = int(os.environ.get("B2B_SGEMM_VARIANT", "0") or 0)
     if tf32x3 or variant not in (0, 20, 21, 22):
         return 1
-    ok = m % 4 == 0 and n % 4 == 0 and (splits is not None or (m >= 128 and n >= 1024)) and 32 <= k <= 65535 * 32
-    if not ok:
+    rowa = variant == 0 and k % 4 == 0 and n % 4 == 0  # the persistent kernel: any size (sgemm_tma_path)
+    transposed = m % 4 == 0 and n % 4 == 0 and (splits is not None or (m >= 128 and n >= 1024)) and \
+        32 <= k <= 65535 * 32
+    if not (rowa or transposed):
         return 1
     forced = int(os.environ.get("B2B_SGEMM_KSPLIT", "0") or 0)
     S = splits if splits is not None else forced if forced > 0 else sgemm_ksplit(sm_count, m, n, k)
-    gemm = 1 if variant == 0 and k % 4 == 0 else 2
-    return gemm + (1 if S > 1 else 0)
+    S = min(S, (k + 31) // 32)
+    return (1 if rowa else 2) + (1 if S > 1 else 0)
 
 
 def sgemm_kernel_name(m, n, k):
     """The dominant kernel of one single SGEMM call (FFMA path)."""
-    if int(os.environ.get("B2B_SGEMM_VARIANT", "0") or 0) == 0 and k % 4 == 0 and 32 <= k <= 65535 * 32 \
-            and m % 4 == 0 and n % 4 == 0 and m >= 128 and n >= 1024:
+    if int(os.environ.get("B2B_SGEMM_VARIANT", "0") or 0) == 0 and k % 4 == 0 and n % 4 == 0:
         split = sgemm_kernels_per_call(m, n, k) > 1
         return "sgemm_tma_rowa_ws_kernel<true> (persistent; A transposed in shared memory)" + \
             (" + split-K reduce" if split else "")

@@ -59,8 +59,8 @@ int b2b_sgemm_splits(b2b_handle *h, size_t m, size_t n, size_t k, int *splits) {
     *splits = 1;
     if (m == 0 || n == 0 || k == 0) return B2B_OK;
     const int64_t M = static_cast<int64_t>(m), N = static_cast<int64_t>(n), K = static_cast<int64_t>(k);
-    if (h->sgemm_variant != 0 && !(h->sgemm_variant >= 20 && h->sgemm_variant <= 22)) return B2B_OK;
-    if (!sgemm_tma_eligible(M, N, K, nullptr, nullptr, nullptr, h->sgemm_ksplit_forced > 1)) return B2B_OK;
+    if (!sgemm_tma_path(h->sgemm_variant, M, N, K, nullptr, nullptr, nullptr, h->sgemm_ksplit_forced > 1))
+        return B2B_OK;
     int S = h->sgemm_ksplit_forced > 0 ? h->sgemm_ksplit_forced : sgemm_ksplit(h->sm_count, M, N, K);
     const int64_t kt = (K + 31) / 32;
     if (S > kt) S = static_cast<int>(kt);

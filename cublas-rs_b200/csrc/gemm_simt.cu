@@ -660,14 +660,14 @@ bool vec_ok(int64_t K, int64_t N, int64_t sA, int64_t sB, int64_t sC, const void
 int run_sgemm(b2b_handle *h, int variant, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
               int64_t sA, const float *B, int64_t sB, float *C, int64_t sC, int64_t batch,
               EpiArgs<float> epi = EpiArgs<float>{nullptr, 0}) {
-    // Single large GEMMs: the TMA-fed kernel (sgemm_tma.cu; same per-element
-    // arithmetic, 10% faster at 8192^3), packed FFMA2 on row pairs by default;
-    // variants 20/21/22 force its scalar / row-pair / column-pair forms and
-    // variant 11 the cp.async kernel below.
-    // A forced split-K (the tiles of a split host-slice call) must take this
-    // kernel whatever the tile's size.
-    if ((variant == 0 || (variant >= 20 && variant <= 22)) && batch == 1 &&
-        b2b::sgemm_tma_eligible(M, N, K, A, B, C, h->sgemm_ksplit_forced > 1))
+    // Single GEMMs: the TMA-fed kernels (sgemm_tma.cu; same per-element
+    // arithmetic) wherever sgemm_tma_path allows -- by default the persistent
+    // row-major-A kernel (N and K multiples of 4, aligned, any size), with
+    // split-K for grids that fill the GPU badly; variants 20/21/22 force the
+    // transposed-A kernel's scalar / row-pair / column-pair forms and variant
+    // 11 the cp.async kernel below.  A forced split-K (the tiles of a split
+    // host-slice call) must take the TMA path whatever the tile's size.
+    if (batch == 1 && b2b::sgemm_tma_path(variant, M, N, K, A, B, C, h->sgemm_ksplit_forced > 1))
         return b2b::launch_sgemm_tma(h, M, N, K, alpha, beta, A, B, C, epi.bias, epi.relu,
                                      variant == 0 ? 1 : variant - 20);
     // Batched calls (and variants 23-28): the TMA-fed kernels on row-major A

@@ -300,12 +300,13 @@ int b2b_sgemm_simple(b2b_handle *h, int algo, size_t m, size_t n, size_t k, floa
     // the whole (16-byte aligned) GEMM would: its split-K factor, computed
     // once here, is forced on every tile, so the result has the device call's
     // bits however the output is tiled.
-    ForcedKsplit fk(h, &b2b_handle::sgemm_ksplit_forced, h && algo != B2B_ALGO_3XTF32 && m && n && k &&
-                               sgemm_tma_eligible(static_cast<int64_t>(m), static_cast<int64_t>(n),
-                                                  static_cast<int64_t>(k), nullptr, nullptr, nullptr)
-                           ? sgemm_ksplit(h->sm_count, static_cast<int64_t>(m), static_cast<int64_t>(n),
-                                          static_cast<int64_t>(k))
-                           : 1);
+    ForcedKsplit fk(h, &b2b_handle::sgemm_ksplit_forced,
+                    h && algo != B2B_ALGO_3XTF32 && m && n && k &&
+                            sgemm_tma_path(h->sgemm_variant, static_cast<int64_t>(m), static_cast<int64_t>(n),
+                                           static_cast<int64_t>(k), nullptr, nullptr, nullptr)
+                        ? sgemm_ksplit(h->sm_count, static_cast<int64_t>(m), static_cast<int64_t>(n),
+                                       static_cast<int64_t>(k))
+                        : 1);
     return gemm_simple<float, float>(
         h, "b2b_sgemm_simple", m, n, k, alpha, A, a_len, B, b_len, beta, C, c_len,
         [algo](b2b_handle *hh, size_t mm, size_t nn, size_t kk, float al, const float *a, const float *b, float be,

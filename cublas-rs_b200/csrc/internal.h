@@ -135,6 +135,8 @@ int launch_sgemm_3xtf32(b2b_handle *h, size_t m, size_t n, size_t k, float alpha
 bool dgemm_dmma_eligible(int64_t N, int64_t K, const void *A, const void *B, const void *C);
 bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C,
                         bool any_size = false);
+bool sgemm_tma_path(int variant, int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C,
+                    bool any_size = false);
 int sgemm_ksplit(int sm_count, int64_t M, int64_t N, int64_t K);
 int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,
                      const float *B, float *C, const float *bias, int relu, int pack);

@@ -1123,6 +1123,20 @@ bool sgemm_tma_rowa_eligible(int64_t M, int64_t N, int64_t K, int64_t sA, int64_
     return tiles < lim;
 }
 
+// Whether a single SGEMM of the given kernel variant takes the TMA-fed path:
+// by default (variant 0) the persistent row-major-A kernel wherever it
+// applies (N and K multiples of 4, 16-byte aligned operands; no size limit,
+// since it needs no transpose pass to amortise), else the transposed-A
+// kernel where sgemm_tma_eligible allows it; variants 20-22 force the
+// transposed-A kernel's forms.  run_sgemm, the host-slice call's split and
+// b2b_sgemm_splits all decide with this, so they agree on the split.
+bool sgemm_tma_path(int variant, int64_t M, int64_t N, int64_t K, const void *A, const void *B, const void *C,
+                    bool any_size) {
+    if (variant == 0 && sgemm_tma_rowa_eligible(M, N, K, M * K, K * N, M * N, 1, A, B, C)) return true;
+    if (variant != 0 && !(variant >= 20 && variant <= 22)) return false;
+    return sgemm_tma_eligible(M, N, K, A, B, C, any_size);
+}
+
 namespace {
 
 template <int WN, bool XP>

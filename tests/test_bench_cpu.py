@@ -67,8 +67,9 @@ def test_sgemm_kernels_per_call(monkeypatch):
     monkeypatch.setenv("B2B_SGEMM_KSPLIT", "1")
     assert bench.sgemm_kernels_per_call(1024, 1024, 1024) == 1
     monkeypatch.delenv("B2B_SGEMM_KSPLIT")
-    assert bench.sgemm_kernels_per_call(512, 512, 512) == 1        # N < 1024
-    assert bench.sgemm_kernels_per_call(100, 2048, 64) == 1        # M < 128
+    assert bench.sgemm_kernels_per_call(512, 512, 512) == 2        # any size on the persistent kernel; S = 2
+    assert bench.sgemm_kernels_per_call(100, 2048, 64) == 1        # M < 128, unsplit
+    assert bench.sgemm_kernels_per_call(129, 257, 65) == 1         # N % 4 != 0: the cp.async kernel
     assert bench.sgemm_kernels_per_call(8192, 8192, 8192, tf32x3=True) == 1
     monkeypatch.setenv("B2B_SGEMM_VARIANT", "11")
     assert bench.sgemm_kernels_per_call(8192, 8192, 8192) == 1

@@ -719,7 +719,8 @@ def test_sgemm_splits_query_and_row_pieces_reproduce_whole(oracle):
     try:
         assert h.sgemm_splits(1024, 1024, 1024) == 4
         assert h.sgemm_splits(8192, 8192, 8192) == 1
-        assert h.sgemm_splits(512, 512, 512) == 1  # the cp.async kernel's shape: no split
+        assert h.sgemm_splits(512, 512, 512) == 2  # 8 tiles on the persistent kernel
+        assert h.sgemm_splits(512, 514, 512) == 1  # N % 4 != 0: the cp.async kernel, no split
         m, n, k = 4096, 1024, 4096
         whole = h.sgemm_splits(m, n, k)
         A = oracle.uniform_f32(m * k, 33, 1)

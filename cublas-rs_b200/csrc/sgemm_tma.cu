@@ -1005,11 +1005,14 @@ bool sgemm_tma_eligible(int64_t M, int64_t N, int64_t K, const void *A, const vo
 // Split-K factor for an M x N x K SGEMM on the TMA-fed kernel: the S in
 // {1, 2, 3, 4, 6, 8} with the least estimated time, where the GEMM costs
 // waves x k-blocks per CTA (a 128 x 256 x 32 k-block takes ~5.2 us at the
-// kernel's FFMA rate) and a split adds its partial sums' HBM round trip
-// (8 S M N bytes at ~6 TB/s) plus a launch.  Each split keeps at least 8
-// k-blocks.  Taken only when it saves 10% or more: grids under one wave
-// (1024^3: 32 tiles, S = 4) and wave counts just past a whole number
-// (4096^3: 3.46 waves, S = 2).
+// kernel's FFMA rate) and a split adds the reduce (reading S partials and
+// writing C, 4 (S + 1) M N bytes at ~6 TB/s: the partials' writes hide under
+// the compute-bound GEMM) plus a launch.  Each split keeps at least 8
+// k-blocks.  Taken when it saves 5% or more: grids under one wave (1024^3:
+// 32 tiles, S = 4) and wave counts just past a whole number (4096^3: 3.46
+// waves, S = 2; 4096 x 4096 x 1024, S = 2: 54.3 vs 47.8 TFLOP/s unsplit;
+// 4096 x 1024 x 4096, S = 8: 56.1 vs 52.7; 2048 x 4096 x 2048, S = 4: 55.5
+// vs 50.8).
 int sgemm_ksplit(int sm_count, int64_t M, int64_t N, int64_t K) {
     const double tiles = static_cast<double>(((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN));
     const int64_t kt = (K + kBK - 1) / kBK;
@@ -1018,7 +1021,7 @@ int sgemm_ksplit(int sm_count, int64_t M, int64_t N, int64_t K) {
         const double waves = std::ceil(tiles * S / sm_count);
         const double kbs = static_cast<double>((kt + S - 1) / S);
         double t = waves * kbs * kb_us;
-        if (S > 1) t += 8.0 * S * static_cast<double>(M) * static_cast<double>(N) / 6e12 * 1e6 + 4.0;
+        if (S > 1) t += 4.0 * (S + 1) * static_cast<double>(M) * static_cast<double>(N) / 6e12 * 1e6 + 4.0;
         return t;
     };
     const double t1 = est(1);
@@ -1032,7 +1035,7 @@ int sgemm_ksplit(int sm_count, int64_t M, int64_t N, int64_t K) {
             best = S;
         }
     }
-    return tb <= 0.9 * t1 ? best : 1;
+    return tb <= 0.95 * t1 ? best : 1;
 }
 
 int launch_sgemm_tma(b2b_handle *h, int64_t M, int64_t N, int64_t K, float alpha, float beta, const float *A,

@@ -53,8 +53,9 @@ def test_sgemm_kernels_per_call(monkeypatch):
     monkeypatch.delenv("B2B_SGEMM_VARIANT", raising=False)
     monkeypatch.delenv("B2B_SGEMM_KSPLIT", raising=False)
     assert bench.sgemm_kernels_per_call(8192, 8192, 8192) == 1
-    assert bench.sgemm_kernels_per_call(4096, 1024, 4096) == 1
-    assert bench.sgemm_kernels_per_call(4096, 1024, 4098) == 2  # K % 4 != 0: transposed-A kernel
+    assert bench.sgemm_kernels_per_call(8192, 4096, 4096) == 1      # 6.9 waves: unsplit
+    assert bench.sgemm_kernels_per_call(4096, 1024, 4096) == 2      # S = 8: GEMM + reduce
+    assert bench.sgemm_kernels_per_call(8192, 8192, 8190) == 2      # K % 4 != 0: transpose + GEMM
     assert bench.sgemm_kernel_name(8192, 8192, 8192).startswith("sgemm_tma_rowa_ws_kernel")
     # split-K adds the reduce: grids under one wave, or just past a whole one
     assert bench.sgemm_ksplit(148, 1024, 1024, 1024) == 4
